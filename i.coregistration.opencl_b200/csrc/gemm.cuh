@@ -1,0 +1,68 @@
+// SPDX-License-Identifier: Unlicense
+//
+// Internal GEMM interface shared by ops_gemm (ops.h) and the models.
+//
+// C = act(alpha * A * op(B) + bias) + R, batched, with the contract of
+// the reference's gemm / gemm_big kernels (ops.cl:39-52): A is M x K
+// row-major (lda); B is N x K (transb, the PyTorch Linear weight layout)
+// or K x N; batch b at offsets (b / nb1) * s0 + (b % nb1) * s1; bias per
+// column (biasrow 0) or per row (biasrow 1); R has C's layout (ldc,
+// batch strides of C) from its own base pointer and may alias C.
+//
+// Element types: A and B are float or bfloat16 (both the same), C and R
+// float or bfloat16.
+
+#pragma once
+
+#include "common.cuh"
+
+namespace coreg {
+
+enum DType { DT_F32 = 0, DT_BF16 = 1 };
+
+struct GemmArgs {
+    int M, N, K;
+    const void *A;
+    long lda, sa0, sa1;
+    const void *B;
+    long ldb, sb0, sb1;
+    int transb;
+    void *C;
+    long ldc, sc0, sc1;
+    int nb, nb1;
+    const float *bias;
+    int biasrow;
+    const void *R; // C's layout and type
+    float alpha;
+    int act;
+    float slope;
+    DType ab;  // type of A and B
+    DType c;   // type of C and R
+};
+
+inline GemmArgs gemm_args(int M, int N, int K)
+{
+    GemmArgs g = {};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.nb = 1;
+    g.nb1 = 1;
+    g.alpha = 1.0f;
+    return g;
+}
+
+// Float32 FMA tiles (the accurate path): any strides, any type mix.
+void gemm_simt(cudaStream_t st, const GemmArgs &g);
+
+// tcgen05 tensor-core tiles for bfloat16 A and B, both K-major
+// (transb), with float32 accumulation; returns false (nothing launched)
+// when the shape or alignment is not supported, so that the caller can
+// use gemm_simt.
+bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count);
+
+// Dispatch: tensor cores when bf16 operands allow it, else SIMT.
+void gemm_run(const struct ocl_backend *ocl, const GemmArgs &g,
+              const char *what);
+
+}  // namespace coreg

@@ -1,0 +1,957 @@
+// SPDX-License-Identifier: Unlicense
+//
+// The generic tensor operations of ops.h on CUDA. Each entry point keeps
+// the argument meaning of the reference's ops.c / ops.cl entry point it
+// replaces (cited per function); the kernels are this build's own.
+
+#include <math.h>
+#include <string.h>
+
+#include "gemm.cuh"
+
+using namespace coreg;
+
+// ------------------------------------------------------------------ setup
+
+extern "C" void ops_init(struct ops *o, struct ocl_backend *ocl)
+{
+    memset(o, 0, sizeof(*o));
+    o->ocl = ocl;
+    o->precision = OPS_FP32;
+    o->im2col_bytes = (size_t)256 << 20;
+}
+
+extern "C" void ops_free(struct ops *o)
+{
+    if (!o->ocl)
+        return;
+    ocl_release(&o->scratch);
+    ocl_release(&o->scratch16);
+    memset(o, 0, sizeof(*o));
+}
+
+extern "C" struct opnd ops_mat(cl_mem buf, long off, int ld)
+{
+    struct opnd m = {buf, off, ld, 0, 0};
+    return m;
+}
+
+extern "C" struct opnd ops_bmat(cl_mem buf, long off, int ld, long s0, long s1)
+{
+    struct opnd m = {buf, off, ld, s0, s1};
+    return m;
+}
+
+static bool need(cl_mem m, const char *what)
+{
+    if (!m) {
+        fail("CUDA: %s: required buffer is NULL", what);
+        return false;
+    }
+    return true;
+}
+
+static const int T256 = 256;
+
+// ------------------------------------------------------------------- GEMM
+
+// Float32 copy of an operand into bfloat16 (OPS_BF16 on ops_gemm): rows
+// x cols of src (leading dimension ld) per batch product, packed.
+__global__ void to_bf16_kernel(const float *src, long ld, long s0, long s1,
+                               int nb1, int rows, int cols,
+                               __nv_bfloat16 *dst)
+{
+    const long b = blockIdx.z, b0 = b / nb1, b1 = b % nb1;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y;
+
+    if (c >= cols)
+        return;
+    dst[(b * rows + r) * (long)cols + c] =
+        __float2bfloat16_rn(src[b0 * s0 + b1 * s1 + (long)r * ld + c]);
+}
+
+extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
+                         struct opnd B, int transb, struct opnd C, int nb,
+                         int nb1, cl_mem bias, int biasrow, cl_mem R, long roff,
+                         float alpha, int act, float slope)
+{
+    GemmArgs g = gemm_args(M, N, K);
+
+    if (pending() || !need(A.buf, "ops_gemm A") || !need(B.buf, "ops_gemm B") ||
+        !need(C.buf, "ops_gemm C"))
+        return;
+    if (nb1 < 1 || nb < 1) {
+        fail("ops_gemm: batch %d / %d", nb, nb1);
+        return;
+    }
+    g.A = fptr(A.buf, A.off);
+    g.lda = A.ld;
+    g.sa0 = A.s0;
+    g.sa1 = A.s1;
+    g.B = fptr(B.buf, B.off);
+    g.ldb = B.ld;
+    g.sb0 = B.s0;
+    g.sb1 = B.s1;
+    g.transb = transb;
+    g.C = fptr(C.buf, C.off);
+    g.ldc = C.ld;
+    g.sc0 = C.s0;
+    g.sc1 = C.s1;
+    g.nb = nb;
+    g.nb1 = nb1;
+    g.bias = fptr(bias);
+    g.biasrow = biasrow;
+    g.R = R ? fptr(R, roff) : nullptr;
+    g.alpha = alpha;
+    g.act = act;
+    g.slope = slope;
+    g.ab = DT_F32;
+    g.c = DT_F32;
+    if (o->precision == OPS_BF16 && transb && M >= 128 && N >= 64 && K >= 64) {
+        // Pack both operands to bfloat16 (row-major, K contiguous), then
+        // the tensor-core tiles.
+        size_t ea = (size_t)nb * M * K, eb = (size_t)nb * N * K;
+        size_t bytes = (ea + eb) * 2 + 256;
+
+        if (bytes > o->scratch16_bytes) {
+            ocl_release(&o->scratch16);
+            o->scratch16 = ocl_alloc(o->ocl, bytes, "bf16 operands");
+            o->scratch16_bytes = bytes;
+            if (pending())
+                return;
+        }
+        __nv_bfloat16 *a16 = (__nv_bfloat16 *)o->scratch16->ptr;
+        __nv_bfloat16 *b16 = a16 + ((ea + 127) / 128) * 128;
+        cudaStream_t st = stream_of(o->ocl);
+        {
+            Prof p(o->ocl, "gemm_pack_bf16");
+            to_bf16_kernel<<<dim3(cdiv(K, 256), M, nb), 256, 0, st>>>(
+                (const float *)g.A, g.lda, g.sa0, g.sa1, nb1, M, K, a16);
+            to_bf16_kernel<<<dim3(cdiv(K, 256), N, nb), 256, 0, st>>>(
+                (const float *)g.B, g.ldb, g.sb0, g.sb1, nb1, N, K, b16);
+            if (!launch_ok("gemm_pack_bf16"))
+                return;
+        }
+        GemmArgs h = g;
+        h.A = a16;
+        h.lda = K;
+        h.sa0 = (long)M * K * nb1;
+        h.sa1 = (long)M * K;
+        h.B = b16;
+        h.ldb = K;
+        h.sb0 = (long)N * K * nb1;
+        h.sb1 = (long)N * K;
+        h.ab = DT_BF16;
+        gemm_run(o->ocl, h, "gemm_tc");
+        return;
+    }
+    gemm_run(o->ocl, g, "gemm");
+}
+
+extern "C" void ops_linear(struct ops *o, int rows, int in, int out, cl_mem X,
+                           long xoff, cl_mem W, cl_mem b, cl_mem Y, long yoff,
+                           int act, float slope, int residual)
+{
+    ops_gemm(o, rows, out, in, ops_mat(X, xoff, in), ops_mat(W, 0, in), 1,
+             ops_mat(Y, yoff, out), 1, 1, b, 0, residual ? Y : NULL, yoff, 1.0f,
+             act, slope);
+}
+
+extern "C" void ops_conv1x1(struct ops *o, cl_mem X, long xoff, int C, int HW,
+                            cl_mem W, cl_mem b, int K, cl_mem Y, long yoff,
+                            int act, float slope)
+{
+    ops_gemm(o, K, HW, C, ops_mat(W, 0, C), ops_mat(X, xoff, HW), 0,
+             ops_mat(Y, yoff, HW), 1, 1, b, 1, NULL, 0, 1.0f, act, slope);
+}
+
+// ------------------------------------------------------------ convolutions
+
+extern "C" struct conv_geom ops_geom(int k, int s, int p)
+{
+    struct conv_geom g = {k, k, s, s, p, p, 1, 1, 1};
+    return g;
+}
+
+extern "C" int ops_conv_out(int n, int k, int s, int p, int d)
+{
+    return (n + 2 * p - d * (k - 1) - 1) / s + 1;
+}
+
+// F.unfold of positions l0 .. l0 + n - 1 (ops.cl:799-816 semantics): row
+// c * kh * kw + i * kw + j, column l - l0.
+__global__ void unfold_kernel(const float *in, int C, int H, int W, int kh,
+                              int kw, int sy, int sx, int py, int px, int dy,
+                              int dx, int Wo, int l0, int n, float *out)
+{
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int row = blockIdx.y;
+    if (t >= n)
+        return;
+    const int c = row / (kh * kw), i = (row / kw) % kh, j = row % kw;
+    const int l = l0 + t;
+    const int iy = (l / Wo) * sy - py + i * dy;
+    const int ix = (l % Wo) * sx - px + j * dx;
+    out[(size_t)row * n + t] = iy >= 0 && iy < H && ix >= 0 && ix < W
+                                   ? in[((size_t)c * H + iy) * W + ix]
+                                   : 0.0f;
+}
+
+// Direct convolution, one thread per output value (ops.cl:397-448
+// semantics, including the normalize-and-gate of the input before the
+// zero padding).
+__global__ void conv_direct_kernel(const float *in, int C, int H, int W,
+                                   const float *wt, const float *bias, int K,
+                                   int Ho, int Wo, int kh, int kw, int sy,
+                                   int sx, int py, int px, int dy, int dx,
+                                   int groups, const float *mean,
+                                   const float *rstd, const float *alpha,
+                                   int act, float slope, float *out)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y;
+    const int k = blockIdx.z;
+    if (x >= Wo)
+        return;
+    const int cg = C / groups, kg = K / groups, c0 = (k / kg) * cg;
+    const float *w = wt + (size_t)k * cg * kh * kw;
+    float acc = 0.0f;
+
+    for (int c = 0; c < cg; c++) {
+        const float *src = in + (size_t)(c0 + c) * H * W;
+        float m = 0.0f, r = 1.0f, a = 1.0f;
+        if (mean) {
+            m = mean[c0 + c];
+            r = rstd[c0 + c];
+            if (alpha)
+                a = alpha[c0 + c];
+        }
+        for (int i = 0; i < kh; i++) {
+            const int iy = y * sy - py + i * dy;
+            if (iy < 0 || iy >= H)
+                continue;
+            for (int j = 0; j < kw; j++) {
+                const int ix = x * sx - px + j * dx;
+                if (ix < 0 || ix >= W)
+                    continue;
+                float v = src[(size_t)iy * W + ix];
+                if (mean) {
+                    v = (v - m) * r;
+                    v = v >= 0.0f ? v : a * v;
+                }
+                acc = fmaf(v, w[(c * kh + i) * kw + j], acc);
+            }
+        }
+    }
+    if (bias)
+        acc += bias[k];
+    out[((size_t)k * Ho + y) * Wo + x] = apply_act(acc, act, slope);
+}
+
+// Convolution as W (K, C kh kw) times the unfolded input, by blocks of
+// output positions that fit the scratch buffer (the reference's
+// conv_im2col, ops.c:238-265).
+static void conv_im2col(struct ops *o, cl_mem in, int C, int H, int W, cl_mem w,
+                        cl_mem b, int K, const struct conv_geom *g, int Ho,
+                        int Wo, int act, float slope, cl_mem out)
+{
+    const int Kc = C * g->kh * g->kw, L = Ho * Wo;
+    int blk = (int)(o->im2col_bytes / sizeof(float) / Kc) / 128 * 128;
+    cudaStream_t st = stream_of(o->ocl);
+
+    if (blk < 128)
+        blk = 128;
+    if (blk > L)
+        blk = L;
+    size_t bytes = (size_t)Kc * blk * sizeof(float);
+    if (bytes > o->scratch_bytes) {
+        ocl_release(&o->scratch);
+        o->scratch = ocl_alloc(o->ocl, bytes, "im2col");
+        o->scratch_bytes = bytes;
+        if (pending())
+            return;
+    }
+    for (int l0 = 0; l0 < L; l0 += blk) {
+        const int n = L - l0 < blk ? L - l0 : blk;
+        {
+            Prof p(o->ocl, "unfold");
+            unfold_kernel<<<dim3(cdiv(n, T256), Kc), T256, 0, st>>>(
+                fptr(in), C, H, W, g->kh, g->kw, g->sy, g->sx, g->py, g->px,
+                g->dy, g->dx, Wo, l0, n, fptr(o->scratch));
+            if (!launch_ok("unfold"))
+                return;
+        }
+        ops_gemm(o, K, n, Kc, ops_mat(w, 0, Kc), ops_mat(o->scratch, 0, n), 0,
+                 ops_mat(out, l0, L), 1, 1, b, 1, NULL, 0, 1.0f, act, slope);
+    }
+}
+
+extern "C" void ops_conv2d(struct ops *o, cl_mem in, int C, int H, int W,
+                           cl_mem w, cl_mem b, int K, const struct conv_geom *g,
+                           cl_mem mean, cl_mem rstd, cl_mem alpha, int act,
+                           float slope, cl_mem out)
+{
+    if (pending() || !need(in, "ops_conv2d in") || !need(w, "ops_conv2d w") ||
+        !need(out, "ops_conv2d out"))
+        return;
+    const int Ho = ops_conv_out(H, g->kh, g->sy, g->py, g->dy);
+    const int Wo = ops_conv_out(W, g->kw, g->sx, g->px, g->dx);
+
+    if (g->groups < 1 || C % g->groups || K % g->groups) {
+        fail("CUDA: %d -> %d channels in %d groups", C, K, g->groups);
+        return;
+    }
+    if (mean && !rstd) {
+        fail("ops_conv2d: mean without rstd");
+        return;
+    }
+    if (!count_ok((long)C * H * W, "convolution input") ||
+        !count_ok((long)K * Ho * Wo, "convolution output"))
+        return;
+    if (Ho <= 0 || Wo <= 0)
+        return;
+    if (g->groups == 1 && !mean && !alpha && g->dy == 1 && g->dx == 1 &&
+        (long)C * g->kh * g->kw * Ho * Wo >= 4096) {
+        if (!count_ok((long)C * g->kh * g->kw * 128, "im2col block"))
+            return;
+        conv_im2col(o, in, C, H, W, w, b, K, g, Ho, Wo, act, slope, out);
+        return;
+    }
+    Prof p(o->ocl, "conv2d");
+    conv_direct_kernel<<<dim3(cdiv(Wo, 64), Ho, K), 64, 0, stream_of(o->ocl)>>>(
+        fptr(in), C, H, W, fptr(w), fptr(b), K, Ho, Wo, g->kh, g->kw, g->sy,
+        g->sx, g->py, g->px, g->dy, g->dx, g->groups, fptr(mean), fptr(rstd),
+        fptr(alpha), act, slope, fptr(out));
+    launch_ok("conv2d");
+}
+
+extern "C" void ops_unfold(struct ops *o, cl_mem in, int C, int H, int W,
+                           const struct conv_geom *g, cl_mem out)
+{
+    if (pending() || !need(in, "ops_unfold in") || !need(out, "ops_unfold out"))
+        return;
+    const int Ho = ops_conv_out(H, g->kh, g->sy, g->py, 1);
+    const int Wo = ops_conv_out(W, g->kw, g->sx, g->px, 1);
+    if (!count_ok((long)C * g->kh * g->kw * Ho * Wo, "unfold output"))
+        return;
+    const int n = Ho * Wo;
+    if (n <= 0)
+        return;
+    Prof p(o->ocl, "unfold");
+    unfold_kernel<<<dim3(cdiv(n, T256), C * g->kh * g->kw), T256, 0,
+                    stream_of(o->ocl)>>>(fptr(in), C, H, W, g->kh, g->kw,
+                                         g->sy, g->sx, g->py, g->px, 1, 1, Wo,
+                                         0, n, fptr(out));
+    launch_ok("unfold");
+}
+
+// ------------------------------------------------------- channel statistics
+
+// Mean and 1 / sqrt(biased variance + eps) of each channel (ops.cl:453-492
+// semantics: two passes over the plane).
+__global__ void chan_stats_kernel(const float *x, int HW, float eps,
+                                  float *mean, float *rstd)
+{
+    __shared__ float red[32];
+    const float *p = x + (size_t)blockIdx.x * HW;
+    float s = 0.0f;
+
+    for (int i = threadIdx.x; i < HW; i += blockDim.x)
+        s += p[i];
+    const float m = block_sum(s, red) / HW;
+    s = 0.0f;
+    for (int i = threadIdx.x; i < HW; i += blockDim.x) {
+        const float d = p[i] - m;
+        s = fmaf(d, d, s);
+    }
+    const float v = block_sum(s, red) / HW;
+    if (threadIdx.x == 0) {
+        mean[blockIdx.x] = m;
+        rstd[blockIdx.x] = rsqrtf(v + eps);
+    }
+}
+
+extern "C" void ops_chan_stats(struct ops *o, cl_mem x, int C, int HW, float eps,
+                               cl_mem mean, cl_mem rstd)
+{
+    if (pending() || !need(x, "ops_chan_stats x") || !need(mean, "mean") ||
+        !need(rstd, "rstd") || C <= 0)
+        return;
+    Prof p(o->ocl, "chan_stats");
+    chan_stats_kernel<<<C, 512, 0, stream_of(o->ocl)>>>(fptr(x), HW, eps,
+                                                        fptr(mean), fptr(rstd));
+    launch_ok("chan_stats");
+}
+
+__global__ void chan_affine_kernel(const float *X, float *Y, int HW, int total,
+                                   const float *mean, const float *rstd,
+                                   const float *g, const float *b, int act,
+                                   float slope)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total)
+        return;
+    const int c = i / HW;
+    float v = X[i];
+    if (mean)
+        v = (v - mean[c]) * rstd[c];
+    if (g)
+        v *= g[c];
+    if (b)
+        v += b[c];
+    Y[i] = apply_act(v, act, slope);
+}
+
+extern "C" void ops_chan_affine(struct ops *o, cl_mem X, cl_mem Y, int C,
+                                int HW, cl_mem mean, cl_mem rstd, cl_mem g,
+                                cl_mem b, int act, float slope)
+{
+    const long n = (long)C * HW;
+    if (pending() || !need(X, "ops_chan_affine X") || !need(Y, "Y") ||
+        !count_ok(n, "chan_affine") || n == 0)
+        return;
+    if (mean && !rstd) {
+        fail("ops_chan_affine: mean without rstd");
+        return;
+    }
+    Prof p(o->ocl, "chan_affine");
+    chan_affine_kernel<<<cdiv(n, T256), T256, 0, stream_of(o->ocl)>>>(
+        fptr(X), fptr(Y), HW, (int)n, fptr(mean), fptr(rstd), fptr(g), fptr(b),
+        act, slope);
+    launch_ok("chan_affine");
+}
+
+__global__ void prelu_kernel(const float *X, float *Y, int HW, int total,
+                             const float *alpha)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total)
+        return;
+    const float v = X[i];
+    Y[i] = v >= 0.0f ? v : alpha[i / HW] * v;
+}
+
+extern "C" void ops_prelu(struct ops *o, cl_mem X, cl_mem Y, int C, int HW,
+                          cl_mem alpha)
+{
+    const long n = (long)C * HW;
+    if (pending() || !need(X, "ops_prelu X") || !need(Y, "Y") ||
+        !need(alpha, "alpha") || !count_ok(n, "prelu") || n == 0)
+        return;
+    Prof p(o->ocl, "prelu");
+    prelu_kernel<<<cdiv(n, T256), T256, 0, stream_of(o->ocl)>>>(
+        fptr(X), fptr(Y), HW, (int)n, fptr(alpha));
+    launch_ok("prelu");
+}
+
+__global__ void act_kernel(const float *X, float *Y, int total, int act,
+                           float slope)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < total)
+        Y[i] = apply_act(X[i], act, slope);
+}
+
+extern "C" void ops_act(struct ops *o, cl_mem X, cl_mem Y, long n, int act,
+                        float slope)
+{
+    if (pending() || !need(X, "ops_act X") || !need(Y, "Y") ||
+        !count_ok(n, "act") || n == 0)
+        return;
+    Prof p(o->ocl, "act");
+    act_kernel<<<cdiv(n, T256), T256, 0, stream_of(o->ocl)>>>(
+        fptr(X), fptr(Y), (int)n, act, slope);
+    launch_ok("act");
+}
+
+// ------------------------------------------------------ LayerNorm, softmax
+
+// Row LayerNorm (ops.cl:547-578 semantics: two passes, rsqrt(var + eps),
+// optional affine, activation); Y may alias X. One block per row.
+template <typename TO>
+__global__ void layernorm_kernel(const float *X, TO *Y, const float *g,
+                                 const float *bt, int C, float eps, int act,
+                                 float slope)
+{
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const float *x = X + row * C;
+    TO *y = Y + row * C;
+    float s = 0.0f;
+
+    for (int c = threadIdx.x; c < C; c += blockDim.x)
+        s += x[c];
+    const float mean = block_sum(s, red) / C;
+    s = 0.0f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float d = x[c] - mean;
+        s = fmaf(d, d, s);
+    }
+    const float r = rsqrtf(block_sum(s, red) / C + eps);
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float v = (x[c] - mean) * r;
+        if (g)
+            v = v * g[c] + bt[c];
+        stf(y + c, apply_act(v, act, slope));
+    }
+}
+
+namespace coreg {
+void layernorm_rows(cudaStream_t st, const float *X, void *Y, DType ty,
+                    const float *g, const float *b, long rows, int C, float eps,
+                    int act, float slope)
+{
+    const int t = C >= 512 ? 256 : C >= 128 ? 128 : 32;
+    if (rows <= 0)
+        return;
+    if (ty == DT_BF16)
+        layernorm_kernel<__nv_bfloat16><<<(unsigned)rows, t, 0, st>>>(
+            X, (__nv_bfloat16 *)Y, g, b, C, eps, act, slope);
+    else
+        layernorm_kernel<float><<<(unsigned)rows, t, 0, st>>>(
+            X, (float *)Y, g, b, C, eps, act, slope);
+}
+}  // namespace coreg
+
+extern "C" void ops_layernorm(struct ops *o, long rows, int C, cl_mem X,
+                              cl_mem Y, cl_mem g, cl_mem b, float eps, int act,
+                              float slope)
+{
+    if (pending() || !need(X, "ops_layernorm X") || !need(Y, "Y"))
+        return;
+    if (g && !b) {
+        fail("ops_layernorm: gamma without beta");
+        return;
+    }
+    Prof p(o->ocl, "layernorm");
+    layernorm_rows(stream_of(o->ocl), fptr(X), fptr(Y), DT_F32, fptr(g),
+                   fptr(b), rows, C, eps, act, slope);
+    launch_ok("layernorm");
+}
+
+// In-place softmax(scale * x) over rows (ops.cl:583-602 semantics).
+__global__ void softmax_kernel(float *S, int L, float scale)
+{
+    __shared__ float red[32];
+    float *s = S + (size_t)blockIdx.x * L;
+    float m = -INFINITY, sum = 0.0f;
+
+    for (int j = threadIdx.x; j < L; j += blockDim.x)
+        m = fmaxf(m, s[j] * scale);
+    m = block_max(m, red);
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+        const float v = expf(s[j] * scale - m);
+        s[j] = v;
+        sum += v;
+    }
+    const float inv = 1.0f / block_sum(sum, red);
+    for (int j = threadIdx.x; j < L; j += blockDim.x)
+        s[j] *= inv;
+}
+
+extern "C" void ops_softmax_rows(struct ops *o, cl_mem S, long rows, int L,
+                                 float scale)
+{
+    if (pending() || !need(S, "ops_softmax_rows S") || rows <= 0)
+        return;
+    const int t = L >= 512 ? 256 : L >= 128 ? 128 : 32;
+    Prof p(o->ocl, "softmax_rows");
+    softmax_kernel<<<(unsigned)rows, t, 0, stream_of(o->ocl)>>>(fptr(S), L,
+                                                                scale);
+    launch_ok("softmax_rows");
+}
+
+// --------------------------------------------------------------- attention
+
+// O = softmax(scale Q K^T) V per head, never storing the scores
+// (ops.cl:604-687 semantics: key mask, a query without keys gets zeros).
+// Block: 4 warps x 4 queries each (16 queries) of one head; keys in
+// chunks of 32 through shared memory, lane j scoring key j of the chunk,
+// each lane owning output columns lane, lane + 32, ...
+#define ATT_Q 16
+#define ATT_KC 32
+__global__ void __launch_bounds__(128)
+attention_kernel(const float *Q, long ldq, const float *K, long ldk,
+                 const float *V, long ldv, float *O, long ldo, int Nq, int Nk,
+                 int d, float scale, const unsigned char *kmask)
+{
+    __shared__ float qs[ATT_Q][OPS_MAX_HEAD_DIM + 1];
+    __shared__ float ks[ATT_KC][OPS_MAX_HEAD_DIM + 1];
+    __shared__ float vs[ATT_KC][OPS_MAX_HEAD_DIM];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int h = blockIdx.y, q0 = blockIdx.x * ATT_Q;
+    const int nd = (d + 31) / 32;
+    float o[4][4], m[4], l[4];
+
+    Q += (size_t)h * d;
+    K += (size_t)h * d;
+    V += (size_t)h * d;
+    for (int e = threadIdx.x; e < ATT_Q * d; e += blockDim.x) {
+        const int r = e / d, c = e % d, q = q0 + r;
+        qs[r][c] = q < Nq ? Q[(size_t)q * ldq + c] * scale : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            o[i][t] = 0.0f;
+    }
+    for (int k0 = 0; k0 < Nk; k0 += ATT_KC) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < ATT_KC * d; e += blockDim.x) {
+            const int r = e / d, c = e % d, k = k0 + r;
+            ks[r][c] = k < Nk ? K[(size_t)k * ldk + c] : 0.0f;
+            vs[r][c] = k < Nk ? V[(size_t)k * ldv + c] : 0.0f;
+        }
+        __syncthreads();
+        const int key = k0 + lane;
+        const bool ok = key < Nk && (!kmask || kmask[key]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = wid * 4 + i;
+            float s = -INFINITY;
+            if (ok) {
+                s = 0.0f;
+                for (int c = 0; c < d; c++)
+                    s = fmaf(qs[r][c], ks[lane][c], s);
+            }
+            const float mn = fmaxf(m[i], warp_max(s));
+            if (mn == -INFINITY)
+                continue;
+            const float corr = expf(m[i] - mn);
+            const float e = ok ? expf(s - mn) : 0.0f;
+            l[i] = l[i] * corr + warp_sum(e);
+            m[i] = mn;
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+                o[i][t] *= corr;
+            for (int j = 0; j < ATT_KC; j++) {
+                const float pj = __shfl_sync(0xffffffffu, e, j);
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    if (t < nd && lane + 32 * t < d)
+                        o[i][t] = fmaf(pj, vs[j][lane + 32 * t], o[i][t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = q0 + wid * 4 + i;
+        if (q >= Nq)
+            continue;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const int c = lane + 32 * t;
+            if (c < d)
+                O[(size_t)q * ldo + (size_t)h * d + c] =
+                    l[i] > 0.0f ? o[i][t] / l[i] : 0.0f;
+        }
+    }
+}
+
+extern "C" void ops_attention(struct ops *o, struct opnd Q, struct opnd K,
+                              struct opnd V, struct opnd O, int Nq, int Nk,
+                              int nh, int d, float scale, cl_mem kmask)
+{
+    if (pending() || !need(Q.buf, "ops_attention Q") || !need(K.buf, "K") ||
+        !need(V.buf, "V") || !need(O.buf, "O"))
+        return;
+    if (d < 1 || d > OPS_MAX_HEAD_DIM) {
+        fail("CUDA: attention head dimension %d not in 1..%d", d,
+             OPS_MAX_HEAD_DIM);
+        return;
+    }
+    if (Nq <= 0 || nh <= 0)
+        return;
+    Prof p(o->ocl, "attention");
+    attention_kernel<<<dim3(cdiv(Nq, ATT_Q), nh), 128, 0, stream_of(o->ocl)>>>(
+        fptr(Q.buf, Q.off), Q.ld, fptr(K.buf, K.off), K.ld, fptr(V.buf, V.off),
+        V.ld, fptr(O.buf, O.off), O.ld, Nq, Nk, d, scale,
+        kmask ? (const unsigned char *)kmask->ptr : nullptr);
+    launch_ok("attention");
+}
+
+// ------------------------------------------------------------------- RoPE
+
+// Rotary encoding in place (ops.cl:695-716 semantics).
+__global__ void rope_kernel(float *X, long ld, int nh, int d, int npos,
+                            const float2 *cs, int interleaved, int total)
+{
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= total)
+        return;
+    const int nf = d / 2;
+    const int f = gid % nf, h = (gid / nf) % nh, r = gid / (nf * nh);
+    float *x = X + (size_t)r * ld + (size_t)h * d;
+    const float2 rot = cs[(r % npos) * nf + f];
+    const int i0 = interleaved ? 2 * f : f;
+    const int i1 = interleaved ? 2 * f + 1 : f + nf;
+    const float a = x[i0], b = x[i1];
+    x[i0] = a * rot.x - b * rot.y;
+    x[i1] = a * rot.y + b * rot.x;
+}
+
+extern "C" void ops_rope(struct ops *o, cl_mem X, long off, int ld, long rows,
+                         int nh, int d, int npos, cl_mem cs, int interleaved)
+{
+    const long n = rows * nh * (d / 2);
+    if (pending() || !need(X, "ops_rope X") || !need(cs, "cs") ||
+        !count_ok(n, "rope") || n == 0)
+        return;
+    if (npos < 1) {
+        fail("ops_rope: npos %d", npos);
+        return;
+    }
+    Prof p(o->ocl, "rope");
+    rope_kernel<<<cdiv(n, T256), T256, 0, stream_of(o->ocl)>>>(
+        fptr(X, off), ld, nh, d, npos, (const float2 *)cs->ptr, interleaved,
+        (int)n);
+    launch_ok("rope");
+}
+
+// ------------------------------------------------------ resampling, pooling
+
+// Bilinear resampling into channels coff.. of out (ops.cl:723-754
+// semantics: align_corners, else source step sy/sx clamped at 0).
+__global__ void resize_kernel(const float *in, int h, int w, float *out, int H,
+                              int W, int coff, int align, float sy, float sx)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y, c = blockIdx.z;
+    if (x >= W)
+        return;
+    float ux, uy;
+    if (align) {
+        ux = W > 1 ? x * (float)(w - 1) / (W - 1) : 0.0f;
+        uy = H > 1 ? y * (float)(h - 1) / (H - 1) : 0.0f;
+    }
+    else {
+        ux = fmaxf((x + 0.5f) * sx - 0.5f, 0.0f);
+        uy = fmaxf((y + 0.5f) * sy - 0.5f, 0.0f);
+    }
+    const int x0 = (int)ux, y0 = (int)uy;
+    const int x1 = min(x0 + 1, w - 1), y1 = min(y0 + 1, h - 1);
+    const float fx = ux - x0, fy = uy - y0;
+    const float *p = in + (size_t)c * h * w;
+    out[((size_t)(c + coff) * H + y) * W + x] =
+        (1.0f - fy) * ((1.0f - fx) * p[y0 * w + x0] + fx * p[y0 * w + x1]) +
+        fy * ((1.0f - fx) * p[y1 * w + x0] + fx * p[y1 * w + x1]);
+}
+
+namespace coreg {
+void resize_planes(cudaStream_t st, const float *in, int C, int h, int w,
+                   float *out, int H, int W, int coff, int align, float scale)
+{
+    const float sy = scale > 0 ? 1.0f / scale : (float)h / H;
+    const float sx = scale > 0 ? 1.0f / scale : (float)w / W;
+    if (C <= 0 || H <= 0 || W <= 0)
+        return;
+    resize_kernel<<<dim3(cdiv(W, 128), H, C), 128, 0, st>>>(in, h, w, out, H, W,
+                                                           coff, align, sy, sx);
+}
+}  // namespace coreg
+
+extern "C" void ops_resize(struct ops *o, cl_mem in, int C, int h, int w,
+                           cl_mem out, int H, int W, int coff,
+                           int align_corners, float scale)
+{
+    if (pending() || !need(in, "ops_resize in") || !need(out, "out"))
+        return;
+    Prof p(o->ocl, "resize_bilinear");
+    resize_planes(stream_of(o->ocl), fptr(in), C, h, w, fptr(out), H, W, coff,
+                  align_corners, scale);
+    launch_ok("resize_bilinear");
+}
+
+// Bilinear sampling at normalized points, zero padding (ops.cl:759-793).
+__global__ void grid_sample_kernel(const float *in, int C, int H, int W,
+                                   const float2 *grid, int n, int align,
+                                   float *out)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.y;
+    if (i >= n)
+        return;
+    const float *p = in + (size_t)c * H * W;
+    const float2 g = grid[i];
+    float ix, iy, v = 0.0f;
+    if (align) {
+        ix = (g.x + 1.0f) * 0.5f * (W - 1);
+        iy = (g.y + 1.0f) * 0.5f * (H - 1);
+    }
+    else {
+        ix = ((g.x + 1.0f) * W - 1.0f) * 0.5f;
+        iy = ((g.y + 1.0f) * H - 1.0f) * 0.5f;
+    }
+    if (isfinite(ix) && isfinite(iy)) {
+        const int x0 = (int)floorf(ix), y0 = (int)floorf(iy);
+        const float fx = ix - x0, fy = iy - y0;
+        auto at = [&](int yy, int xx) {
+            return xx >= 0 && xx < W && yy >= 0 && yy < H ? p[yy * W + xx]
+                                                          : 0.0f;
+        };
+        v = (1.0f - fy) * ((1.0f - fx) * at(y0, x0) + fx * at(y0, x0 + 1)) +
+            fy * ((1.0f - fx) * at(y0 + 1, x0) + fx * at(y0 + 1, x0 + 1));
+    }
+    out[(size_t)c * n + i] = v;
+}
+
+extern "C" void ops_grid_sample(struct ops *o, cl_mem in, int C, int H, int W,
+                                cl_mem grid, int n, int align_corners,
+                                cl_mem out)
+{
+    if (pending() || !need(in, "ops_grid_sample in") || !need(grid, "grid") ||
+        !need(out, "out") || n <= 0 || C <= 0)
+        return;
+    Prof p(o->ocl, "grid_sample");
+    grid_sample_kernel<<<dim3(cdiv(n, T256), C), T256, 0, stream_of(o->ocl)>>>(
+        fptr(in), C, H, W, (const float2 *)grid->ptr, n, align_corners,
+        fptr(out));
+    launch_ok("grid_sample");
+}
+
+__global__ void avgpool2_kernel(const float *in, int H, int W, float *out)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y, c = blockIdx.z;
+    const int w = W / 2;
+    if (x >= w)
+        return;
+    const float *p = in + ((size_t)c * H + 2 * y) * W + 2 * x;
+    out[((size_t)c * (H / 2) + y) * w + x] =
+        0.25f * (p[0] + p[1] + p[W] + p[W + 1]);
+}
+
+extern "C" void ops_avgpool2(struct ops *o, cl_mem in, int C, int H, int W,
+                             cl_mem out)
+{
+    if (pending() || !need(in, "ops_avgpool2 in") || !need(out, "out") ||
+        H < 2 || W < 2 || C <= 0)
+        return;
+    Prof p(o->ocl, "avgpool2");
+    avgpool2_kernel<<<dim3(cdiv(W / 2, 128), H / 2, C), 128, 0,
+                      stream_of(o->ocl)>>>(fptr(in), H, W, fptr(out));
+    launch_ok("avgpool2");
+}
+
+// k x k pooling (ops.cl:835-860 semantics: max ignores the padding,
+// average counts it).
+__global__ void pool2d_kernel(const float *in, int H, int W, int Ho, int Wo,
+                              int k, int s, int pad, int max, float *out)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int y = blockIdx.y, c = blockIdx.z;
+    if (x >= Wo)
+        return;
+    const float *p = in + (size_t)c * H * W;
+    float acc = max ? -INFINITY : 0.0f;
+    for (int i = 0; i < k; i++) {
+        const int iy = y * s - pad + i;
+        if (iy < 0 || iy >= H)
+            continue;
+        for (int j = 0; j < k; j++) {
+            const int ix = x * s - pad + j;
+            if (ix < 0 || ix >= W)
+                continue;
+            const float v = p[iy * W + ix];
+            acc = max ? fmaxf(acc, v) : acc + v;
+        }
+    }
+    out[((size_t)c * Ho + y) * Wo + x] = max ? acc : acc / (k * k);
+}
+
+extern "C" void ops_pool2d(struct ops *o, cl_mem in, int C, int H, int W, int k,
+                           int s, int p, int max, cl_mem out)
+{
+    if (pending() || !need(in, "ops_pool2d in") || !need(out, "out"))
+        return;
+    const int Ho = ops_conv_out(H, k, s, p, 1), Wo = ops_conv_out(W, k, s, p, 1);
+    if (Ho <= 0 || Wo <= 0 || C <= 0)
+        return;
+    Prof pr(o->ocl, max ? "maxpool" : "avgpool");
+    pool2d_kernel<<<dim3(cdiv(Wo, 128), Ho, C), 128, 0, stream_of(o->ocl)>>>(
+        fptr(in), H, W, Ho, Wo, k, s, p, max, fptr(out));
+    launch_ok("pool2d");
+}
+
+// ----------------------------------------------------- transpose, axpby
+
+__global__ void transpose_kernel(const float *in, float *out, int R, int C)
+{
+    __shared__ float t[32][33];
+    const size_t base = (size_t)blockIdx.z * R * C;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < R && c < C)
+            t[i][threadIdx.x] = in[base + (size_t)r * C + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < R && c < C)
+            out[base + (size_t)c * R + r] = t[threadIdx.x][i];
+    }
+}
+
+namespace coreg {
+void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
+                   int C)
+{
+    if (B <= 0 || R <= 0 || C <= 0)
+        return;
+    transpose_kernel<<<dim3(cdiv(C, 32), cdiv(R, 32), B), dim3(32, 8), 0, st>>>(
+        in, out, R, C);
+}
+}  // namespace coreg
+
+extern "C" void ops_transpose(struct ops *o, cl_mem in, cl_mem out, int B, int R,
+                              int C)
+{
+    if (pending() || !need(in, "ops_transpose in") || !need(out, "out") ||
+        !count_ok((long)B * R * C, "transpose"))
+        return;
+    Prof p(o->ocl, "transpose");
+    transpose_f32(stream_of(o->ocl), fptr(in), fptr(out), B, R, C);
+    launch_ok("transpose");
+}
+
+__global__ void axpby_kernel(float *out, const float *a, float alpha,
+                             const float *b, float beta, int n, int bmod)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n)
+        return;
+    out[i] = alpha * a[i] + (b ? beta * b[i % bmod] : 0.0f);
+}
+
+extern "C" void ops_axpby(struct ops *o, cl_mem out, cl_mem a, float alpha,
+                          cl_mem b, float beta, long n, long bmod)
+{
+    if (pending() || !need(out, "ops_axpby out") || !need(a, "a") ||
+        !count_ok(n, "axpby") || n == 0)
+        return;
+    Prof p(o->ocl, "axpby");
+    axpby_kernel<<<cdiv(n, T256), T256, 0, stream_of(o->ocl)>>>(
+        fptr(out), fptr(a), alpha, fptr(b), beta, (int)n,
+        bmod > 0 ? (int)bmod : 1);
+    launch_ok("axpby");
+}
+
+// ------------------------------------------------------------ BN folding
+
+// Host BatchNorm folding in double (ops.c:612-626 semantics).
+extern "C" void ops_fold_bn(float *w, float *b, int K, long per,
+                            const float *gamma, const float *beta,
+                            const float *mean, const float *var, float eps)
+{
+    for (int k = 0; k < K; k++) {
+        const double s = gamma[k] / sqrt((double)var[k] + eps);
+        for (long i = 0; i < per; i++)
+            w[(size_t)k * per + i] = (float)(w[(size_t)k * per + i] * s);
+        b[k] = (float)((b[k] - mean[k]) * s + beta[k]);
+    }
+}
