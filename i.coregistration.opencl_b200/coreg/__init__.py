@@ -135,12 +135,14 @@ def load(path=None):
     not exported."""
     global _lib
     if _lib is not None and path is None:
-        return _lib
-    lib = C.CDLL(str(path or LIB_PATH))
-    for name, (res, args) in SIGNATURES.items():
-        fn = getattr(lib, name)
-        fn.restype = res
-        fn.argtypes = args
+        lib = _lib
+    else:
+        lib = C.CDLL(str(path or LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+    # Model modules add their entry points to EXTRA_SIGNATURES on import.
     for name, (res, args) in EXTRA_SIGNATURES.items():
         fn = getattr(lib, name, None)
         if fn is not None:

@@ -38,6 +38,13 @@ struct GemmArgs {
     float slope;
     DType ab;  // type of A and B
     DType c;   // type of C and R
+    // A operand mode: 0 dense row-major; 1 implicit im2col of a 3x3 /
+    // stride 1 / padding 1 convolution over a channels-last (cH, cW, cC)
+    // image (row m = pixel, column k = (ky, kx, c)); 2 implicit im2col of
+    // a patchify convolution (cP x cP, stride cP) over a channels-last
+    // (cH, cW, cC) image (row m = patch, column k = (c, ky, kx)).
+    int amode;
+    int cH, cW, cC, cP;
 };
 
 inline GemmArgs gemm_args(int M, int N, int K)
@@ -64,5 +71,21 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count);
 // Dispatch: tensor cores when bf16 operands allow it, else SIMT.
 void gemm_run(const struct ocl_backend *ocl, const GemmArgs &g,
               const char *what);
+
+// Internal launchers of ops.cu shared with the models.
+void layernorm_rows(cudaStream_t st, const float *X, void *Y, DType ty,
+                    const float *g, const float *b, long rows, int C, float eps,
+                    int act, float slope);
+void attention_l(cudaStream_t st, const void *Q, long ldq, const void *K,
+                 long ldk, const void *V, long ldv, void *O, long ldo, int Nq,
+                 int Nk, int nh, int d, float scale, const unsigned char *kmask,
+                 DType t);
+void resize_planes(cudaStream_t st, const float *in, int C, int h, int w,
+                   float *out, int H, int W, int coff, int align, float scale);
+void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
+                   int C);
+// Double-precision GP solve (gp_chol.cu).
+void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
+                  double noise, float *X, double *work, int *flag);
 
 }  // namespace coreg

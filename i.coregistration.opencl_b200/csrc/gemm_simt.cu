@@ -14,6 +14,28 @@ namespace coreg {
 template <typename T>
 __device__ __forceinline__ float gld(const T *p) { return ldf(p); }
 
+// Element (m, k) of the A operand in its mode (see GemmArgs::amode).
+template <typename T>
+__device__ __forceinline__ float a_elem(const GemmArgs &g, const T *A, int m,
+                                        int k)
+{
+    if (g.amode == 1) {
+        const int C = g.cC, x = m % g.cW, y = m / g.cW;
+        const int c = k % C, kx = (k / C) % 3, ky = k / (3 * C);
+        const int yy = y + ky - 1, xx = x + kx - 1;
+        if (yy < 0 || yy >= g.cH || xx < 0 || xx >= g.cW)
+            return 0.0f;
+        return gld(A + ((long)yy * g.cW + xx) * C + c);
+    }
+    if (g.amode == 2) {
+        const int P = g.cP, pw = g.cW / P;
+        const int px = m % pw, py = m / pw;
+        const int kx = k % P, ky = (k / P) % P, c = k / (P * P);
+        return gld(A + ((long)(py * P + ky) * g.cW + px * P + kx) * g.cC + c);
+    }
+    return gld(A + (long)m * g.lda + k);
+}
+
 template <typename TA, typename TC, int BM, int BN, int TM, int TN>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(GemmArgs g)
@@ -47,7 +69,7 @@ gemm_simt_kernel(GemmArgs g)
         for (int i = 0; i < NA; i++) {
             const int e = tid + 256 * i, r = e / BK, c = e % BK;
             const int gm = m0 + r, gk = k0 + c;
-            ra[i] = gm < M && gk < K ? gld(A + (long)gm * g.lda + gk) : 0.0f;
+            ra[i] = gm < M && gk < K ? a_elem(g, A, gm, gk) : 0.0f;
         }
     };
     auto load_b = [&](int k0) {
@@ -191,7 +213,8 @@ void gemm_run(const struct ocl_backend *ocl, const GemmArgs &g,
 
     if (pending())
         return;
-    if (g.ab == DT_BF16 && g.transb && gemm_tc(stream_of(ocl), g, ocl->sm_count))
+    if (g.ab == DT_BF16 && g.transb && g.amode == 0 &&
+        gemm_tc(stream_of(ocl), g, ocl->sm_count))
         return;
     gemm_simt(stream_of(ocl), g);
 }

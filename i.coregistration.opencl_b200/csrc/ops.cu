@@ -571,10 +571,11 @@ extern "C" void ops_softmax_rows(struct ops *o, cl_mem S, long rows, int L,
 // each lane owning output columns lane, lane + 32, ...
 #define ATT_Q 16
 #define ATT_KC 32
+template <typename T>
 __global__ void __launch_bounds__(128)
-attention_kernel(const float *Q, long ldq, const float *K, long ldk,
-                 const float *V, long ldv, float *O, long ldo, int Nq, int Nk,
-                 int d, float scale, const unsigned char *kmask)
+attention_kernel(const T *Q, long ldq, const T *K, long ldk, const T *V,
+                 long ldv, T *O, long ldo, int Nq, int Nk, int d, float scale,
+                 const unsigned char *kmask)
 {
     __shared__ float qs[ATT_Q][OPS_MAX_HEAD_DIM + 1];
     __shared__ float ks[ATT_KC][OPS_MAX_HEAD_DIM + 1];
@@ -589,7 +590,7 @@ attention_kernel(const float *Q, long ldq, const float *K, long ldk,
     V += (size_t)h * d;
     for (int e = threadIdx.x; e < ATT_Q * d; e += blockDim.x) {
         const int r = e / d, c = e % d, q = q0 + r;
-        qs[r][c] = q < Nq ? Q[(size_t)q * ldq + c] * scale : 0.0f;
+        qs[r][c] = q < Nq ? ldf(Q + (size_t)q * ldq + c) * scale : 0.0f;
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -603,8 +604,8 @@ attention_kernel(const float *Q, long ldq, const float *K, long ldk,
         __syncthreads();
         for (int e = threadIdx.x; e < ATT_KC * d; e += blockDim.x) {
             const int r = e / d, c = e % d, k = k0 + r;
-            ks[r][c] = k < Nk ? K[(size_t)k * ldk + c] : 0.0f;
-            vs[r][c] = k < Nk ? V[(size_t)k * ldv + c] : 0.0f;
+            ks[r][c] = k < Nk ? ldf(K + (size_t)k * ldk + c) : 0.0f;
+            vs[r][c] = k < Nk ? ldf(V + (size_t)k * ldv + c) : 0.0f;
         }
         __syncthreads();
         const int key = k0 + lane;
@@ -646,11 +647,30 @@ attention_kernel(const float *Q, long ldq, const float *K, long ldk,
         for (int t = 0; t < 4; t++) {
             const int c = lane + 32 * t;
             if (c < d)
-                O[(size_t)q * ldo + (size_t)h * d + c] =
-                    l[i] > 0.0f ? o[i][t] / l[i] : 0.0f;
+                stf(O + (size_t)q * ldo + (size_t)h * d + c,
+                    l[i] > 0.0f ? o[i][t] / l[i] : 0.0f);
         }
     }
 }
+
+namespace coreg {
+void attention_l(cudaStream_t st, const void *Q, long ldq, const void *K,
+                 long ldk, const void *V, long ldv, void *O, long ldo, int Nq,
+                 int Nk, int nh, int d, float scale, const unsigned char *kmask,
+                 DType t)
+{
+    dim3 grid(cdiv(Nq, ATT_Q), nh);
+    if (t == DT_BF16)
+        attention_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(
+            (const __nv_bfloat16 *)Q, ldq, (const __nv_bfloat16 *)K, ldk,
+            (const __nv_bfloat16 *)V, ldv, (__nv_bfloat16 *)O, ldo, Nq, Nk, d,
+            scale, kmask);
+    else
+        attention_kernel<float><<<grid, 128, 0, st>>>(
+            (const float *)Q, ldq, (const float *)K, ldk, (const float *)V, ldv,
+            (float *)O, ldo, Nq, Nk, d, scale, kmask);
+}
+}  // namespace coreg
 
 extern "C" void ops_attention(struct ops *o, struct opnd Q, struct opnd K,
                               struct opnd V, struct opnd O, int Nq, int Nk,
@@ -667,10 +687,10 @@ extern "C" void ops_attention(struct ops *o, struct opnd Q, struct opnd K,
     if (Nq <= 0 || nh <= 0)
         return;
     Prof p(o->ocl, "attention");
-    attention_kernel<<<dim3(cdiv(Nq, ATT_Q), nh), 128, 0, stream_of(o->ocl)>>>(
-        fptr(Q.buf, Q.off), Q.ld, fptr(K.buf, K.off), K.ld, fptr(V.buf, V.off),
-        V.ld, fptr(O.buf, O.off), O.ld, Nq, Nk, d, scale,
-        kmask ? (const unsigned char *)kmask->ptr : nullptr);
+    attention_l(stream_of(o->ocl), fptr(Q.buf, Q.off), Q.ld, fptr(K.buf, K.off),
+                K.ld, fptr(V.buf, V.off), V.ld, fptr(O.buf, O.off), O.ld, Nq, Nk,
+                nh, d, scale, kmask ? (const unsigned char *)kmask->ptr : nullptr,
+                DT_F32);
     launch_ok("attention");
 }
 

@@ -1,0 +1,121 @@
+// SPDX-License-Identifier: Unlicense
+//
+// roma_ops.h: RoMa's kernels on channel-major float32 buffers, for
+// callers of the reference's kernel argument lists.
+
+#include "roma_kernels.cuh"
+#include "roma_ops.h"
+
+using namespace coreg;
+
+static bool bufs_ok(std::initializer_list<cl_mem> l, const char *what)
+{
+    if (pending())
+        return false;
+    for (cl_mem m : l)
+        if (!m) {
+            fail("%s: required buffer is NULL", what);
+            return false;
+        }
+    return true;
+}
+
+extern "C" void roma_row_norm(struct ops *o, cl_mem X, int rows, int C,
+                              cl_mem out)
+{
+    if (!bufs_ok({X, out}, "roma_row_norm"))
+        return;
+    Prof p(o->ocl, "roma_row_norm");
+    roma_row_norm_l(stream_of(o->ocl), fptr(X), rows, C, fptr(out));
+    launch_ok("roma_row_norm");
+}
+
+extern "C" void roma_cos_exp(struct ops *o, cl_mem S, cl_mem nx, cl_mem ny,
+                             int N, int M, float T, float eps)
+{
+    if (!bufs_ok({S, nx, ny}, "roma_cos_exp"))
+        return;
+    Prof p(o->ocl, "roma_cos_exp");
+    roma_cos_exp_l(stream_of(o->ocl), fptr(S), fptr(nx), fptr(ny), N, M, T, eps);
+    launch_ok("roma_cos_exp");
+}
+
+extern "C" void roma_cls_to_flow(struct ops *o, cl_mem L, int ld, int C,
+                                 int res, int n, cl_mem flow, cl_mem cert)
+{
+    if (!bufs_ok({L, flow, cert}, "roma_cls_to_flow"))
+        return;
+    Prof p(o->ocl, "roma_cls_to_flow");
+    roma_cls_to_flow_l(stream_of(o->ocl), fptr(L), ld, C, res, n, fptr(flow),
+                       fptr(cert));
+    launch_ok("roma_cls_to_flow");
+}
+
+extern "C" void roma_warp_sample(struct ops *o, cl_mem in, int C, int H, int W,
+                                 cl_mem flow, cl_mem out, int coff)
+{
+    if (!bufs_ok({in, flow, out}, "roma_warp_sample"))
+        return;
+    const long n = (long)H * W;
+    Prof p(o->ocl, "roma_warp_sample");
+    roma_warp_sample_l(stream_of(o->ocl), cm_map(fptr(in), n), C, H, W,
+                       fptr(flow), cm_out(fptr(out), n), coff);
+    launch_ok("roma_warp_sample");
+}
+
+extern "C" void roma_local_corr(struct ops *o, cl_mem f1, cl_mem f2, int C,
+                                int H, int W, int r, cl_mem flow, cl_mem out,
+                                int coff)
+{
+    if (!bufs_ok({f1, f2, flow, out}, "roma_local_corr"))
+        return;
+    const long n = (long)H * W;
+    Prof p(o->ocl, "roma_local_corr");
+    roma_local_corr_l(stream_of(o->ocl), cm_map(fptr(f1), n), cm_map(fptr(f2), n),
+                      C, H, W, r, fptr(flow), cm_out(fptr(out), n), coff);
+    launch_ok("roma_local_corr");
+}
+
+extern "C" void roma_disp(struct ops *o, cl_mem flow, int H, int W, float fx,
+                          float fy, cl_mem out)
+{
+    if (!bufs_ok({flow, out}, "roma_disp"))
+        return;
+    Prof p(o->ocl, "roma_disp");
+    roma_disp_l(stream_of(o->ocl), fptr(flow), H, W, fx, fy, fptr(out));
+    launch_ok("roma_disp");
+}
+
+extern "C" void roma_update(struct ops *o, cl_mem flow, cl_mem cert, cl_mem d,
+                            int n, float scale, float Wf, float Hf)
+{
+    if (!bufs_ok({flow, cert, d}, "roma_update"))
+        return;
+    Prof p(o->ocl, "roma_update");
+    roma_update_l(stream_of(o->ocl), fptr(flow), fptr(cert), cm_map(fptr(d), n),
+                  n, scale, Wf, Hf);
+    launch_ok("roma_update");
+}
+
+extern "C" void roma2_update(struct ops *o, cl_mem flow, cl_mem conf, cl_mem d,
+                             int n, float W, float H)
+{
+    if (!bufs_ok({flow, conf, d}, "roma2_update"))
+        return;
+    Prof p(o->ocl, "roma2_update");
+    roma2_update_l(stream_of(o->ocl), fptr(flow), fptr(conf), cm_map(fptr(d), n),
+                   n, W, H);
+    launch_ok("roma2_update");
+}
+
+extern "C" void roma_dwconv5(struct ops *o, cl_mem in, int C, int H, int W,
+                             cl_mem wt, cl_mem bias, cl_mem out)
+{
+    if (!bufs_ok({in, wt, bias, out}, "roma_dwconv5"))
+        return;
+    const long n = (long)H * W;
+    Prof p(o->ocl, "roma_dwconv5");
+    roma_dwconv5_l(stream_of(o->ocl), cm_map(fptr(in), n), C, H, W, fptr(wt),
+                   fptr(bias), cm_out(fptr(out), n));
+    launch_ok("roma_dwconv5");
+}
