@@ -1,0 +1,450 @@
+# SPDX-License-Identifier: Unlicense
+"""Benchmark of the dense-matching path: RoMa-v2ref tile pairs per second.
+
+One step = one roma_match of a tile pair at 864 x 864 with the coarse pass
+at 560 (the default matcher roma_v2ref), random
+init weights (seed 0) in the reference's layout, synthetic imagery of the
+configuration's generator. Tiles are independent, so N GPUs each process
+their own tiles (one process per GPU, no collective on the data path;
+"scaling": "weak"): value = all tiles / max-over-ranks device time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--precision bf16|fp32]
+  python bench.py --impl reference ...   (the CPU baseline arm)
+
+Prints one JSON line (rank 0).
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "i.coregistration.opencl_b200"))
+
+H = W = 864
+COARSE = 560
+TILE_SRC = 1024
+METRIC = "RoMa-v2ref tile pairs/s"
+UNIT = "tile_pairs/s"
+CACHE = Path(os.environ.get("COREG_CACHE", "/tmp/coreg_cache"))
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        # Host-side barrier and max-over-ranks of the device times only;
+        # the data path has no collective.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allmax(world, v):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_tiles(seeds):
+    """Synthetic 1024 x 1024 tile pairs of the configuration's scene
+    generator, resampled to the 864 x 864 processing size (float32 in
+    0..1, (3, H, W))."""
+    from scipy.ndimage import zoom
+
+    from coreg import synth
+
+    out = []
+    for s in seeds:
+        a, b, _ = synth.scene_pair(1000 + s, TILE_SRC, TILE_SRC)
+        pair = []
+        for img in (a, b):
+            f = img.astype(np.float32) / 255.0
+            f = zoom(f, (1, H / TILE_SRC, W / TILE_SRC), order=1, grid_mode=True, mode="nearest")
+            pair.append(np.ascontiguousarray(np.clip(f, 0, 1), np.float32))
+        out.append(pair)
+    return out
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.p = None
+        self.path = Path("/tmp") / f"coreg_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+            self.f.close()
+
+    def summary(self):
+        if not self.p or not self.path.exists():
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- work model
+
+def work_model(Hp=H, Wp=W, Cs=COARSE):
+    """Algorithmic FLOPs (tensor work) and bytes (memory-bound work) per
+    tile pair of roma_v2ref, by the profiler's operation names."""
+    D, c16 = 1024, Cs // 14
+    n16, ntok = c16 * c16, c16 * c16 + 1
+    fl, by = {}, {}
+
+    def add(d, k, v):
+        d[k] = d.get(k, 0) + v
+
+    for N, blocks, imgs in ((ntok, 24, 2), (n16, 5, 1)):
+        for name, f in (("qkv", 2 * N * D * 3 * D), ("proj", 2 * N * D * D),
+                        ("fc1", 2 * N * D * 4 * D), ("fc2", 2 * N * 4 * D * D),
+                        ("attention", 4 * N * N * D)):
+            add(fl, name, f * blocks * imgs)
+    add(fl, "patch_embed", 2 * 2 * n16 * 588 * D)
+    add(fl, "proj16", 2 * 2 * n16 * D * 512)
+    add(fl, "to_out", 2 * n16 * D * 4097)
+    add(fl, "gp_gemm", 3 * 2 * n16 * n16 * 512)
+    widths, blocks = (64, 128, 256, 512), (2, 2, 4, 4)
+
+    def vgg(h, w, nblk, name):
+        cin = 3
+        for b in range(nblk):
+            for _ in range(blocks[b]):
+                add(fl, name, 2 * 2 * h * w * 9 * cin * widths[b])
+                cin = widths[b]
+            if b < nblk - 1:
+                h, w = h // 2, w // 2
+
+    vgg(Cs, Cs, 4, "vgg_conv3x3")
+    vgg(Cs, Cs, 3, "vgg_conv3x3")
+    vgg(Hp, Wp, 3, "vgg_conv3x3")
+    add(fl, "vgg_proj", 2 * 2 * (Cs // 8) ** 2 * 512 * 512)
+    for hh, ww in ((Cs, Cs), (Hp, Wp)):
+        for sc, fin, fo in ((4, 256, 192), (2, 128, 48), (1, 64, 12)):
+            add(fl, "vgg2_proj", 2 * 2 * (hh // sc) * (ww // sc) * fin * fo)
+
+    def refiner(n, cin, feat, r, nout, es=4):
+        add(fl, "refiner_pw", 9 * 2 * n * cin * cin)
+        add(fl, "refiner_out", 2 * n * cin * nout)
+        add(fl, "roma_dwconv5", 9 * 2 * 25 * n * cin)
+        add(by, "roma_dwconv5", 9 * 2 * n * cin * es)
+        if r:
+            add(fl, "roma_local_corr", 2 * (2 * r + 2) ** 2 * feat * n)
+
+    refiner(c16 * c16, 1377, 512, 7, 3)
+    refiner((Cs // 8) ** 2, 1137, 512, 3, 3)
+    for hh, ww in ((Cs, Cs), (Hp, Wp)):
+        for sc, cin, feat, r in ((4, 512, 192, 3), (2, 128, 48, 1), (1, 32, 12, 0)):
+            refiner((hh // sc) * (ww // sc), cin, feat, r, 6)
+    return fl, by
+
+
+def profile_step(lib, dev, net, dA, dB):
+    """One profiled (per-launch CUDA events, serialized) tile: {name: (ms,
+    calls)}."""
+    import ctypes
+
+    lib.ops_report_reset()
+    dev.ocl.profile = 1
+    net.match_dev(dA, dB)
+    dev.finish()
+    dev.ocl.profile = 0
+    n = lib.ops_report_text(None, 0)
+    buf = ctypes.create_string_buffer(n)
+    lib.ops_report_text(buf, n)
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, ms, calls = line.rsplit(" ", 2)
+        out[name] = (float(ms), int(calls))
+    return out
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def traffic_from_profiles(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if
+    one exists (profiles/roofline_traffic.json), else None."""
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        v = d.get(kernel)
+        if v:
+            return v.get("dram_bytes_per_launch")
+    return None
+
+
+# -------------------------------------------------------------- CPU arm
+
+def cpu_sample(tiles, threads, reps=1):
+    """The oracle (the reference's roma.c restated, torch float32 on the
+    host cores) on full tile pairs: seconds per pair."""
+    import torch
+
+    from oracle import roma_ref
+    from coreg import synth
+
+    torch.set_num_threads(threads)
+    paths = synth.write_roma_weights(CACHE / "weights", 0)
+    sds = [synth.read_safetensors(p) for p in paths]
+    model = roma_ref.Model(*sds)
+    r = roma_ref.Runner(model, coarse=COARSE)
+    times = []
+    for i in range(reps):
+        a, b = tiles[i % len(tiles)]
+        t = time.perf_counter()
+        r.run(a, b)
+        times.append(time.perf_counter() - t)
+    return times
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    tiles = make_tiles(range(2))
+    times = cpu_sample(tiles, threads, reps=args.warmup_ref + args.steps_ref)
+    t = times[args.warmup_ref:] or times
+    v = len(t) / sum(t)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": len(t), "warmup": args.warmup_ref, "ms_per_step": 1000 * sum(t) / len(t),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded scene generator, random-init weights seed 0)",
+        "config": {"workload": "roma_v2ref tile pair, coarse 560, fine 864x864", "tile_px": H,
+                   "coarse_px": COARSE},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{len(t)} full tile pair(s) through the oracle "
+                                   "(torch float32 restatement of roma.c; the reference's "
+                                   "OpenCL path cannot run: no OpenCL platform on the box)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- GPU arm
+
+def gpu_arm(args, rank, world, local):
+    import coreg
+    from coreg import synth
+    from coreg.roma import Roma
+
+    prec = coreg.OPS_BF16 if args.precision == "bf16" else coreg.OPS_FP32
+    if rank == 0:
+        synth.write_roma_weights(CACHE / "weights", 0)
+    barrier(world)
+    main, dino, v2 = synth.write_roma_weights(CACHE / "weights", 0)
+    dev = coreg.Device(local, precision=prec)
+    lib = dev.lib
+    net = Roma(dev, main, dino, v2, H=H, W=W, coarse=COARSE)
+    ntiles = args.tiles
+    tiles = make_tiles([rank * ntiles + i for i in range(ntiles)])
+    hw3 = 3 * H * W
+    # Device-resident tiles, and the graph's fixed input buffers.
+    dtiles = [(dev.upload(a), dev.upload(b)) for a, b in tiles]
+    inA, inB = dev.alloc(hw3 * 4), dev.alloc(hw3 * 4)
+
+    def load_tile(i):
+        a, b = dtiles[i % ntiles]
+        lib.ocl_copy(dev.ocl_p, a.handle, 0, inA.handle, 0, hw3 * 4)
+        lib.ocl_copy(dev.ocl_p, b.handle, 0, inB.handle, 0, hw3 * 4)
+
+    kernels = net.graph_build(inA.ptr, inB.ptr)
+    for i in range(args.warmup):
+        load_tile(i)
+        net.graph_launch()
+    dev.finish()
+    net.sync()
+    barrier(world)
+    with Clocks(local) as clk:
+        lib.ocl_timer_start(dev.ocl_p)
+        for i in range(args.steps):
+            load_tile(i)
+            net.graph_launch()
+        ms = lib.ocl_timer_stop(dev.ocl_p)
+    coreg.check(lib)
+    net.sync()
+    ms_max = allmax(world, ms)
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # End to end through the public API: host (pinned) images in, host
+    # results out, per step.
+    pin = []
+    for a, b in tiles:
+        pa = lib.coreg_host_alloc(hw3 * 4)
+        pb = lib.coreg_host_alloc(hw3 * 4)
+        import ctypes
+
+        ctypes.memmove(pa, a.ctypes.data, hw3 * 4)
+        ctypes.memmove(pb, b.ctypes.data, hw3 * 4)
+        pin.append((pa, pb))
+    for i in range(min(2, args.warmup)):
+        pa, pb = pin[i % ntiles]
+        lib.roma_match(net.mp, pa, pb, None, 1)
+    coreg.check(lib)
+    barrier(world)
+    e2e_steps = max(1, args.steps // 2)
+    lib.ocl_timer_start(dev.ocl_p)
+    for i in range(e2e_steps):
+        pa, pb = pin[i % ntiles]
+        lib.roma_match(net.mp, pa, pb, None, 1)
+    e2e_ms = lib.ocl_timer_stop(dev.ocl_p)
+    coreg.check(lib)
+    e2e_max = allmax(world, e2e_ms)
+    e2e_value = world * e2e_steps / (e2e_max / 1000.0)
+    for pa, pb in pin:
+        lib.coreg_host_free(pa)
+        lib.coreg_host_free(pb)
+
+    # Roofline of the dominant kernel, from one profiled tile.
+    prof = profile_step(lib, dev, net, inA.ptr, inB.ptr)
+    fl, by = work_model()
+    hbm, bf16, peak_kind = peaks()
+    dom = max(prof, key=lambda k: prof[k][0])
+    roof = None
+    if dom in fl and (dom not in by or fl[dom] / max(by[dom], 1) > 50):
+        ms_d, calls = prof[dom]
+        ach = fl[dom] / (ms_d / 1000.0) / 1e12
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
+                "frac": ach / bf16, "peak_kind": peak_kind,
+                "traffic": traffic_from_profiles(dom), "launches_per_step": calls,
+                "algorithmic_per_launch": fl[dom] / calls}
+    elif dom in by:
+        ms_d, calls = prof[dom]
+        ach = by[dom] / (ms_d / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": hbm, "unit": "GB/s",
+                "frac": ach / hbm, "peak_kind": peak_kind,
+                "traffic": traffic_from_profiles(dom), "launches_per_step": calls,
+                "algorithmic_per_launch": by[dom] / calls}
+    tot_ms = sum(v[0] for v in prof.values())
+    shares = sorted(((k, v[0] / tot_ms) for k, v in prof.items()), key=lambda x: -x[1])[:8]
+    flops_pair = sum(fl.values())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        t = cpu_sample(tiles, threads, reps=1)
+        cpu = {"value": 1.0 / t[0], "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": "1 full tile pair (coarse 560, fine 864) through the oracle, torch "
+                         "float32 on the host cores (the reference's OpenCL path cannot run: "
+                         "no OpenCL platform on the box)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if prec else "f32",
+            "data": "synthetic (seeded scene generator per 1024^2 tile, resampled to 864^2; "
+                    "random-init weights seed 0)",
+            "config": {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 "
+                                   "(BASELINE configs[3])",
+                       "tile_px": H, "coarse_px": COARSE, "tiles_per_rank": ntiles,
+                       "parallelism": f"tiles sharded over {world} GPU(s)",
+                       "l2": "no flush: every step streams the weights and activations "
+                             "(> 1 GB) through the 126 MB L2"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * hw3 * 4,
+                    "d2h_bytes_per_step": 4 * H * W * 4,
+                    "api": "roma_match (host images in pinned memory, host results)"},
+            "gpu_launches": kernels * args.steps,
+            "roofline": roof,
+            "path_tflops": flops_pair / (ms_max / args.steps / 1000.0) / 1e12,
+            "time_shares": {k: round(v, 4) for k, v in shares},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    net.close()
+    dev.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--tiles", type=int, default=4, help="distinct tile pairs per GPU")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--steps-ref", type=int, default=2, help="CPU-arm timed tile pairs")
+    ap.add_argument("--warmup-ref", type=int, default=0)
+    args = ap.parse_args()
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+    else:
+        gpu_arm(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -81,6 +81,10 @@ EXTRA_SIGNATURES.update({
     "roma_match_dev": (None, [C.POINTER(RomaModel), P, P]),
     "roma_results_dev": (None, [C.POINTER(RomaModel), C.POINTER(P), C.POINTER(P), C.POINTER(P)]),
     "roma_sync": (I, [C.POINTER(RomaModel)]),
+    "roma_graph_build": (I, [C.POINTER(RomaModel), P, P]),
+    "roma_graph_launch": (None, [C.POINTER(RomaModel)]),
+    "coreg_host_alloc": (P, [C.c_size_t]),
+    "coreg_host_free": (None, [P]),
     "roma_free": (None, [C.POINTER(RomaModel)]),
     "matcher_roma_create": (None, [C.POINTER(Matcher), C.POINTER(Ops), C.POINTER(PthFile),
                                    C.POINTER(PthFile), C.POINTER(PthFile), C.c_char_p, I, I, F]),
@@ -151,6 +155,14 @@ class Roma:
         r = self.lib.roma_sync(self.mp)
         check(self.lib)
         return r
+
+    def graph_build(self, ptrA, ptrB):
+        n = self.lib.roma_graph_build(self.mp, ptrA, ptrB)
+        check(self.lib)
+        return n
+
+    def graph_launch(self):
+        self.lib.roma_graph_launch(self.mp)
 
     def close(self):
         if self.mp is not None:

@@ -445,3 +445,29 @@ extern "C" void ocl_finish(struct ocl_backend *ocl)
         return;
     cuda_ok(cudaStreamSynchronize(stream_of(ocl)), "cudaStreamSynchronize");
 }
+
+// One pair of timing events per thread (ocl_timer_start / _stop).
+static thread_local cudaEvent_t t_ev0 = nullptr, t_ev1 = nullptr;
+
+extern "C" void ocl_timer_start(struct ocl_backend *ocl)
+{
+    if (pending())
+        return;
+    if (!t_ev0) {
+        cudaEventCreate(&t_ev0);
+        cudaEventCreate(&t_ev1);
+    }
+    cuda_ok(cudaEventRecord(t_ev0, stream_of(ocl)), "cudaEventRecord");
+}
+
+extern "C" double ocl_timer_stop(struct ocl_backend *ocl)
+{
+    float ms = 0;
+    if (pending() || !t_ev0)
+        return -1;
+    if (!cuda_ok(cudaEventRecord(t_ev1, stream_of(ocl)), "cudaEventRecord") ||
+        !cuda_ok(cudaEventSynchronize(t_ev1), "cudaEventSynchronize") ||
+        !cuda_ok(cudaEventElapsedTime(&ms, t_ev0, t_ev1), "cudaEventElapsedTime"))
+        return -1;
+    return ms;
+}

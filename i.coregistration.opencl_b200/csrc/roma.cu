@@ -120,6 +120,8 @@ struct roma_impl {
     float *o_flow, *o_cert, *o_sd;
     PilDev pil_cx, pil_cy, pil_fx, pil_fy;
     bool alloc_done = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
 };
 
 // ------------------------------------------------------------- utilities
@@ -687,6 +689,10 @@ extern "C" void roma_free(struct roma_model *m)
     if (I) {
         cudaSetDevice(m->ocl->device);
         cudaStreamSynchronize(stream_of(m->ocl));
+        if (I->graph_exec)
+            cudaGraphExecDestroy(I->graph_exec);
+        if (I->graph)
+            cudaGraphDestroy(I->graph);
         for (void *p : I->allocs)
             cudaFree(p);
         delete I;
@@ -1422,4 +1428,78 @@ extern "C" void roma_match(struct roma_model *m, const float *imgA,
         if (m->v2)
             dump_host(c, "sd", m->sd, hw);
     }
+}
+
+extern "C" int roma_graph_build(struct roma_model *m, const float *imgA,
+                                const float *imgB)
+{
+    if (!ready(m))
+        return -1;
+    cudaSetDevice(m->ocl->device);
+    roma_impl *I = m->impl;
+    cudaStream_t st = stream_of(m->ocl);
+    if (I->graph_exec) {
+        cudaGraphExecDestroy(I->graph_exec);
+        I->graph_exec = nullptr;
+    }
+    if (I->graph) {
+        cudaGraphDestroy(I->graph);
+        I->graph = nullptr;
+    }
+    if (!cuda_ok(cudaStreamSynchronize(st), "roma_graph_build") ||
+        !cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal),
+                 "cudaStreamBeginCapture"))
+        return -1;
+    Ctx c{m, I, st, nullptr, 0};
+    run_tile(c, imgA, imgB);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (pending() || !cuda_ok(e, "cudaStreamEndCapture")) {
+        if (g)
+            cudaGraphDestroy(g);
+        return -1;
+    }
+    I->graph = g;
+    if (!cuda_ok(cudaGraphInstantiate(&I->graph_exec, g, 0), "cudaGraphInstantiate"))
+        return -1;
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    int kernels = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        cudaGraphNodeGetType(nd, &t);
+        kernels += t == cudaGraphNodeTypeKernel;
+    }
+    return kernels;
+}
+
+extern "C" void roma_graph_launch(struct roma_model *m)
+{
+    if (!ready(m))
+        return;
+    if (!m->impl->graph_exec) {
+        fail("RoMa: roma_graph_launch before roma_graph_build");
+        return;
+    }
+    cudaSetDevice(m->ocl->device);
+    cuda_ok(cudaGraphLaunch(m->impl->graph_exec, stream_of(m->ocl)),
+            "cudaGraphLaunch");
+}
+
+extern "C" void *coreg_host_alloc(size_t bytes)
+{
+    void *p = nullptr;
+    if (pending())
+        return nullptr;
+    if (!cuda_ok(cudaMallocHost(&p, bytes ? bytes : 16), "cudaMallocHost"))
+        return nullptr;
+    return p;
+}
+
+extern "C" void coreg_host_free(void *p)
+{
+    if (p)
+        cudaFreeHost(p);
 }

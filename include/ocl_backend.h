@@ -83,6 +83,12 @@ void ocl_zero(struct ocl_backend *ocl, cl_mem m, size_t off, size_t n);
 /* Wait for every launch of the backend's stream. */
 void ocl_finish(struct ocl_backend *ocl);
 
+/* Device timing of the backend's stream: ocl_timer_start records a CUDA
+ * event on it, ocl_timer_stop records a second one, waits for it and
+ * returns the milliseconds between them. */
+void ocl_timer_start(struct ocl_backend *ocl);
+double ocl_timer_stop(struct ocl_backend *ocl);
+
 /* Error handling of every entry point of the library. */
 #define COREG_ERRORS_FATAL 0
 #define COREG_ERRORS_RECORD 1

@@ -105,6 +105,19 @@ void roma_results_dev(struct roma_model *m, float **flow, float **cert,
  * during the tiles run since the last call; 0 when all is well. */
 int roma_sync(struct roma_model *m);
 
+/* Capture one tile (roma_match_dev on these device images) into a CUDA
+ * graph held by the model, replacing any previous one; returns the number
+ * of kernel launches it holds, or -1 on error. roma_graph_launch replays
+ * it on the model's stream (asynchronous; the images are read at replay
+ * time, so new tiles are written into the same device buffers). */
+int roma_graph_build(struct roma_model *m, const float *imgA,
+                     const float *imgB);
+void roma_graph_launch(struct roma_model *m);
+
+/* Pinned host memory (for asynchronous host <-> device copies). */
+void *coreg_host_alloc(size_t bytes);
+void coreg_host_free(void *p);
+
 #ifdef __cplusplus
 }
 #endif
