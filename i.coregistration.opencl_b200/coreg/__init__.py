@@ -126,6 +126,7 @@ SIGNATURES = {
     "ops_transpose": (None, [C.POINTER(Ops), P, P, I, I, I]),
     "ops_axpby": (None, [C.POINTER(Ops), P, P, F, P, F, L, L]),
     "ops_fold_bn": (None, [P, P, I, L, P, P, P, P, F]),
+    "coreg_tc_status": (I, []),
 }
 
 _lib = None

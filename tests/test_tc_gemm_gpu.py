@@ -1,0 +1,69 @@
+# SPDX-License-Identifier: Unlicense
+"""The tcgen05 tensor-core GEMM (ops_gemm with precision OPS_BF16, the
+reference's gemm contract of ops.cl:39-52) against the oracle evaluated on
+the bfloat16-rounded operands (GPU).
+
+Float32 accumulation of bfloat16 products: the result must match the
+float64 product of the rounded operands to float32 accumulation error
+(relative L2 <= 1e-5); against the float32 operands it is within the
+bfloat16 mode bound of the build's contract (relative L2 <= 2e-2)."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import coreg
+from coreg import Opnd
+from oracle.ops_ref import gemm as ref_gemm
+
+SHAPES = [
+    # M, N, K, act, residual
+    (128, 256, 64, 0, False),
+    (300, 200, 96, 2, True),     # BN 128 tiles, ragged M and N
+    (77, 130, 40, 1, False),     # one ragged tile, K below one stage
+    (1601, 3072, 1024, 0, False),  # DINOv2 qkv
+    (1601, 1024, 4096, 0, True),   # DINOv2 fc2 with the residual
+    (1600, 4097, 1024, 0, False),  # decoder to_out (odd N)
+    (4900, 1136, 1136, 0, False),  # refiner 1 x 1 at 1/8
+]
+
+
+def bf16_round(x):
+    u = np.asarray(x, np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+@pytest.fixture(scope="module")
+def dev16():
+    d = coreg.Device(0, precision=coreg.OPS_BF16)
+    yield d
+    d.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"{s[0]}x{s[1]}x{s[2]}" for s in SHAPES])
+def test_tc_gemm_matches_rounded_oracle(dev16, shape):
+    M, N, K, act, residual = shape
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    a = rng.standard_normal((M, K), dtype=np.float32)
+    b = (rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)).astype(np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    A, B, Bi = dev16.upload(a), dev16.upload(b), dev16.upload(bias)
+    Cb = dev16.upload(r) if residual else dev16.zeros(M * N)
+    lib = dev16.lib
+    lib.ops_gemm(dev16.ops_p, M, N, K, Opnd(A.handle, 0, K, 0, 0), Opnd(B.handle, 0, K, 0, 0), 1,
+                 Opnd(Cb.handle, 0, N, 0, 0), 1, 1, Bi.handle, 0,
+                 Cb.handle if residual else None, 0, 0.75, act, 0.1)
+    got = Cb.read(count=M * N).reshape(M, N)
+    coreg.check(lib)
+    assert lib.coreg_tc_status() == 0
+    want = ref_gemm(bf16_round(a), bf16_round(b), 1, M, N, K, bias=bias, R=r if residual else None,
+                    alpha=0.75, a=act, slope=0.1)[0]
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err
+    want32 = ref_gemm(a, b, 1, M, N, K, bias=bias, R=r if residual else None, alpha=0.75, a=act,
+                      slope=0.1)[0]
+    assert np.linalg.norm(got - want32) / np.linalg.norm(want32) <= 2e-2
