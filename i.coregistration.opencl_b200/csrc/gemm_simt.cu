@@ -213,8 +213,7 @@ void gemm_run(const struct ocl_backend *ocl, const GemmArgs &g,
 
     if (pending())
         return;
-    if (g.ab == DT_BF16 && g.transb && g.amode == 0 &&
-        gemm_tc(stream_of(ocl), g, ocl->sm_count))
+    if (g.ab == DT_BF16 && g.transb && gemm_tc(stream_of(ocl), g, ocl->sm_count))
         return;
     gemm_simt(stream_of(ocl), g);
 }

@@ -327,6 +327,86 @@ extern "C" void ops_conv2d(struct ops *o, cl_mem in, int C, int H, int W,
     launch_ok("conv2d");
 }
 
+// (K, C, 3, 3) -> (K, 3, 3, C), converted to T.
+template <typename T>
+__global__ void conv3_reorder_k(const float *w, int K, int C, T *out)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)K * C * 9)
+        return;
+    const int c = (int)(e % C), t = (int)((e / C) % 9), k = (int)(e / (9L * C));
+    stf(out + e, w[((long)k * C + c) * 9 + t]);
+}
+
+template <typename T>
+__global__ void to_type_k(const float *in, long n, T *out)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < n)
+        stf(out + e, in[e]);
+}
+
+extern "C" void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C,
+                               cl_mem w, cl_mem b, int K, int act, float slope,
+                               cl_mem out)
+{
+    if (pending() || !need(in, "ops_conv3x3_cl in") || !need(w, "w") ||
+        !need(out, "out"))
+        return;
+    const long n = (long)H * W;
+    if (!count_ok(n * C, "conv3x3 input") || !count_ok(n * K, "conv3x3 output") ||
+        n <= 0 || K <= 0 || C <= 0)
+        return;
+    const bool tc = o->precision == OPS_BF16 && C % 64 == 0;
+    const size_t es = tc ? 2 : 4;
+    const size_t wbytes = ((size_t)K * 9 * C * es + 255) / 256 * 256;
+    const size_t bytes = wbytes + (tc ? (size_t)n * C * 2 : 0);
+    cl_mem *scr = tc ? &o->scratch16 : &o->scratch;
+    size_t *cap = tc ? &o->scratch16_bytes : &o->scratch_bytes;
+    if (bytes > *cap) {
+        ocl_release(scr);
+        *scr = ocl_alloc(o->ocl, bytes, "conv3x3 operands");
+        *cap = bytes;
+        if (pending())
+            return;
+    }
+    cudaStream_t st = stream_of(o->ocl);
+    void *wr = (*scr)->ptr, *a = in->ptr;
+    const long nw = (long)K * 9 * C;
+    {
+        Prof p(o->ocl, "conv3x3_pack");
+        if (tc) {
+            conv3_reorder_k<__nv_bfloat16><<<cdiv(nw, 256), 256, 0, st>>>(
+                fptr(w), K, C, (__nv_bfloat16 *)wr);
+            a = (char *)wr + wbytes;
+            to_type_k<__nv_bfloat16><<<cdiv(n * C, 256), 256, 0, st>>>(
+                fptr(in), n * C, (__nv_bfloat16 *)a);
+        }
+        else
+            conv3_reorder_k<float><<<cdiv(nw, 256), 256, 0, st>>>(fptr(w), K, C,
+                                                                  (float *)wr);
+        if (!launch_ok("conv3x3_pack"))
+            return;
+    }
+    GemmArgs g = gemm_args((int)n, K, 9 * C);
+    g.A = a;
+    g.amode = 1;
+    g.cH = H;
+    g.cW = W;
+    g.cC = C;
+    g.B = wr;
+    g.ldb = 9 * C;
+    g.transb = 1;
+    g.C = out->ptr;
+    g.ldc = K;
+    g.bias = fptr(b);
+    g.act = act;
+    g.slope = slope;
+    g.ab = tc ? DT_BF16 : DT_F32;
+    g.c = DT_F32;
+    gemm_run(o->ocl, g, tc ? "conv3x3_tc" : "conv3x3");
+}
+
 extern "C" void ops_unfold(struct ops *o, cl_mem in, int C, int H, int W,
                            const struct conv_geom *g, cl_mem out)
 {

@@ -61,6 +61,7 @@ struct Block {
 
 struct Refiner {
     int scale, feat, emb, radius, cin, nout;
+    int cinp; // cin padded (row stride of the refiner maps)
     float *dw_w[ROMA_HIDDEN + 1], *dw_b[ROMA_HIDDEN + 1];
     void *pw_w[ROMA_HIDDEN + 1];
     float *pw_b[ROMA_HIDDEN + 1];
@@ -333,6 +334,20 @@ bool load_block(roma_impl *I, struct pth_file *pf, const std::string &pre,
     return !pending();
 }
 
+// rows x cols row-major into prows x pcols, zero padded.
+std::vector<float> pad_matrix(const float *v, int rows, int cols, int prows,
+                              int pcols)
+{
+    std::vector<float> out((size_t)prows * pcols, 0.0f);
+    for (int r = 0; r < rows; r++)
+        memcpy(&out[(size_t)r * pcols], v + (size_t)r * cols, cols * sizeof(float));
+    return out;
+}
+
+// Refiner input width padded to a multiple of 16 channels (16-byte rows
+// of bfloat16 for the tensor-memory-access loads of the 1 x 1 GEMMs).
+int pad16(int c) { return (c + 15) / 16 * 16; }
+
 // ConvRefiner blocks: depthwise 5 x 5 with its BatchNorm folded, 1 x 1.
 bool load_ref_blocks(roma_impl *I, struct pth_file *pf, Refiner *r,
                      const std::string &pre, bool v2)
@@ -348,10 +363,21 @@ bool load_ref_blocks(roma_impl *I, struct pth_file *pf, Refiner *r,
         std::vector<float> w, bias;
         if (!conv_bn_host(pf, conv, bn, r->cin, 4, sdw, w, bias))
             return false;
+        // Channels padded to cinp with zero weights and biases: the padded
+        // channels of every block stay 0.
+        w.resize((size_t)r->cinp * 25, 0.0f);
+        bias.resize(r->cinp, 0.0f);
         r->dw_w[b] = upload_f(I, w.data(), w.size(), "dw");
         r->dw_b[b] = upload_f(I, bias.data(), bias.size(), "dw");
-        r->pw_w[b] = load_dev(I, pf, pw + ".weight", 4, spw, I->wt);
-        r->pw_b[b] = (float *)load_dev(I, pf, pw + ".bias", 1, sb, DT_F32);
+        HostT pw_w, pw_b;
+        if (!read_host(pf, (pw + ".weight").c_str(), 4, spw, pw_w) ||
+            !read_host(pf, (pw + ".bias").c_str(), 1, sb, pw_b))
+            return false;
+        std::vector<float> pwp = pad_matrix(pw_w.v, r->cin, r->cin, r->cinp, r->cinp);
+        std::vector<float> pbp(pw_b.v, pw_b.v + r->cin);
+        pbp.resize(r->cinp, 0.0f);
+        r->pw_w[b] = upload(I, pwp.data(), pwp.size(), I->wt, "pw");
+        r->pw_b[b] = upload_f(I, pbp.data(), pbp.size(), "pw");
     }
     return !pending();
 }
@@ -366,13 +392,20 @@ bool load_refiner(roma_impl *I, struct pth_file *pf, int s)
     r->radius = ref_radius[s];
     const int corr = r->radius ? (2 * r->radius + 1) * (2 * r->radius + 1) : 0;
     r->cin = 2 * r->feat + r->emb + corr;
+    r->cinp = pad16(r->cin);
     r->nout = 3;
     const std::string pre = fmt("decoder.conv_refiner.%d", r->scale);
     if (!load_ref_blocks(I, pf, r, pre, false))
         return false;
     long so[4] = {3, r->cin, 1, 1}, sob[1] = {3};
     long se[4] = {r->emb, 2, 1, 1}, seb[1] = {r->emb};
-    r->out_w = load_dev(I, pf, pre + ".out_conv.weight", 4, so, I->wt);
+    {
+        HostT ow;
+        if (!read_host(pf, (pre + ".out_conv.weight").c_str(), 4, so, ow))
+            return false;
+        std::vector<float> p = pad_matrix(ow.v, 3, r->cin, 3, r->cinp);
+        r->out_w = upload(I, p.data(), p.size(), I->wt, "out_conv");
+    }
     r->out_b = (float *)load_dev(I, pf, pre + ".out_conv.bias", 1, sob, DT_F32);
     r->emb_w = (float *)load_dev(I, pf, pre + ".disp_emb.weight", 4, se, DT_F32);
     r->emb_b = (float *)load_dev(I, pf, pre + ".disp_emb.bias", 1, seb, DT_F32);
@@ -390,6 +423,7 @@ bool load_refiner2(roma_impl *I, struct pth_file *pf, int j)
     r->radius = ref2_radius[j];
     const int corr = r->radius ? (2 * r->radius + 1) * (2 * r->radius + 1) : 0;
     r->cin = 2 * r->feat + r->emb + corr;
+    r->cinp = pad16(r->cin);
     r->nout = 6;
     const std::string pre = fmt("refiners.%d", r->scale);
     long sp[2] = {ref2_feat[j], ref2_in[j]}, spb[1] = {ref2_feat[j]};
@@ -415,6 +449,7 @@ bool load_refiner2(roma_impl *I, struct pth_file *pf, int j)
         bias[k] = wb.v[k];
     for (int k = 0; k < 4; k++)
         bias[2 + k] = cb.v[k];
+    w = pad_matrix(w.data(), 6, r->cin, 6, r->cinp);
     r->out_w = upload(I, w.data(), w.size(), I->wt, "heads");
     r->out_b = upload_f(I, bias.data(), 6, "heads");
     return !pending();
@@ -772,14 +807,14 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
         for (int s = p; s < ROMA_SCALES; s++) {
             const int ph = p ? H : I->Cs, pw = p ? W : I->Cs;
             const size_t n = (size_t)side(I, ph, s) * side(I, pw, s);
-            dmax = std::max(dmax, (size_t)I->ref[s].cin * n);
+            dmax = std::max(dmax, (size_t)I->ref[s].cinp * n);
         }
     if (m->v2)
         for (int p = 0; p < 2; p++)
             for (int s = 0; s < ROMA2_SCALES; s++) {
                 const int ph = p ? H : I->Cs, pw = p ? W : I->Cs;
                 const size_t n = (size_t)(ph / ref2_scale[s]) * (pw / ref2_scale[s]);
-                dmax = std::max(dmax, (size_t)I->ref2[s].cin * n);
+                dmax = std::max(dmax, (size_t)I->ref2[s].cinp * n);
             }
     I->d_a = dmalloc(I, dmax * as, "refiner");
     I->d_b = dmalloc(I, dmax * as, "refiner");
@@ -1146,31 +1181,36 @@ void refiner_body(Ctx &c, const Refiner &r, const void *fa, const void *fb,
     const DType at = I->at;
     {
         Prof p(c.m->ocl, "refiner_input");
-        copy2d(c.st, fa, tf, r.feat, I->d_a, at, r.cin, n, r.feat);
+        if (r.cinp != r.cin) {
+            const size_t es = dsize(at);
+            cudaMemset2DAsync((char *)I->d_a + r.cin * es, r.cinp * es, 0,
+                              (r.cinp - r.cin) * es, n, c.st);
+        }
+        copy2d(c.st, fa, tf, r.feat, I->d_a, at, r.cinp, n, r.feat);
         roma_warp_sample_l(c.st, {fb, 1, r.feat, tf}, r.feat, hs, ws, flow,
-                           {I->d_a, 1, r.cin, at}, r.feat);
+                           {I->d_a, 1, r.cinp, at}, r.feat);
         roma_disp_emb_l(c.st, flow, hs, ws, dfx, dfy, r.emb_w, r.emb_b, r.emb,
-                        {I->d_a, 1, r.cin, at}, 2 * r.feat);
+                        {I->d_a, 1, r.cinp, at}, 2 * r.feat);
         launch_ok("refiner_input");
     }
     if (r.radius) {
         Prof p(c.m->ocl, "roma_local_corr");
         roma_local_corr_l(c.st, {fa, 1, r.feat, tf}, {fb, 1, r.feat, tf}, r.feat, hs,
-                          ws, r.radius, flow, {I->d_a, 1, r.cin, at},
+                          ws, r.radius, flow, {I->d_a, 1, r.cinp, at},
                           2 * r.feat + r.emb);
         launch_ok("roma_local_corr");
     }
     for (int b = 0; b <= ROMA_HIDDEN; b++) {
         {
             Prof p(c.m->ocl, "roma_dwconv5");
-            roma_dwconv5_l(c.st, {I->d_a, 1, r.cin, at}, r.cin, hs, ws, r.dw_w[b],
-                           r.dw_b[b], {I->d_b, 1, r.cin, at});
+            roma_dwconv5_l(c.st, {I->d_a, 1, r.cinp, at}, r.cinp, hs, ws, r.dw_w[b],
+                           r.dw_b[b], {I->d_b, 1, r.cinp, at});
             launch_ok("roma_dwconv5");
         }
-        gemm_nt(c, "refiner_pw", (int)n, r.cin, r.cin, I->d_b, r.cin, at, r.pw_w[b],
-                r.pw_b[b], I->d_a, r.cin, at, ACTF_NONE, false);
+        gemm_nt(c, "refiner_pw", (int)n, r.cinp, r.cinp, I->d_b, r.cinp, at, r.pw_w[b],
+                r.pw_b[b], I->d_a, r.cinp, at, ACTF_NONE, false);
     }
-    gemm_nt(c, "refiner_out", (int)n, r.nout, r.cin, I->d_a, r.cin, at, r.out_w,
+    gemm_nt(c, "refiner_out", (int)n, r.nout, r.cinp, I->d_a, r.cinp, at, r.out_w,
             r.out_b, I->d_c, r.nout, DT_F32, ACTF_NONE, false);
 }
 

@@ -24,6 +24,7 @@
 
 #include <cuda.h>
 #include <mutex>
+#include <string.h>
 
 #include "gemm.cuh"
 
@@ -96,6 +97,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
                  : "memory");
 }
 
+// 3-D box (innermost coordinate x first); coordinates outside the tensor
+// (negative ones included) read zeros.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int x, int y, int z)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
+                 "l"((uint64_t)map), "r"(su32(bar)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 // Shared-memory matrix descriptor of a K-major tile with 128-byte
 // swizzling: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO);
 // version 1 (tcgen05), layout type 2 (SWIZZLE_128B).
@@ -163,6 +175,10 @@ struct TcParams {
     int act;
     float slope;
     int c_bf16;
+    // Convolution mode (3 x 3, stride 1, padding 1, channels-last input of
+    // cH x cW x cC, cC a multiple of 64): the tile is TW x TH output pixels
+    // (TW TH = 128), k-block kb = (tap, 64-channel chunk).
+    int conv, cH, cW, cC, TW, TH, tiles_x;
 };
 
 template <int BN, int STAGES>
@@ -185,6 +201,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int nk = (p.K + BK - 1) / BK;
+    // Convolution tile origin (pixels x0 .., rows y0 ..).
+    const int cx0 = p.conv ? (blockIdx.y % p.tiles_x) * p.TW : 0;
+    const int cy0 = p.conv ? (blockIdx.y / p.tiles_x) * p.TH : 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
@@ -214,7 +233,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     !mbar_wait(&s.empty[st], ((kb / STAGES) - 1) & 1, 1))
                     break;
                 mbar_expect_tx(&s.full[st], bytes);
-                tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, m0);
+                if (p.conv) {
+                    const int chunks = p.cC / BK, tap = kb / chunks;
+                    const int c0 = (kb % chunks) * BK;
+                    tma_load_3d(s.a[st], &tma_a, &s.full[st], c0, cx0 + tap % 3 - 1,
+                                cy0 + tap / 3 - 1);
+                }
+                else
+                    tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, m0);
                 tma_load_2d(s.b[st], &tma_b, &s.full[st], kb * BK, n0);
             }
         }
@@ -244,7 +270,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     else {
         // Epilogue: warp w owns TMEM lanes (rows) 32 (w % 4) ...
         const int q = warp % 4;
-        const int row = m0 + 32 * q + lane;
+        const int r = 32 * q + lane;
+        int row = m0 + r;
+        if (p.conv) {
+            const int px = cx0 + r % p.TW, py = cy0 + r / p.TW;
+            row = px < p.cW && py < p.cH ? py * p.cW + px : p.M;
+        }
         if (mbar_wait(&s.done, 0, 3)) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -331,14 +362,64 @@ bool make_map(CUtensorMap *map, const void *base, long rows, long cols, long ld,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D bfloat16 tensor map of a channels-last (H, W, C) image, box of TH
+// rows x TW pixels x 64 channels, 128-byte swizzle, zero fill outside.
+bool make_map_conv(CUtensorMap *map, const void *base, int H, int W, int C, int TW,
+                   int TH)
+{
+    EncodeTiled enc = encoder();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H};
+    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)TW, (cuuint32_t)TH};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tile width (pixels) of the convolution mode with the fewest wasted
+// output positions for an H x W map.
+int conv_tile_width(int H, int W)
+{
+    int best = 128;
+    long best_w = -1;
+    for (int tw = 128; tw >= 8; tw /= 2) {
+        const int th = BM / tw;
+        const long cells = (long)cdiv(W, tw) * tw * cdiv(H, th) * th;
+        if (best_w < 0 || cells < best_w) {
+            best_w = cells;
+            best = tw;
+        }
+    }
+    return best;
+}
+
 template <int BN, int STAGES>
 bool launch_tc(cudaStream_t st, const GemmArgs &g)
 {
     CUtensorMap ma, mb;
-    if (!make_map(&ma, g.A, g.M, g.K, g.lda, BM) ||
-        !make_map(&mb, g.B, g.N, g.K, g.ldb, BN))
-        return false;
     TcParams p;
+    memset(&p, 0, sizeof(p));
+    int grid_y = cdiv(g.M, BM);
+    if (g.amode == 1) {
+        p.conv = 1;
+        p.cH = g.cH;
+        p.cW = g.cW;
+        p.cC = g.cC;
+        p.TW = conv_tile_width(g.cH, g.cW);
+        p.TH = BM / p.TW;
+        p.tiles_x = cdiv(g.cW, p.TW);
+        grid_y = p.tiles_x * cdiv(g.cH, p.TH);
+        if (!make_map_conv(&ma, g.A, g.cH, g.cW, g.cC, p.TW, p.TH))
+            return false;
+    }
+    else if (!make_map(&ma, g.A, g.M, g.K, g.lda, BM))
+        return false;
+    if (!make_map(&mb, g.B, g.N, g.K, g.ldb, BN))
+        return false;
     p.M = g.M;
     p.N = g.N;
     p.K = g.K;
@@ -364,7 +445,7 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g)
         }
         attr_done |= 1u << (dev & 31);
     }
-    dim3 grid(cdiv(g.N, BN), cdiv(g.M, BM));
+    dim3 grid(cdiv(g.N, BN), grid_y);
     tc_gemm_kernel<BN, STAGES><<<grid, NTHREADS, smem, st>>>(ma, mb, p);
     return true;
 }
@@ -374,13 +455,16 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g)
 bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
     (void)sm_count;
-    if (g.ab != DT_BF16 || !g.transb || g.nb != 1 || g.amode != 0)
+    if (g.ab != DT_BF16 || !g.transb || g.nb != 1)
+        return false;
+    if (g.amode == 2 || (g.amode == 1 && (g.cC % BK || g.K != 9 * g.cC)))
         return false;
     if (g.biasrow && g.bias)
         return false;
     if (g.M < 64 || g.N < 64 || g.K < 16)
         return false;
-    if (((uintptr_t)g.A & 15) || ((uintptr_t)g.B & 15) || (g.lda & 7) || (g.ldb & 7))
+    if (((uintptr_t)g.A & 15) || ((uintptr_t)g.B & 15) ||
+        (g.amode == 0 && (g.lda & 7)) || (g.ldb & 7))
         return false;
     if (g.N >= 256)
         return launch_tc<256, 4>(st, g);

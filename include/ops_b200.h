@@ -1,0 +1,38 @@
+/* SPDX-License-Identifier: Unlicense */
+
+/* Operations of the B200 build without a counterpart in the reference's
+ * ops.h: the channels-last ("token-major") 3 x 3 convolution the models
+ * run (the reference's VGG convolutions, roma.c:742-768 and 1000-1027,
+ * go through ops_conv2d on channel-major maps; this build keeps feature
+ * maps channels-last so that every convolution is an implicit GEMM with
+ * K-major operands), and the tensor-core status of the library. */
+
+#ifndef I_COREGISTRATION_B200_OPS_B200_H
+#define I_COREGISTRATION_B200_OPS_B200_H
+
+#include "ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* 3 x 3 convolution, stride 1, zero padding 1, of a channels-last
+ * (H, W, C) float32 map into (H, W, K): weights in the PyTorch layout
+ * (K, C, 3, 3), bias per output channel (may be NULL), activation after
+ * the bias. With o->precision OPS_BF16 and C a multiple of 64 it runs
+ * as an implicit GEMM on tcgen05 tensor cores (the input and weights
+ * rounded to bfloat16, 3-D TMA boxes of the map per tap, no im2col
+ * buffer); otherwise in float32. */
+void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem w,
+                    cl_mem b, int K, int act, float slope, cl_mem out);
+
+/* Non-zero when a bounded wait of a tensor-core kernel ran out since the
+ * last call (the kernel then stopped and its results are invalid); the
+ * code is cleared. */
+int coreg_tc_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* I_COREGISTRATION_B200_OPS_B200_H */

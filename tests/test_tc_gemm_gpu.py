@@ -67,3 +67,40 @@ def test_tc_gemm_matches_rounded_oracle(dev16, shape):
     want32 = ref_gemm(a, b, 1, M, N, K, bias=bias, R=r if residual else None, alpha=0.75, a=act,
                       slope=0.1)[0]
     assert np.linalg.norm(got - want32) / np.linalg.norm(want32) <= 2e-2
+
+
+CONVS = [
+    # H, W, C, K (the VGG shapes at reduced size, ragged tiles)
+    (40, 40, 64, 64),
+    (35, 70, 128, 256),
+    (72, 136, 64, 128),
+    (17, 9, 256, 64),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", CONVS, ids=[f"{s[0]}x{s[1]}x{s[2]}to{s[3]}" for s in CONVS])
+@pytest.mark.parametrize("prec", [coreg.OPS_FP32, coreg.OPS_BF16], ids=["fp32", "bf16"])
+def test_conv3x3_channels_last(shape, prec):
+    """ops_conv3x3_cl (implicit GEMM; tensor cores with 3-D TMA boxes in
+    bfloat16 mode) against the oracle convolution (ops.cl conv2d
+    semantics) on the same channels-last data."""
+    from oracle.ops_ref import conv2d
+
+    H, W, C_, K = shape
+    dev = coreg.Device(0, precision=prec)
+    rng = np.random.default_rng(H * W + C_)
+    x = rng.standard_normal((H, W, C_), dtype=np.float32)
+    w = (rng.standard_normal((K, C_, 3, 3), dtype=np.float32) / np.sqrt(9 * C_)).astype(np.float32)
+    b = rng.standard_normal(K, dtype=np.float32)
+    X, Wt, B, Y = dev.upload(x), dev.upload(w), dev.upload(b), dev.zeros(H * W * K)
+    dev.lib.ops_conv3x3_cl(dev.ops_p, X.handle, H, W, C_, Wt.handle, B.handle, K, 2, 0.0, Y.handle)
+    got = Y.read(count=H * W * K).reshape(H, W, K)
+    coreg.check(dev.lib)
+    assert dev.lib.coreg_tc_status() == 0
+    xr, wr = (bf16_round(x), bf16_round(w)) if prec == coreg.OPS_BF16 else (x, w)
+    want = conv2d(xr.transpose(2, 0, 1), C_, H, W, wr, b, K, 3, 3, 1, 1, 1, 1, a=2)
+    want = want.transpose(1, 2, 0)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err
+    dev.close()
