@@ -128,6 +128,7 @@ SIGNATURES = {
     "ops_fold_bn": (None, [P, P, I, L, P, P, P, P, F]),
     "coreg_tc_status": (I, []),
     "ops_conv3x3_cl": (None, [C.POINTER(Ops), P, I, I, I, P, P, I, I, F, P]),
+    "ops_attention_qkv": (None, [C.POINTER(Ops), P, I, I, I, F, P]),
 }
 
 _lib = None

@@ -84,6 +84,11 @@ void resize_planes(cudaStream_t st, const float *in, int C, int h, int w,
                    float *out, int H, int W, int coff, int align, float scale);
 void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
                    int C);
+// Fused attention of a token-major qkv buffer (N x 3 Dm, bfloat16) into
+// out (N rows of ldo, bfloat16) on tcgen05 tensor cores (tc_attention.cu);
+// false when the head size (64 or 128) or alignment is not supported.
+bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
+                  long ldo, float scale);
 // Double-precision GP solve (gp_chol.cu).
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
                   double noise, float *X, double *work, int *flag);

@@ -407,6 +407,53 @@ extern "C" void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C,
     gemm_run(o->ocl, g, tc ? "conv3x3_tc" : "conv3x3");
 }
 
+template <typename T>
+__global__ void from_type_k(const T *in, long n, float *out)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < n)
+        out[e] = ldf(in + e);
+}
+
+extern "C" void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm,
+                                  int heads, float scale, cl_mem out)
+{
+    if (pending() || !need(qkv, "ops_attention_qkv qkv") || !need(out, "out"))
+        return;
+    if (N <= 0 || heads <= 0 || Dm % heads || Dm / heads > OPS_MAX_HEAD_DIM) {
+        fail("ops_attention_qkv: %d tokens, %d channels, %d heads", N, Dm, heads);
+        return;
+    }
+    const int d = Dm / heads;
+    const long nin = (long)N * 3 * Dm, nout = (long)N * Dm;
+    cudaStream_t st = stream_of(o->ocl);
+    if (o->precision == OPS_BF16 && (d == 64 || d == 128) && Dm % 64 == 0) {
+        const size_t bytes = (size_t)(nin + nout) * 2 + 256;
+        if (bytes > o->scratch16_bytes) {
+            ocl_release(&o->scratch16);
+            o->scratch16 = ocl_alloc(o->ocl, bytes, "attention operands");
+            o->scratch16_bytes = bytes;
+            if (pending())
+                return;
+        }
+        __nv_bfloat16 *q16 = (__nv_bfloat16 *)o->scratch16->ptr;
+        __nv_bfloat16 *o16 = q16 + (nin + 127) / 128 * 128;
+        Prof p(o->ocl, "attention_tc");
+        to_type_k<__nv_bfloat16><<<cdiv(nin, 256), 256, 0, st>>>(fptr(qkv), nin, q16);
+        if (!attention_tc(st, q16, N, Dm, heads, o16, Dm, scale)) {
+            fail("ops_attention_qkv: tensor-core attention refused the operands");
+            return;
+        }
+        from_type_k<__nv_bfloat16><<<cdiv(nout, 256), 256, 0, st>>>(o16, nout, fptr(out));
+        launch_ok("attention_tc");
+        return;
+    }
+    Prof p(o->ocl, "attention");
+    attention_l(st, fptr(qkv), 3L * Dm, fptr(qkv) + Dm, 3L * Dm, fptr(qkv) + 2 * Dm,
+                3L * Dm, fptr(out), Dm, N, N, heads, d, scale, nullptr, DT_F32);
+    launch_ok("attention");
+}
+
 extern "C" void ops_unfold(struct ops *o, cl_mem in, int C, int H, int W,
                            const struct conv_geom *g, cl_mem out)
 {

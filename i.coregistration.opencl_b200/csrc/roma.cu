@@ -1038,9 +1038,11 @@ void block(Ctx &c, const Block &b, int N, int D, int heads, float eps)
         const int hd = D / heads;
         const size_t es = dsize(at);
         Prof p(c.m->ocl, "attention");
-        attention_l(c.st, I->t_qkv, 3 * D, (const char *)I->t_qkv + D * es, 3 * D,
-                    (const char *)I->t_qkv + 2 * D * es, 3 * D, I->t_o, D, N, N,
-                    heads, hd, 1.0f / sqrtf((float)hd), nullptr, at);
+        if (at != DT_BF16 || !attention_tc(c.st, I->t_qkv, N, D, heads, I->t_o, D,
+                                           1.0f / sqrtf((float)hd)))
+            attention_l(c.st, I->t_qkv, 3 * D, (const char *)I->t_qkv + D * es, 3 * D,
+                        (const char *)I->t_qkv + 2 * D * es, 3 * D, I->t_o, D, N, N,
+                        heads, hd, 1.0f / sqrtf((float)hd), nullptr, at);
         launch_ok("attention");
     }
     gemm_nt(c, "proj", N, D, D, I->t_o, D, at, b.proj_w, b.proj_b, I->t_x, D,

@@ -26,6 +26,18 @@ extern "C" {
 void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem w,
                     cl_mem b, int K, int act, float slope, cl_mem out);
 
+/* Multi-head attention of a fused token-major qkv buffer (N rows of 3 Dm
+ * float32: queries, keys, values; head h at columns h (Dm / heads) of
+ * each) into out (N x Dm): O = softmax(scale Q K^T) V per head, the
+ * transformer attention of the models (the reference computes it with
+ * two ops_gemm and ops_softmax_rows, roma.c:675-694). With o->precision
+ * OPS_BF16 and a head size of 64 or 128 it runs the fused tcgen05 kernel
+ * (bfloat16 operands, the probabilities rounded to bfloat16, float32
+ * accumulation, no score matrix); otherwise the float32 kernel of
+ * ops_attention. */
+void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm, int heads,
+                       float scale, cl_mem out);
+
 /* Non-zero when a bounded wait of a tensor-core kernel ran out since the
  * last call (the kernel then stopped and its results are invalid); the
  * code is cleared. */
