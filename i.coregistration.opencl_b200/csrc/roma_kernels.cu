@@ -481,10 +481,82 @@ __global__ void dwconv5_k(const TI *in, long cs, long ps, int C, int H, int W,
     stf(out + (long)c * ocs + i * ops, fmaxf(acc, 0.0f));
 }
 
+// The same on token-major maps (channel stride 1, cell stride ps / ops):
+// a 16 x 16 cell x 32 channel tile per block, its 20 x 20 input halo in
+// shared memory; lane = channel, each thread two rows of 16 outputs with
+// a sliding 5 x 5 window in registers (5 shared-memory reads per output
+// instead of 25).
+#define DW_T 16
+template <typename TI, typename TO, int DW_C>
+__global__ void __launch_bounds__(256)
+dwconv5_tm_k(const TI *in, long ps, int C, int H, int W, const float *wt,
+             const float *bias, TO *out, long ops)
+{
+    __shared__ TI tile[DW_T + 4][DW_T + 4][DW_C];
+    const int tid = threadIdx.x, c0 = blockIdx.z * DW_C;
+    const int x0 = blockIdx.x * DW_T - 2, y0 = blockIdx.y * DW_T - 2;
+    for (int e = tid; e < (DW_T + 4) * (DW_T + 4) * DW_C; e += 256) {
+        const int c = e % DW_C, px = (e / DW_C) % (DW_T + 4), py = e / (DW_C * (DW_T + 4));
+        const int x = x0 + px, y = y0 + py;
+        TI v = TI(0.0f);
+        if (x >= 0 && x < W && y >= 0 && y < H && c0 + c < C)
+            v = in[((long)y * W + x) * ps + c0 + c];
+        tile[py][px][c] = v;
+    }
+    __syncthreads();
+    const int c = tid % DW_C, cg = c0 + c;
+    if (cg >= C)
+        return;
+    float w[25];
+#pragma unroll
+    for (int i = 0; i < 25; i++)
+        w[i] = wt[cg * 25 + i];
+    const float b = bias[cg];
+    for (int oy = tid / DW_C; oy < DW_T; oy += 256 / DW_C) {
+        const int y = blockIdx.y * DW_T + oy;
+        if (y >= H)
+            break;
+        float win[5][5];
+#pragma unroll
+        for (int a = 0; a < 5; a++)
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                win[a][k + 1] = ldf(&tile[oy + a][k][c]);
+        for (int ox = 0; ox < DW_T; ox++) {
+#pragma unroll
+            for (int a = 0; a < 5; a++) {
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    win[a][k] = win[a][k + 1];
+                win[a][4] = ldf(&tile[oy + a][ox + 4][c]);
+            }
+            const int x = blockIdx.x * DW_T + ox;
+            if (x >= W)
+                break;
+            float acc = b;
+#pragma unroll
+            for (int a = 0; a < 5; a++)
+#pragma unroll
+                for (int k = 0; k < 5; k++)
+                    acc = fmaf(win[a][k], w[a * 5 + k], acc);
+            stf(out + ((long)y * W + x) * ops + cg, fmaxf(acc, 0.0f));
+        }
+    }
+}
+
 template <typename TI, typename TO>
 static void dwconv5_t(cudaStream_t st, Map in, int C, int H, int W,
                       const float *w, const float *b, MapOut out)
 {
+    if (in.cs == 1 && out.cs == 1) {
+        // 32 channels per block for 2-byte inputs, 16 for float (the
+        // halo tile stays within 48 KB of shared memory).
+        constexpr int CB = sizeof(TI) == 2 ? 32 : 16;
+        dim3 grid(cdiv(W, DW_T), cdiv(H, DW_T), cdiv(C, CB));
+        dwconv5_tm_k<TI, TO, CB><<<grid, 256, 0, st>>>((const TI *)in.p, in.ps, C, H, W, w,
+                                                       b, (TO *)out.p, out.ps);
+        return;
+    }
     const long tot = (long)H * W * C;
     dwconv5_k<TI, TO><<<cdiv(tot, 256), 256, 0, st>>>(
         (const TI *)in.p, in.cs, in.ps, C, H, W, w, b, (TO *)out.p, out.cs,

@@ -81,6 +81,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int code
     return true;
 }
 
+// The same for waiters that are not on the critical path (epilogue warps
+// waiting for the whole main loop): back off between tries so that they
+// leave the issue slots and the barrier unit to the producer and MMA warps.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *b, uint32_t parity, int code)
+{
+    if (mbar_try(b, parity))
+        return true;
+    const uint64_t t0 = gtime();
+    while (!mbar_try(b, parity)) {
+        __nanosleep(256);
+        if (gtime() - t0 > 2000000000ull) {
+            atomicCAS(&g_error, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
                                             uint64_t *bar, int x, int y)
 {
@@ -99,6 +117,51 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,
                  " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
                  "l"((uint64_t)map), "r"(su32(bar)), "r"(x), "r"(y), "r"(z)
                  : "memory");
+}
+
+// TMA stores from shared memory (elements outside the tensor are not
+// written), their bulk groups, and a named barrier of the epilogue warps.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x,
+                                             int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     (uint64_t)map),
+                 "r"(su32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x,
+                                             int y, int z)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            (uint64_t)map),
+        "r"(su32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit()
+{
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until every bulk group of this thread has completed (its global
+// writes done).
+__device__ __forceinline__ void bulk_wait_all()
+{
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
@@ -226,6 +289,12 @@ bool make_map_2d(CUtensorMap *map, const void *base, long rows, long cols, long 
 // TH x TW x 64.
 bool make_map_conv(CUtensorMap *map, const void *base, int H, int W, int C, int TW,
                    int TH);
+// Host: tensor map of the output of a GEMM for TMA stores: 2-D rows x cols
+// (ld elements) or, with conv set, 3-D channels-last (H, W, cols); element
+// size es (4 float, 2 bfloat16), box of 128 bytes of columns x box_rows
+// (2-D) or TW x TH pixels (3-D), 128-byte swizzle.
+bool make_map_out(CUtensorMap *map, void *base, int es, long rows, long cols, long ld,
+                  int conv, int H, int W, int TW, int TH);
 // Host: opt in to `bytes` of dynamic shared memory for kernel `fn` on the
 // current device (once per device).
 bool smem_opt_in(const void *fn, size_t bytes, unsigned *done_mask);

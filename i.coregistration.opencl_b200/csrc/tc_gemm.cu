@@ -17,9 +17,13 @@
 //               4 tcgen05.mma (K = 16 each) per stage into a 128 x BN
 //               float32 accumulator in TMEM and commits each stage to
 //               empty[s] (the producer's refill signal), the last to done;
-//   warps 2..5  epilogue: wait on done, tcgen05.ld 32 columns at a time
-//               (warp w reads TMEM lanes 32 (w % 4) ..), bias, activation,
-//               residual, store.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant (alternate
+//               32-column chunks): each reads its 32 lanes (rows) with
+//               tcgen05.ld, transposes them through a padded shared-memory
+//               block and writes every row with one coalesced warp store
+//               (lane = column), bias, activation and residual applied on
+//               the way. Stores of one row per thread would make 32
+//               separate memory requests per instruction.
 // Every mbarrier wait is bounded (about two seconds); a wait that runs out
 // records an error code (coreg_tc_status) and the CTA leaves its loops,
 // frees its tensor memory and returns.
@@ -35,7 +39,8 @@ namespace tc {
 namespace {
 
 constexpr int BM = 128, BK = 64;
-constexpr int NTHREADS = 192;
+// Producer warp, MMA warp, eight epilogue warps.
+constexpr int NTHREADS = 320;
 
 struct TcParams {
     int M, N, K;
@@ -61,12 +66,20 @@ struct Smem {
     uint32_t tmem;
 };
 
-template <int BN, int STAGES>
+// The activation (ACT, or -1 for the run-time one of p.act) and the output
+// type are template parameters: a run-time switch would inline every
+// activation's math into the unrolled epilogue loop, and that code size
+// slows the epilogue down by several times.
+template <int BN, int STAGES, int ACT, typename TC>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                const __grid_constant__ CUtensorMap tma_b, TcParams p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // Epilogue transposes, per epilogue warp 32 rows x 32 columns: a
+    // statically declared shared array, so that its accesses compile to
+    // shared-memory instructions.
+    __shared__ float stage_all[NTHREADS / 32 - 2][32][33];
     Smem<BN, STAGES> &s = *reinterpret_cast<Smem<BN, STAGES> *>(
         (void *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -117,9 +130,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             constexpr uint32_t idesc = idesc_bf16(BM, BN);
             for (int kb = 0; kb < nk; kb++) {
                 const int st = kb % STAGES;
+                // TMA completion through the mbarrier orders the tile for
+                // the tensor cores; no tcgen05 fence is needed here.
                 if (!mbar_wait(&s.full[st], (kb / STAGES) & 1, 2))
                     break;
-                fence_after();
                 const uint64_t da = sw128_desc(su32(s.a[st]));
                 const uint64_t db = sw128_desc(su32(s.b[st]));
 #pragma unroll
@@ -132,45 +146,47 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         }
     }
     else {
-        // Epilogue: warp w owns TMEM lanes (rows) 32 (w % 4) ...
-        const int q = warp % 4;
+        // Epilogue: warp w owns TMEM lanes (rows) 32 (w % 4) ..., and of
+        // their columns the 32-column chunks of parity (w - 2) / 4: two
+        // warps per lane quadrant, so that each scheduler interleaves two
+        // epilogue warps.
+        const int q = warp % 4, half = (warp - 2) / 4;
         const int r = 32 * q + lane;
         int row = m0 + r;
         if (p.conv) {
             const int px = cx0 + r % p.TW, py = cy0 + r / p.TW;
             row = px < p.cW && py < p.cH ? py * p.cW + px : p.M;
         }
+        float(*stage)[33] = stage_all[warp - 2];
         // Decided per warp: the TMEM loads below are warp-collective.
-        if (__all_sync(0xffffffffu, mbar_wait(&s.done, 0, 3))) {
+        if (__all_sync(0xffffffffu, mbar_wait_backoff(&s.done, 0, 3))) {
             fence_after();
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 32 * half; c0 < BN && n0 + c0 < p.N; c0 += 64) {
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
-                if (row >= p.M)
-                    continue;
-                const long base = (long)row * p.ldc;
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int col = n0 + c0 + j;
-                    if (col >= p.N)
-                        break;
-                    float x = p.alpha * v[j];
-                    if (p.bias)
-                        x += p.bias[col];
-                    x = apply_act(x, p.act, p.slope);
-                    if (p.c_bf16) {
-                        __nv_bfloat16 *C = (__nv_bfloat16 *)p.C + base + col;
-                        if (p.R)
-                            x += __bfloat162float(((const __nv_bfloat16 *)p.R)[base + col]);
-                        *C = __float2bfloat16_rn(x);
-                    }
-                    else {
-                        float *C = (float *)p.C + base + col;
-                        if (p.R)
-                            x += ((const float *)p.R)[base + col];
-                        *C = x;
+                for (int j = 0; j < 32; j++)
+                    stage[lane][j] = v[j];
+                __syncwarp();
+                // Lane = column from here on.
+                const int col = n0 + c0 + lane;
+                const bool cok = col < p.N;
+                const float bias = cok && p.bias ? p.bias[col] : 0.0f;
+                TC *C = (TC *)p.C;
+                const TC *R = (const TC *)p.R;
+#pragma unroll 4
+                for (int rr = 0; rr < 32; rr++) {
+                    const int grow = __shfl_sync(0xffffffffu, row, rr);
+                    if (grow < p.M && cok) {
+                        const long idx = (long)grow * p.ldc + col;
+                        float x = p.alpha * stage[rr][lane] + bias;
+                        x = apply_act(x, ACT >= 0 ? ACT : p.act, p.slope);
+                        if (R)
+                            x += ldf(R + idx);
+                        stf(C + idx, x);
                     }
                 }
+                __syncwarp();
             }
         }
     }
@@ -197,6 +213,18 @@ int conv_tile_width(int H, int W)
         }
     }
     return best;
+}
+
+template <int BN, int STAGES, int ACT, typename TC>
+bool run_tc(cudaStream_t st, dim3 grid, const CUtensorMap &ma, const CUtensorMap &mb,
+            const TcParams &p)
+{
+    const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
+    static unsigned done = 0;
+    if (!smem_opt_in((const void *)tc_gemm_kernel<BN, STAGES, ACT, TC>, smem, &done))
+        return false;
+    tc_gemm_kernel<BN, STAGES, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, p);
+    return true;
 }
 
 template <int BN, int STAGES>
@@ -233,13 +261,19 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g)
     p.act = g.act;
     p.slope = g.slope;
     p.c_bf16 = g.c == DT_BF16;
-    const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
-    static unsigned done = 0;
-    if (!smem_opt_in((const void *)tc_gemm_kernel<BN, STAGES>, smem, &done))
-        return false;
     dim3 grid(cdiv(g.N, BN), grid_y);
-    tc_gemm_kernel<BN, STAGES><<<grid, NTHREADS, smem, st>>>(ma, mb, p);
-    return true;
+    if (p.c_bf16) {
+        if (g.act == ACTF_NONE)
+            return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, p);
+        if (g.act == ACTF_GELU)
+            return run_tc<BN, STAGES, ACTF_GELU, __nv_bfloat16>(st, grid, ma, mb, p);
+        if (g.act == ACTF_RELU)
+            return run_tc<BN, STAGES, ACTF_RELU, __nv_bfloat16>(st, grid, ma, mb, p);
+        return run_tc<BN, STAGES, -1, __nv_bfloat16>(st, grid, ma, mb, p);
+    }
+    if (g.act == ACTF_NONE)
+        return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, p);
+    return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, p);
 }
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
