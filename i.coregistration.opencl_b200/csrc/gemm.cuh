@@ -89,7 +89,8 @@ void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
 // false when the head size (64 or 128) or alignment is not supported.
 bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
                   long ldo, float scale);
-// Double-precision GP solve (gp_chol.cu).
+// Double-precision GP solve (gp_chol.cu); work holds gp_work_doubles(n, d).
+size_t gp_work_doubles(int n, int d);
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
                   double noise, float *X, double *work, int *flag);
 

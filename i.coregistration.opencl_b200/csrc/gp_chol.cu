@@ -7,11 +7,15 @@
 // gp_solve (roma.c:772-836: Cholesky in double, L Z = F then L^T X = Z),
 // whose device round trip (roma.c:885-888) disappears.
 //
-// Blocks of NB = 64: the diagonal block is factored (or solved) by one
-// thread block in shared memory, the panels and trailing updates are
-// double-precision GEMMs. A non-positive pivot sets *flag (the reference
-// stops with "kernel not positive definite"); the host reads it after
-// the tile.
+// Blocks of NB = 64. One CTA factors each diagonal block in shared memory
+// and also inverts it (Linv); with the inverses every other step is a
+// double-precision GEMM:
+//   panel      L21 = A21 Linv^T
+//   trailing   A22 -= L21 L21^T (lower triangle)
+//   forward    Z_j = Linv_j F'_j, then F'_below -= L_below,j Z_j
+//   backward   X_j = Linv_j^T Z'_j, then Z'_above -= L_j,above^T X_j
+// A non-positive pivot sets *flag (the reference stops with "kernel not
+// positive definite"); the host reads it after the tile.
 
 #include "common.cuh"
 
@@ -29,77 +33,73 @@ __global__ void gp_init_k(const float *K, int n, double noise, double *A)
     A[e] = (double)K[e] + (i == j ? noise : 0.0);
 }
 
-// Factor the b x b diagonal block at (j0, j0) in place: column by column
-// (left-looking within the block, as the reference's loop).
+// Factor the b x b diagonal block at (j0, j0) in place (right-looking
+// within the block) and write its inverse into Linv (GP_NB x GP_NB, zero
+// padded beyond b).
 __global__ void __launch_bounds__(256)
-gp_potrf_k(double *A, int n, int j0, int b, int *flag)
+gp_potrf_inv_k(double *A, int n, int j0, int b, double *Linv, int *flag)
 {
-    __shared__ double L[GP_NB][GP_NB + 1];
+    // Dynamic shared memory: the factor and its inverse (2 x 64 x 65
+    // doubles, above the static 48 KB).
+    extern __shared__ double gp_smem[];
+    double(*L)[GP_NB + 1] = reinterpret_cast<double(*)[GP_NB + 1]>(gp_smem);
+    double(*X)[GP_NB + 1] = reinterpret_cast<double(*)[GP_NB + 1]>(gp_smem + GP_NB * (GP_NB + 1));
     const int t = threadIdx.x;
-    for (int e = t; e < b * b; e += blockDim.x) {
-        const int i = e / b, j = e % b;
-        L[i][j] = A[(long)(j0 + i) * n + j0 + j];
+    for (int e = t; e < GP_NB * GP_NB; e += blockDim.x) {
+        const int i = e / GP_NB, j = e % GP_NB;
+        L[i][j] = i < b && j < b ? A[(long)(j0 + i) * n + j0 + j] : (i == j ? 1.0 : 0.0);
     }
     __syncthreads();
-    for (int j = 0; j < b; j++) {
-        __shared__ double diag;
-        if (t == 0) {
-            double s = L[j][j];
-            for (int k = 0; k < j; k++)
-                s -= L[j][k] * L[j][k];
-            if (!(s > 0)) {
-                *flag = 1;
-                s = 1.0;
-            }
-            diag = sqrt(s);
-            L[j][j] = diag;
-        }
-        __syncthreads();
-        for (int i = j + 1 + t; i < b; i += blockDim.x) {
-            double s = L[i][j];
-            for (int k = 0; k < j; k++)
-                s -= L[i][k] * L[j][k];
-            L[i][j] = s / diag;
-        }
-        __syncthreads();
-    }
-    for (int e = t; e < b * b; e += blockDim.x) {
-        const int i = e / b, j = e % b;
-        A[(long)(j0 + i) * n + j0 + j] = j <= i ? L[i][j] : 0.0;
-    }
-}
-
-// Panel: rows i >= j0 + b of the block column: x L_d^T = a, one row per
-// thread (forward substitution against the factored diagonal block).
-__global__ void gp_trsm_panel_k(double *A, int n, int j0, int b)
-{
-    __shared__ double L[GP_NB][GP_NB + 1];
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e / b, j = e % b;
-        L[i][j] = A[(long)(j0 + i) * n + j0 + j];
-    }
-    __syncthreads();
-    const int i = j0 + b + blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n)
-        return;
-    double x[GP_NB];
-    double *row = A + (long)i * n + j0;
     for (int k = 0; k < b; k++) {
-        double s = row[k];
-        for (int q = 0; q < k; q++)
-            s -= x[q] * L[k][q];
-        x[k] = s / L[k][k];
+        if (t == 0) {
+            double d = L[k][k];
+            if (!(d > 0)) {
+                *flag = 1;
+                d = 1.0;
+            }
+            L[k][k] = sqrt(d);
+        }
+        __syncthreads();
+        const double dk = L[k][k];
+        for (int i = k + 1 + t; i < b; i += blockDim.x)
+            L[i][k] /= dk;
+        __syncthreads();
+        // Trailing lower triangle of the block: 16 x 16 threads stepping
+        // over rows and columns (no division in the loop).
+        const int ty = t / 16, tx = t % 16;
+        for (int i = k + 1 + ty; i < b; i += 16) {
+            const double lik = L[i][k];
+            for (int j = k + 1 + tx; j <= i; j += 16)
+                L[i][j] -= lik * L[j][k];
+        }
+        __syncthreads();
     }
-    for (int k = 0; k < b; k++)
-        row[k] = x[k];
+    // Inverse of the lower-triangular factor, column c by thread c
+    // (forward substitution L x = e_c).
+    if (t < GP_NB) {
+        const int c = t;
+        for (int i = 0; i < GP_NB; i++) {
+            double s = i == c ? 1.0 : 0.0;
+            for (int k = c; k < i; k++)
+                s -= L[i][k] * X[k][c];
+            X[i][c] = i < c ? 0.0 : s / L[i][i];
+        }
+    }
+    __syncthreads();
+    for (int e = t; e < GP_NB * GP_NB; e += blockDim.x) {
+        const int i = e / GP_NB, j = e % GP_NB;
+        Linv[e] = X[i][j];
+        if (i < b && j < b)
+            A[(long)(j0 + i) * n + j0 + j] = j <= i ? L[i][j] : 0.0;
+    }
 }
 
-// C (M x N, ldc) -= A B with A(m, k) = A[m sam + k sak], B(k, n) =
-// B[k sbk + n sbn]; 64 x 64 tiles, 16 k per step, 4 x 4 per thread.
+// C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
+// sak], B(k, n) = B[k sbk + n sbn]; 64 x 64 tiles, 16 k per step, 4 x 4
+// per thread; lower_only skips tiles and elements above the diagonal.
 __global__ void __launch_bounds__(256)
-dgemm_sub_k(int M, int N, int K, const double *A, long sam, long sak,
-            const double *B, long sbk, long sbn, double *C, long ldc,
-            int lower_only)
+dgemm_k(int M, int N, int K, const double *A, long sam, long sak, const double *B,
+        long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
 {
     __shared__ double As[16][64 + 1];
     __shared__ double Bs[16][64 + 1];
@@ -108,12 +108,18 @@ dgemm_sub_k(int M, int N, int K, const double *A, long sam, long sak,
     if (lower_only && n0 > m0 + 63)
         return;
     double acc[4][4] = {};
+    // Tile loads with consecutive threads along each operand's unit-stride
+    // dimension (coalesced whichever way the operand is stored).
+    const bool a_k = sak == 1, b_n = sbn == 1;
     for (int k0 = 0; k0 < K; k0 += 16) {
         for (int e = threadIdx.x; e < 64 * 16; e += 256) {
-            const int r = e / 16, k = e % 16;
-            const int m = m0 + r, kk = k0 + k;
+            int r = a_k ? e / 16 : e % 64, k = a_k ? e % 16 : e / 64;
+            int m = m0 + r, kk = k0 + k;
             As[k][r] = m < M && kk < K ? A[m * sam + kk * sak] : 0.0;
+            r = b_n ? e % 64 : e / 16;
+            k = b_n ? e / 64 : e % 16;
             const int nn = n0 + r;
+            kk = k0 + k;
             Bs[k][r] = nn < N && kk < K ? B[kk * sbk + nn * sbn] : 0.0;
         }
         __syncthreads();
@@ -141,65 +147,29 @@ dgemm_sub_k(int M, int N, int K, const double *A, long sam, long sak,
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int nn = n0 + tx + 16 * j;
-            if (nn < N && (!lower_only || nn <= m))
-                C[(long)m * ldc + nn] -= acc[i][j];
+            if (nn < N && (!lower_only || nn <= m)) {
+                double *c = C + (long)m * ldc + nn;
+                *c = sub ? *c - acc[i][j] : acc[i][j];
+            }
         }
     }
 }
 
-static void dgemm_sub(cudaStream_t st, int M, int N, int K, const double *A,
-                      long sam, long sak, const double *B, long sbk, long sbn,
-                      double *C, long ldc, int lower_only)
+static void dgemm(cudaStream_t st, int M, int N, int K, const double *A, long sam, long sak,
+                  const double *B, long sbk, long sbn, double *C, long ldc, int sub,
+                  int lower_only)
 {
     if (M <= 0 || N <= 0 || K <= 0)
         return;
-    dgemm_sub_k<<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, st>>>(
-        M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, lower_only);
+    dgemm_k<<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, st>>>(M, N, K, A, sam, sak, B, sbk, sbn,
+                                                           C, ldc, sub, lower_only);
 }
 
-// Z (n x d) from F (float), for the solves.
 __global__ void gp_load_rhs_k(const float *F, long e_n, double *Z)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e < e_n)
         Z[e] = F[e];
-}
-
-// Diagonal-block triangular solve for every column of Z rows j0 .. j0+b:
-// forward (L_d z = f) or backward (L_d^T x = z); one thread per column.
-__global__ void gp_trsv_block_k(const double *A, int n, int j0, int b,
-                                double *Z, int d, int backward)
-{
-    __shared__ double L[GP_NB][GP_NB + 1];
-    for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
-        const int i = e / b, j = e % b;
-        L[i][j] = A[(long)(j0 + i) * n + j0 + j];
-    }
-    __syncthreads();
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= d)
-        return;
-    double z[GP_NB];
-    for (int k = 0; k < b; k++)
-        z[k] = Z[(long)(j0 + k) * d + c];
-    if (!backward) {
-        for (int k = 0; k < b; k++) {
-            double s = z[k];
-            for (int q = 0; q < k; q++)
-                s -= L[k][q] * z[q];
-            z[k] = s / L[k][k];
-        }
-    }
-    else {
-        for (int k = b - 1; k >= 0; k--) {
-            double s = z[k];
-            for (int q = k + 1; q < b; q++)
-                s -= L[q][k] * z[q];
-            z[k] = s / L[k][k];
-        }
-    }
-    for (int k = 0; k < b; k++)
-        Z[(long)(j0 + k) * d + c] = z[k];
 }
 
 __global__ void gp_store_k(const double *Z, long e_n, float *X)
@@ -209,45 +179,76 @@ __global__ void gp_store_k(const double *Z, long e_n, float *X)
         X[e] = (float)Z[e];
 }
 
-// Work: n * n + n * d doubles.
+// Work: n n + n d doubles (A, Z), cdiv(n, 64) 64 x 64 doubles (inverses)
+// and 64 max(n, d) doubles (the panel or right-hand-side block copy).
+size_t gp_work_doubles(int n, int d)
+{
+    const size_t nb = (size_t)cdiv(n, GP_NB);
+    const size_t w = (size_t)(n > d ? n : d);
+    return (size_t)n * n + (size_t)n * d + nb * GP_NB * GP_NB + GP_NB * w;
+}
+
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
                   double noise, float *X, double *work, int *flag)
 {
-    double *A = work, *Z = work + (size_t)n * n;
+    const int nb = cdiv(n, GP_NB);
+    double *A = work, *Z = A + (size_t)n * n;
+    double *Linv = Z + (size_t)n * d;
+    double *T = Linv + (size_t)nb * GP_NB * GP_NB;
     const long nn = (long)n * n, nd = (long)n * d;
 
+    const size_t potrf_smem = 2 * GP_NB * (GP_NB + 1) * sizeof(double);
+    static unsigned opted = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(opted >> (dev & 31) & 1)) {
+        if (!cuda_ok(cudaFuncSetAttribute(gp_potrf_inv_k,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)potrf_smem),
+                     "gp_potrf_inv_k"))
+            return;
+        opted |= 1u << (dev & 31);
+    }
     gp_init_k<<<cdiv(nn, 256), 256, 0, st>>>(K, n, noise, A);
-    for (int j0 = 0; j0 < n; j0 += GP_NB) {
-        const int b = n - j0 < GP_NB ? n - j0 : GP_NB;
+    for (int j = 0; j < nb; j++) {
+        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const int rest = n - j0 - b;
-        gp_potrf_k<<<1, 256, 0, st>>>(A, n, j0, b, flag);
+        double *Li = Linv + (size_t)j * GP_NB * GP_NB;
+        gp_potrf_inv_k<<<1, 256, potrf_smem, st>>>(A, n, j0, b, Li, flag);
         if (rest > 0) {
-            gp_trsm_panel_k<<<cdiv(rest, 64), 64, 0, st>>>(A, n, j0, b);
-            // Trailing lower triangle -= panel panel^T.
-            const double *P = A + (long)(j0 + b) * n + j0;
-            dgemm_sub(st, rest, rest, b, P, n, 1, P, 1, n,
-                      A + (long)(j0 + b) * n + j0 + b, n, 1);
+            double *P = A + (long)(j0 + b) * n + j0;
+            // Panel: L21 = A21 Linv^T, through a copy of A21.
+            cudaMemcpy2DAsync(T, GP_NB * sizeof(double), P, n * sizeof(double),
+                              b * sizeof(double), rest, cudaMemcpyDeviceToDevice, st);
+            dgemm(st, rest, b, b, T, GP_NB, 1, Li, 1, GP_NB, P, n, 0, 0);
+            // Trailing lower triangle -= L21 L21^T.
+            dgemm(st, rest, rest, b, P, n, 1, P, 1, n, A + (long)(j0 + b) * n + j0 + b, n, 1,
+                  1);
         }
     }
     gp_load_rhs_k<<<cdiv(nd, 256), 256, 0, st>>>(F, nd, Z);
-    // L Z = F: solve block j, then update the rows below.
-    for (int j0 = 0; j0 < n; j0 += GP_NB) {
-        const int b = n - j0 < GP_NB ? n - j0 : GP_NB;
+    // L Z = F: Z_j = Linv_j F'_j, then the rows below.
+    for (int j = 0; j < nb; j++) {
+        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const int rest = n - j0 - b;
-        gp_trsv_block_k<<<cdiv(d, 64), 64, 0, st>>>(A, n, j0, b, Z, d, 0);
+        const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
+        cudaMemcpyAsync(T, Z + (long)j0 * d, (size_t)b * d * sizeof(double),
+                        cudaMemcpyDeviceToDevice, st);
+        dgemm(st, b, d, b, Li, GP_NB, 1, T, d, 1, Z + (long)j0 * d, d, 0, 0);
         if (rest > 0)
-            dgemm_sub(st, rest, d, b, A + (long)(j0 + b) * n + j0, n, 1,
-                      Z + (long)j0 * d, d, 1, Z + (long)(j0 + b) * d, d, 0);
+            dgemm(st, rest, d, b, A + (long)(j0 + b) * n + j0, n, 1, Z + (long)j0 * d, d, 1,
+                  Z + (long)(j0 + b) * d, d, 1, 0);
     }
-    // L^T X = Z: from the last block up; the rows above get
-    // Z[0:j0] -= L[j0:j0+b, 0:j0]^T X[j0:j0+b].
-    int last = ((n - 1) / GP_NB) * GP_NB;
-    for (int j0 = last; j0 >= 0; j0 -= GP_NB) {
-        const int b = n - j0 < GP_NB ? n - j0 : GP_NB;
-        gp_trsv_block_k<<<cdiv(d, 64), 64, 0, st>>>(A, n, j0, b, Z, d, 1);
+    // L^T X = Z: X_j = Linv_j^T Z'_j from the last block up, then
+    // Z'_above -= L_j,above^T X_j.
+    for (int j = nb - 1; j >= 0; j--) {
+        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
+        const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
+        cudaMemcpyAsync(T, Z + (long)j0 * d, (size_t)b * d * sizeof(double),
+                        cudaMemcpyDeviceToDevice, st);
+        dgemm(st, b, d, b, Li, 1, GP_NB, T, d, 1, Z + (long)j0 * d, d, 0, 0);
         if (j0 > 0)
-            dgemm_sub(st, j0, d, b, A + (long)j0 * n, 1, n, Z + (long)j0 * d, d,
-                      1, Z, d, 0);
+            dgemm(st, j0, d, b, A + (long)j0 * n, 1, n, Z + (long)j0 * d, d, 1, Z, d, 1, 0);
     }
     gp_store_k<<<cdiv(nd, 256), 256, 0, st>>>(Z, nd, X);
 }

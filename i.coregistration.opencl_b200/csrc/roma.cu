@@ -800,7 +800,7 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
     I->g_kyy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_kxy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_x = (float *)dmalloc(I, n16 * GP_DIM * 4, "GP solve");
-    I->gp_work = (double *)dmalloc(I, (n16 * n16 + n16 * GP_DIM) * 8, "GP work");
+    I->gp_work = (double *)dmalloc(I, gp_work_doubles((int)n16, GP_DIM) * 8, "GP work");
     I->gp_flag = (int *)dmalloc(I, sizeof(int), "GP flag");
     size_t dmax = 0;
     for (int p = 0; p < 2; p++)
