@@ -34,6 +34,8 @@ COARSE = 560
 TILE_SRC = 1024
 METRIC = "RoMa-v2ref tile pairs/s"
 UNIT = "tile_pairs/s"
+# Seconds of timed CPU work in the reference arm (whole tile pairs).
+REF_BUDGET_S = 120.0
 CACHE = Path(os.environ.get("COREG_CACHE", "/tmp/coreg_cache"))
 
 
@@ -145,9 +147,11 @@ class Clocks:
 
 # ------------------------------------------------------------- work model
 
-def work_model(Hp=H, Wp=W, Cs=COARSE):
+def work_model(Hp=H, Wp=W, Cs=COARSE, es=2):
     """Algorithmic FLOPs (tensor work) and bytes (memory-bound work) per
-    tile pair of roma_v2ref, by the profiler's operation names."""
+    tile pair of roma_v2ref, by the profiler's operation names; es is the
+    element size of the refiner activations (2 in bfloat16 mode, 4 in
+    float32 mode)."""
     D, c16 = 1024, Cs // 14
     n16, ntok = c16 * c16, c16 * c16 + 1
     fl, by = {}, {}
@@ -183,7 +187,7 @@ def work_model(Hp=H, Wp=W, Cs=COARSE):
         for sc, fin, fo in ((4, 256, 192), (2, 128, 48), (1, 64, 12)):
             add(fl, "vgg2_proj", 2 * 2 * (hh // sc) * (ww // sc) * fin * fo)
 
-    def refiner(n, cin, feat, r, nout, es=4):
+    def refiner(n, cin, feat, r, nout):
         add(fl, "refiner_pw", 9 * 2 * n * cin * cin)
         add(fl, "refiner_out", 2 * n * cin * nout)
         add(fl, "roma_dwconv5", 9 * 2 * 25 * n * cin)
@@ -241,9 +245,11 @@ def traffic_from_profiles(kernel):
 
 # -------------------------------------------------------------- CPU arm
 
-def cpu_sample(tiles, threads, reps=1):
+def cpu_sample(tiles, threads, reps=1, warmup=0, budget_s=None):
     """The oracle (the reference's roma.c restated, torch float32 on the
-    host cores) on full tile pairs: seconds per pair."""
+    host cores) on full tile pairs: seconds per timed pair, after `warmup`
+    untimed pairs; stops early once `budget_s` seconds of timed pairs are
+    spent (at least one pair is timed)."""
     import torch
 
     from oracle import roma_ref
@@ -255,29 +261,36 @@ def cpu_sample(tiles, threads, reps=1):
     model = roma_ref.Model(*sds)
     r = roma_ref.Runner(model, coarse=COARSE)
     times = []
-    for i in range(reps):
+    for i in range(warmup + reps):
         a, b = tiles[i % len(tiles)]
         t = time.perf_counter()
         r.run(a, b)
-        times.append(time.perf_counter() - t)
+        if i >= warmup:
+            times.append(time.perf_counter() - t)
+            if budget_s is not None and sum(times) > budget_s:
+                break
     return times
 
 
 def reference_arm(args, rank, world):
+    """The reference's CPU implementation of the path: the oracle port on
+    all host cores (the reference's OpenCL path has no OpenCL platform to
+    run on). One step is one full tile pair; at most one warm-up pair and
+    REF_BUDGET_S seconds of timed pairs, so that the run ends in minutes."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     tiles = make_tiles(range(2))
-    times = cpu_sample(tiles, threads, reps=args.warmup_ref + args.steps_ref)
-    t = times[args.warmup_ref:] or times
+    warm = min(args.warmup, 1)
+    t = cpu_sample(tiles, threads, reps=max(1, args.steps), warmup=warm, budget_s=REF_BUDGET_S)
     v = len(t) / sum(t)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": len(t), "warmup": args.warmup_ref, "ms_per_step": 1000 * sum(t) / len(t),
+        "steps": len(t), "warmup": warm, "ms_per_step": 1000 * sum(t) / len(t),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded scene generator, random-init weights seed 0)",
-        "config": {"workload": "roma_v2ref tile pair, coarse 560, fine 864x864", "tile_px": H,
-                   "coarse_px": COARSE},
+        "config": {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 "
+                               "(BASELINE configs[3])", "tile_px": H, "coarse_px": COARSE},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{len(t)} full tile pair(s) through the oracle "
                                    "(torch float32 restatement of roma.c; the reference's "
@@ -363,9 +376,10 @@ def gpu_arm(args, rank, world, local):
 
     # Roofline of the dominant kernel, from one profiled tile.
     prof = profile_step(lib, dev, net, inA.ptr, inB.ptr)
-    fl, by = work_model()
+    fl, by = work_model(es=2 if prec else 4)
     hbm, bf16, peak_kind = peaks()
-    dom = max(prof, key=lambda k: prof[k][0])
+    # The dominant profiled operation that has a work model.
+    dom = max((k for k in prof if k in fl or k in by), key=lambda k: prof[k][0])
     roof = None
     if dom in fl and (dom not in by or fl[dom] / max(by[dom], 1) > 50):
         ms_d, calls = prof[dom]
@@ -431,8 +445,6 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--tiles", type=int, default=4, help="distinct tile pairs per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--steps-ref", type=int, default=2, help="CPU-arm timed tile pairs")
-    ap.add_argument("--warmup-ref", type=int, default=0)
     args = ap.parse_args()
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":

@@ -28,7 +28,7 @@ ERRORS_FATAL, ERRORS_RECORD = 0, 1
 class OclBackend(C.Structure):
     _fields_ = [
         ("device", C.c_int),
-        ("stream", C.c_void_p),
+        ("queue", C.c_void_p),
         ("device_name", C.c_char * 256),
         ("platform_name", C.c_char * 256),
         ("max_alloc", C.c_uint64),

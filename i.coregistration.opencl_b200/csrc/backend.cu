@@ -236,13 +236,13 @@ extern "C" void ocl_init(struct ocl_backend *ocl, const char *device_opt,
         if (!cuda_ok(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking),
                      "cudaStreamCreate"))
             return;
-        ocl->stream = st;
+        ocl->queue = st;
     }
 }
 
 extern "C" void ocl_free(struct ocl_backend *ocl)
 {
-    if (ocl->stream) {
+    if (ocl->queue) {
         cudaSetDevice(ocl->device);
         cudaStreamSynchronize(stream_of(ocl));
         cudaStreamDestroy(stream_of(ocl));
@@ -437,6 +437,11 @@ extern "C" void ocl_zero(struct ocl_backend *ocl, cl_mem m, size_t off, size_t n
         return;
     cuda_ok(cudaMemsetAsync((char *)m->ptr + off, 0, n, stream_of(ocl)),
             "cudaMemsetAsync");
+}
+
+extern "C" cl_int clFinish(cl_command_queue queue)
+{
+    return (cl_int)cudaStreamSynchronize((cudaStream_t)queue);
 }
 
 extern "C" void ocl_finish(struct ocl_backend *ocl)

@@ -45,7 +45,7 @@ struct Prof {
 
 inline cudaStream_t stream_of(const struct ocl_backend *ocl)
 {
-    return (cudaStream_t)ocl->stream;
+    return (cudaStream_t)ocl->queue;
 }
 
 inline float *fptr(cl_mem m, long off = 0)

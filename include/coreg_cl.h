@@ -22,6 +22,22 @@ typedef float cl_float;
 /* A device buffer: pointer, size in bytes, owner flag. */
 typedef struct _cl_mem *cl_mem;
 
+/* The backend's in-order queue: a cudaStream_t. */
+typedef void *cl_command_queue;
+
 #define CL_SUCCESS 0
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Waits until every launch on the queue has finished; CL_SUCCESS, or the
+ * CUDA error code. The reference's callers finish their queue with it
+ * (tests/ops_check.c:489 of i.coregistration.opencl). */
+cl_int clFinish(cl_command_queue queue);
+
+#ifdef __cplusplus
+}
+#endif
 
 #endif /* COREG_CL_H */

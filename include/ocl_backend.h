@@ -31,7 +31,7 @@ extern "C" {
 
 struct ocl_backend {
     int device;      /* CUDA device ordinal. */
-    void *stream;    /* cudaStream_t of every launch of this backend. */
+    cl_command_queue queue; /* cudaStream_t of every launch of this backend. */
     char device_name[256];
     char platform_name[256]; /* "CUDA <runtime version>". */
     cl_ulong max_alloc;

@@ -10,6 +10,13 @@ Gaussian-process solve in float64 as the reference's host code. Each
 function cites the lines it restates. The coarse-pass side is a parameter
 (roma.c fixes it at ROMA_COARSE = 560) so that the parity tests can run
 small.
+
+Parity unpinned at model level: the reference's own RoMa path needs an
+OpenCL platform to run and its model-level compare scripts need the
+upstream romatch / RoMaV2 packages, none of which is available, so this
+restatement is checked only through the generic ops it shares with
+oracle/ops_ref.py (pinned to the reference's ops_compare.py) and by
+reading the cited lines.
 """
 
 import math
