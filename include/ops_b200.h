@@ -38,6 +38,31 @@ void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem w,
 void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm, int heads,
                        float scale, cl_mem out);
 
+/* ops_gemm that allocates no device memory; it has no counterpart in the
+ * reference. Same arguments, meaning and results as ops_gemm. With
+ * o->precision OPS_BF16, ops_gemm packs the operands to bfloat16 in a
+ * buffer it grows with cudaMalloc; this variant packs them into a fixed
+ * device array of ops_gemm_noalloc_max_bytes() bytes (16 MiB) that is part
+ * of the library. It is meant for callers that must not allocate while
+ * they run: a plug-in whose host framework's caching allocator already
+ * holds the device's free memory, or a pipeline that does all allocation at
+ * start-up because cudaMalloc synchronises the device. A product whose
+ * packed operands, 2 (M + N) K nb bytes plus alignment, exceed the array is
+ * rejected with an error naming the sizes (ops_gemm still runs it). The
+ * first call on each device looks up the array's address and may load
+ * the library's module there, so make it before any stream capture. All
+ * calls on a device share the one array: calls that overlap in time
+ * (several streams, host threads or ops contexts) corrupt each other's
+ * results and must be serialised by the caller. Float32 products
+ * (OPS_FP32, or shapes the tensor-core path does not take) stage nothing. */
+void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd A,
+                      struct opnd B, int transb, struct opnd C, int nb, int nb1,
+                      cl_mem bias, int biasrow, cl_mem R, long roff, float alpha,
+                      int act, float slope);
+
+/* Size in bytes of ops_gemm_noalloc's scratch array. */
+size_t ops_gemm_noalloc_max_bytes(void);
+
 /* Non-zero when a bounded wait of a tensor-core kernel ran out since the
  * last call (the kernel then stopped and its results are invalid); the
  * code is cleared. */
