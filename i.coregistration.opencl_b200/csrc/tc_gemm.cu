@@ -9,21 +9,28 @@
 // each k-block a 3-D TMA box of the map shifted by the tap, zeros read at
 // the borders: no im2col buffer.
 //
-// One CTA per 128 x BN output tile, warp-specialized:
+// Persistent: one CTA per SM walks the 128 x BN output tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (row blocks fastest, so that the CTAs running
+// at one time share the weight columns in L2). Warp-specialized:
 //   warp 0      TMA producer: A and B tiles of 64 K-elements per stage,
 //               128-byte swizzled, into a ring of STAGES shared-memory
-//               stages (mbarrier full[s], transaction bytes);
+//               stages (mbarrier full[s], transaction bytes); the ring runs
+//               on across tile boundaries;
 //   warp 1      tensor-memory allocator and MMA issuer: one thread issues
-//               4 tcgen05.mma (K = 16 each) per stage into a 128 x BN
-//               float32 accumulator in TMEM and commits each stage to
-//               empty[s] (the producer's refill signal), the last to done;
+//               4 tcgen05.mma (K = 16 each) per stage into one of two
+//               128 x BN float32 accumulators in TMEM (tiles alternate),
+//               commits each stage to empty[s] (the producer's refill
+//               signal) and each finished tile to acc_full[buffer];
 //   warps 2..9  epilogue, two warps per TMEM lane quadrant (alternate
 //               32-column chunks): each reads its 32 lanes (rows) with
 //               tcgen05.ld, transposes them through a padded shared-memory
 //               block and writes every row with one coalesced warp store
 //               (lane = column), bias, activation and residual applied on
-//               the way. Stores of one row per thread would make 32
-//               separate memory requests per instruction.
+//               the way, then frees the accumulator (acc_empty[buffer]).
+//               Stores of one row per thread would make 32 separate memory
+//               requests per instruction.
+// With two accumulators the epilogue of a tile overlaps the main loop of
+// the next one.
 // Every mbarrier wait is bounded (about two seconds); a wait that runs out
 // records an error code (coreg_tc_status) and the CTA leaves its loops,
 // frees its tensor memory and returns.
@@ -55,16 +62,36 @@ struct TcParams {
     // Convolution mode (3 x 3, stride 1, padding 1, channels-last input of
     // cH x cW x cC, cC a multiple of 64): the tile is TW x TH output pixels
     // (TW TH = 128), k-block kb = (tap, 64-channel chunk).
-    int conv, cH, cW, cC, TW, TH, tiles_x;
+    int conv, cH, cW, cC, TW, TH, tiles_x, tiles_y;
 };
 
 template <int BN, int STAGES>
 struct Smem {
     alignas(1024) __nv_bfloat16 a[STAGES][BM * BK];
     alignas(1024) __nv_bfloat16 b[STAGES][BN * BK];
-    uint64_t full[STAGES], empty[STAGES], done;
+    uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
     uint32_t tmem;
 };
+
+constexpr int EPI_WARPS = NTHREADS / 32 - 2;
+
+// Output tile t: first row (dense) or pixel origin (convolution) and first
+// column.
+struct Tile {
+    int m0, n0, cx0, cy0;
+};
+
+template <int BN>
+__device__ __forceinline__ Tile tile_of(const TcParams &p, int t, int tiles_m)
+{
+    const int mt = t % tiles_m;
+    Tile r;
+    r.m0 = mt * BM;
+    r.n0 = (t / tiles_m) * BN;
+    r.cx0 = p.conv ? (mt % p.tiles_x) * p.TW : 0;
+    r.cy0 = p.conv ? (mt / p.tiles_x) * p.TH : 0;
+    return r;
+}
 
 // The activation (ACT, or -1 for the run-time one of p.act) and the output
 // type are template parameters: a run-time switch would inline every
@@ -79,26 +106,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     // Epilogue transposes, per epilogue warp 32 rows x 32 columns: a
     // statically declared shared array, so that its accesses compile to
     // shared-memory instructions.
-    __shared__ float stage_all[NTHREADS / 32 - 2][32][33];
+    __shared__ float stage_all[EPI_WARPS][32][33];
     Smem<BN, STAGES> &s = *reinterpret_cast<Smem<BN, STAGES> *>(
         (void *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int nk = (p.K + BK - 1) / BK;
-    // Convolution tile origin (pixels x0 .., rows y0 ..).
-    const int cx0 = p.conv ? (blockIdx.y % p.tiles_x) * p.TW : 0;
-    const int cy0 = p.conv ? (blockIdx.y / p.tiles_x) * p.TH : 0;
+    const int tiles_m = p.conv ? p.tiles_x * p.tiles_y : (p.M + BM - 1) / BM;
+    const int ntiles = tiles_m * ((p.N + BN - 1) / BN);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
         }
-        mbar_init(&s.done, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s.acc_full[i], 1);
+            mbar_init(&s.acc_empty[i], EPI_WARPS);
+        }
         mbar_fence_init();
     }
     if (warp == 1)
-        tmem_alloc(&s.tmem, BN);
+        tmem_alloc(&s.tmem, 2 * BN);
     fence_before();
     __syncthreads();
     fence_after();
@@ -107,42 +135,61 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     if (warp == 0) {
         if (lane == 0) {
             const uint32_t bytes = (BM + BN) * BK * 2;
-            for (int kb = 0; kb < nk; kb++) {
-                const int st = kb % STAGES;
-                if (kb >= STAGES &&
-                    !mbar_wait(&s.empty[st], ((kb / STAGES) - 1) & 1, 1))
-                    break;
-                mbar_expect_tx(&s.full[st], bytes);
-                if (p.conv) {
-                    const int chunks = p.cC / BK, tap = kb / chunks;
-                    const int c0 = (kb % chunks) * BK;
-                    tma_load_3d(s.a[st], &tma_a, &s.full[st], c0, cx0 + tap % 3 - 1,
-                                cy0 + tap / 3 - 1);
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const Tile tl = tile_of<BN>(p, t, tiles_m);
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int st = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(&s.empty[st], ((it / STAGES) - 1) & 1, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&s.full[st], bytes);
+                    if (p.conv) {
+                        const int chunks = p.cC / BK, tap = kb / chunks;
+                        const int c0 = (kb % chunks) * BK;
+                        tma_load_3d(s.a[st], &tma_a, &s.full[st], c0, tl.cx0 + tap % 3 - 1,
+                                    tl.cy0 + tap / 3 - 1);
+                    }
+                    else
+                        tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, tl.m0);
+                    tma_load_2d(s.b[st], &tma_b, &s.full[st], kb * BK, tl.n0);
                 }
-                else
-                    tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, m0);
-                tma_load_2d(s.b[st], &tma_b, &s.full[st], kb * BK, n0);
             }
         }
     }
     else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(BM, BN);
-            for (int kb = 0; kb < nk; kb++) {
-                const int st = kb % STAGES;
-                // TMA completion through the mbarrier orders the tile for
-                // the tensor cores; no tcgen05 fence is needed here.
-                if (!mbar_wait(&s.full[st], (kb / STAGES) & 1, 2))
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
+                const int buf = lt & 1, use = lt >> 1;
+                // The epilogue has read this accumulator's previous tile.
+                if (use > 0 && !mbar_wait(&s.acc_empty[buf], (use - 1) & 1, 4))
                     break;
-                const uint64_t da = sw128_desc(su32(s.a[st]));
-                const uint64_t db = sw128_desc(su32(s.b[st]));
+                fence_after();
+                const uint32_t acc = tmem + (uint32_t)(buf * BN);
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int st = it % STAGES;
+                    // TMA completion through the mbarrier orders the tile
+                    // for the tensor cores; no tcgen05 fence is needed here.
+                    if (!mbar_wait(&s.full[st], (it / STAGES) & 1, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t da = sw128_desc(su32(s.a[st]));
+                    const uint64_t db = sw128_desc(su32(s.b[st]));
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++)
-                    mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc,
-                             (kb > 0 || k > 0) ? 1u : 0u);
-                mma_commit(&s.empty[st]);
+                    for (int k = 0; k < BK / 16; k++)
+                        mma_bf16(acc, da + 2 * k, db + 2 * k, idesc,
+                                 (kb > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(&s.empty[st]);
+                }
+                if (ok)
+                    mma_commit(&s.acc_full[buf]);
             }
-            mma_commit(&s.done);
         }
     }
     else {
@@ -152,28 +199,34 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         // epilogue warps.
         const int q = warp % 4, half = (warp - 2) / 4;
         const int r = 32 * q + lane;
-        int row = m0 + r;
-        if (p.conv) {
-            const int px = cx0 + r % p.TW, py = cy0 + r / p.TW;
-            row = px < p.cW && py < p.cH ? py * p.cW + px : p.M;
-        }
         float(*stage)[33] = stage_all[warp - 2];
-        // Decided per warp: the TMEM loads below are warp-collective.
-        if (__all_sync(0xffffffffu, mbar_wait_backoff(&s.done, 0, 3))) {
+        TC *C = (TC *)p.C;
+        const TC *R = (const TC *)p.R;
+        int lt = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+            const int buf = lt & 1, use = lt >> 1;
+            const Tile tl = tile_of<BN>(p, t, tiles_m);
+            int row = tl.m0 + r;
+            if (p.conv) {
+                const int px = tl.cx0 + r % p.TW, py = tl.cy0 + r / p.TW;
+                row = px < p.cW && py < p.cH ? py * p.cW + px : p.M;
+            }
+            // Decided per warp: the TMEM loads below are warp-collective.
+            if (!__all_sync(0xffffffffu, mbar_wait_backoff(&s.acc_full[buf], use & 1, 3)))
+                break;
             fence_after();
-            for (int c0 = 32 * half; c0 < BN && n0 + c0 < p.N; c0 += 64) {
+            const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
+            for (int c0 = 32 * half; c0 < BN && tl.n0 + c0 < p.N; c0 += 64) {
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+                tmem_ld32(acc + c0, v);
 #pragma unroll
                 for (int j = 0; j < 32; j++)
                     stage[lane][j] = v[j];
                 __syncwarp();
                 // Lane = column from here on.
-                const int col = n0 + c0 + lane;
+                const int col = tl.n0 + c0 + lane;
                 const bool cok = col < p.N;
                 const float bias = cok && p.bias ? p.bias[col] : 0.0f;
-                TC *C = (TC *)p.C;
-                const TC *R = (const TC *)p.R;
 #pragma unroll 4
                 for (int rr = 0; rr < 32; rr++) {
                     const int grow = __shfl_sync(0xffffffffu, row, rr);
@@ -188,13 +241,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                 }
                 __syncwarp();
             }
+            // This warp's reads of the accumulator are complete (each
+            // tcgen05.ld waited): hand it back to the MMA warp.
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&s.acc_empty[buf]);
         }
     }
     fence_before();
     __syncthreads();
     if (warp == 1) {
         fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, 2 * BN);
     }
 }
 
@@ -216,7 +275,7 @@ int conv_tile_width(int H, int W)
 }
 
 template <int BN, int STAGES, int ACT, typename TC>
-bool run_tc(cudaStream_t st, dim3 grid, const CUtensorMap &ma, const CUtensorMap &mb,
+bool run_tc(cudaStream_t st, int grid, const CUtensorMap &ma, const CUtensorMap &mb,
             const TcParams &p)
 {
     const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
@@ -228,12 +287,12 @@ bool run_tc(cudaStream_t st, dim3 grid, const CUtensorMap &ma, const CUtensorMap
 }
 
 template <int BN, int STAGES>
-bool launch_tc(cudaStream_t st, const GemmArgs &g)
+bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
     CUtensorMap ma, mb;
     TcParams p;
     memset(&p, 0, sizeof(p));
-    int grid_y = cdiv(g.M, BM);
+    long tiles_m = cdiv(g.M, BM);
     if (g.amode == 1) {
         p.conv = 1;
         p.cH = g.cH;
@@ -242,7 +301,8 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g)
         p.TW = conv_tile_width(g.cH, g.cW);
         p.TH = BM / p.TW;
         p.tiles_x = cdiv(g.cW, p.TW);
-        grid_y = p.tiles_x * cdiv(g.cH, p.TH);
+        p.tiles_y = cdiv(g.cH, p.TH);
+        tiles_m = (long)p.tiles_x * p.tiles_y;
         if (!make_map_conv(&ma, g.A, g.cH, g.cW, g.cC, p.TW, p.TH))
             return false;
     }
@@ -261,7 +321,11 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g)
     p.act = g.act;
     p.slope = g.slope;
     p.c_bf16 = g.c == DT_BF16;
-    dim3 grid(cdiv(g.N, BN), grid_y);
+    const long ntiles = tiles_m * cdiv(g.N, BN);
+    if (ntiles >= (1L << 31))
+        return false;
+    // Persistent: at most one CTA per SM (the shared memory allows one).
+    const int grid = (int)(ntiles < sm_count ? ntiles : sm_count);
     if (p.c_bf16) {
         if (g.act == ACTF_NONE)
             return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, p);
@@ -359,9 +423,21 @@ int gemm_status()
 
 }  // namespace tc
 
+// Output tiles of 128 x bn for g.
+static long tiles_for(const GemmArgs &g, int bn)
+{
+    long tm = cdiv(g.M, tc::BM);
+    if (g.amode == 1) {
+        const int tw = tc::conv_tile_width(g.cH, g.cW);
+        tm = (long)cdiv(g.cW, tw) * cdiv(g.cH, tc::BM / tw);
+    }
+    return tm * cdiv(g.N, bn);
+}
+
 bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
-    (void)sm_count;
+    if (sm_count <= 0)
+        sm_count = 148;
     if (g.ab != DT_BF16 || !g.transb || g.nb != 1)
         return false;
     if (g.amode == 2 || (g.amode == 1 && (g.cC % tc::BK || g.K != 9 * g.cC)))
@@ -373,9 +449,16 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     if (((uintptr_t)g.A & 15) || ((uintptr_t)g.B & 15) ||
         (g.amode == 0 && (g.lda & 7)) || (g.ldb & 7))
         return false;
-    if (g.N >= 256)
-        return tc::launch_tc<256, 4>(st, g);
-    return tc::launch_tc<128, 6>(st, g);
+    // Tile width by the rounds of tiles the persistent CTAs walk: a 128 x
+    // 128 tile takes about half the time of a 128 x 256 one plus the
+    // overhead of reading its operands twice as often (weighted 1.15).
+    if (g.N >= 256) {
+        const long r256 = (tiles_for(g, 256) + sm_count - 1) / sm_count;
+        const long r128 = (tiles_for(g, 128) + sm_count - 1) / sm_count;
+        if (r256 * 256 * 100 <= r128 * 128 * 115)
+            return tc::launch_tc<256, 4>(st, g, sm_count);
+    }
+    return tc::launch_tc<128, 6>(st, g, sm_count);
 }
 
 }  // namespace coreg
