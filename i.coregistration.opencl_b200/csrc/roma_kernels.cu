@@ -544,10 +544,97 @@ dwconv5_tm_k(const TI *in, long ps, int C, int H, int W, const float *wt,
     }
 }
 
+// Packed float32 pair FMA of sm_100 (a * b + c on both lanes).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
+{
+    unsigned long long aa, bb, cc, dd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c.x), "f"(c.y));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dd) : "l"(aa), "l"(bb), "l"(cc));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
+    return d;
+}
+
+// bfloat16 channels-last depthwise 5 x 5 (+ bias, ReLU) for maps whose
+// pixel pitch and channel count are multiples of 8: a 16 x 16 pixel x 32
+// channel block stages its 20 x 20 halo tile with 16-byte loads into shared
+// memory as bfloat16 pairs (rows padded by 16 words, so that the two
+// output rows of a warp read different banks); each thread then computes
+// one output row of 16 pixels for one channel pair, accumulating the 5
+// input rows in turn (every input pixel feeds up to 5 outputs of the row)
+// with packed float32 FMAs.
+constexpr int DWP_T = 16, DWP_C = 32, DWP_TW = DWP_T + 4;
+constexpr int DWP_RP = DWP_TW * (DWP_C / 2) + 16;  // words per tile row
+
+__global__ void __launch_bounds__(256)
+dwconv5_pair_k(const __nv_bfloat16 *in, long ps, int C, int H, int W, const float *wt,
+               const float *bias, __nv_bfloat16 *out, long ops)
+{
+    __shared__ __align__(16) uint32_t tile[DWP_TW * DWP_RP];
+    const int tid = threadIdx.x, c0 = blockIdx.z * DWP_C;
+    const int x0 = blockIdx.x * DWP_T - 2, y0 = blockIdx.y * DWP_T - 2;
+    for (int e = tid; e < DWP_TW * DWP_TW * (DWP_C / 8); e += 256) {
+        const int j = e % (DWP_C / 8), px = (e / (DWP_C / 8)) % DWP_TW;
+        const int py = e / ((DWP_C / 8) * DWP_TW);
+        const int x = x0 + px, y = y0 + py, c = c0 + 8 * j;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (x >= 0 && x < W && y >= 0 && y < H && c < C)
+            v = *(const uint4 *)(in + ((long)y * W + x) * ps + c);
+        *(uint4 *)&tile[py * DWP_RP + px * (DWP_C / 2) + 4 * j] = v;
+    }
+    __syncthreads();
+    const int pr = tid % (DWP_C / 2), oy = tid / (DWP_C / 2);
+    const int cg = c0 + 2 * pr, y = blockIdx.y * DWP_T + oy;
+    if (cg >= C || y >= H)
+        return;
+    float2 acc[DWP_T];
+    const float2 b = make_float2(bias[cg], bias[cg + 1]);
+#pragma unroll
+    for (int i = 0; i < DWP_T; i++)
+        acc[i] = b;
+#pragma unroll 1
+    for (int a = 0; a < 5; a++) {
+        float2 w[5];
+#pragma unroll
+        for (int k = 0; k < 5; k++)
+            w[k] = make_float2(wt[cg * 25 + a * 5 + k], wt[(cg + 1) * 25 + a * 5 + k]);
+        const uint32_t *row = tile + (oy + a) * DWP_RP + pr;
+#pragma unroll
+        for (int x = 0; x < DWP_TW; x++) {
+            const uint32_t u = row[x * (DWP_C / 2)];
+            const float2 v = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+#pragma unroll
+            for (int k = 0; k < 5; k++) {
+                const int ox = x - k;
+                if (ox >= 0 && ox < DWP_T)
+                    acc[ox] = fma2(v, w[k], acc[ox]);
+            }
+        }
+    }
+    __nv_bfloat16 *o = out + (long)y * W * ops + cg;
+#pragma unroll
+    for (int i = 0; i < DWP_T; i++) {
+        const int x = blockIdx.x * DWP_T + i;
+        if (x < W)
+            *(__nv_bfloat162 *)(o + (long)x * ops) =
+                __floats2bfloat162_rn(fmaxf(acc[i].x, 0.0f), fmaxf(acc[i].y, 0.0f));
+    }
+}
+
 template <typename TI, typename TO>
 static void dwconv5_t(cudaStream_t st, Map in, int C, int H, int W,
                       const float *w, const float *b, MapOut out)
 {
+    if (sizeof(TI) == 2 && sizeof(TO) == 2 && in.cs == 1 && out.cs == 1 && C % 8 == 0 &&
+        in.ps % 8 == 0 && out.ps % 2 == 0 && ((uintptr_t)in.p & 15) == 0 &&
+        ((uintptr_t)out.p & 3) == 0) {
+        dim3 grid(cdiv(W, DWP_T), cdiv(H, DWP_T), cdiv(C, DWP_C));
+        dwconv5_pair_k<<<grid, 256, 0, st>>>((const __nv_bfloat16 *)in.p, in.ps, C, H, W, w,
+                                             b, (__nv_bfloat16 *)out.p, out.ps);
+        return;
+    }
     if (in.cs == 1 && out.cs == 1) {
         // 32 channels per block for 2-byte inputs, 16 for float (the
         // halo tile stays within 48 KB of shared memory).

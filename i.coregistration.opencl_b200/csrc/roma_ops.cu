@@ -4,6 +4,7 @@
 // callers of the reference's kernel argument lists.
 
 #include "roma_kernels.cuh"
+#include "ops_b200.h"
 #include "roma_ops.h"
 
 using namespace coreg;
@@ -118,4 +119,38 @@ extern "C" void roma_dwconv5(struct ops *o, cl_mem in, int C, int H, int W,
     roma_dwconv5_l(stream_of(o->ocl), cm_map(fptr(in), n), C, H, W, fptr(wt),
                    fptr(bias), cm_out(fptr(out), n));
     launch_ok("roma_dwconv5");
+}
+
+extern "C" void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem wt,
+                                cl_mem bias, cl_mem out)
+{
+    if (!bufs_ok({in, wt, bias, out}, "roma_dwconv5_cl"))
+        return;
+    const long n = (long)H * W;
+    if (n <= 0 || C <= 0 || !count_ok(n * C, "roma_dwconv5_cl map"))
+        return;
+    cudaStream_t st = stream_of(o->ocl);
+    Prof p(o->ocl, "roma_dwconv5");
+    if (o->precision != OPS_BF16) {
+        roma_dwconv5_l(st, tm_map(fptr(in), C), C, H, W, fptr(wt), fptr(bias),
+                       tm_out(fptr(out), C));
+        launch_ok("roma_dwconv5_cl");
+        return;
+    }
+    // bfloat16 mode: the map rounded to bfloat16, the model's kernel, the
+    // result widened back.
+    const size_t half = ((size_t)n * C * 2 + 255) / 256 * 256;
+    if (2 * half > o->scratch16_bytes) {
+        ocl_release(&o->scratch16);
+        o->scratch16 = ocl_alloc(o->ocl, 2 * half, "dwconv5 operands");
+        o->scratch16_bytes = 2 * half;
+        if (pending())
+            return;
+    }
+    char *a16 = (char *)o->scratch16->ptr, *o16 = a16 + half;
+    copy2d(st, fptr(in), DT_F32, C, a16, DT_BF16, C, n, C);
+    roma_dwconv5_l(st, tm_map(a16, C, DT_BF16), C, H, W, fptr(wt), fptr(bias),
+                   tm_out(o16, C, DT_BF16));
+    copy2d(st, o16, DT_BF16, C, fptr(out), DT_F32, C, n, C);
+    launch_ok("roma_dwconv5_cl");
 }

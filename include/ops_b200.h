@@ -38,6 +38,16 @@ void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem w,
 void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm, int heads,
                        float scale, cl_mem out);
 
+/* Depthwise 5 x 5 convolution, zero padding 2, + bias + ReLU of a
+ * channels-last (H, W, C) float32 map into (H, W, C): the first half of a
+ * RoMa refiner block with its BatchNorm folded (roma_dwconv5,
+ * roma_kernels.cl:256-284, on channel-major maps). Weights (C, 1, 5, 5),
+ * bias C floats. With o->precision OPS_BF16 the map is rounded to
+ * bfloat16 and the model's bfloat16 kernel runs (float32 arithmetic,
+ * bfloat16 result), as inside roma_match. */
+void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem wt,
+                     cl_mem bias, cl_mem out);
+
 /* ops_gemm that allocates no device memory; it has no counterpart in the
  * reference. Same arguments, meaning and results as ops_gemm. With
  * o->precision OPS_BF16, ops_gemm packs the operands to bfloat16 in a
