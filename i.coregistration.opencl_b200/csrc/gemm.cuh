@@ -89,6 +89,15 @@ void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
 // false when the head size (64 or 128) or alignment is not supported.
 bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
                   long ldo, float scale);
+// 3 x 3 / stride 1 / padding 1 convolution of a channels-last bfloat16
+// (H, W, C) map with few channels (9 C <= kp, kp a multiple of 16) on the
+// tensor cores: an explicit im2col into col (H W x kp bfloat16), then the
+// GEMM with wk, the weights as (K, kp) bfloat16 rows in (tap, channel)
+// order and zero beyond 9 C; out (H W x K) of type ot, bias and activation
+// applied (ops.cu).
+void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, int C, int kp,
+                       const __nv_bfloat16 *wk, const float *bias, int K, int act,
+                       float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count);
 // Double-precision GP solve (gp_chol.cu); work holds gp_work_doubles(n, d).
 size_t gp_work_doubles(int n, int d);
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,

@@ -346,6 +346,69 @@ __global__ void to_type_k(const float *in, long n, T *out)
         stf(out + e, in[e]);
 }
 
+// (K, C, 3, 3) float32 weights -> (K, kp) bfloat16 rows in (tap, channel)
+// order, zero beyond 9 C: the B operand of the few-channel convolution.
+__global__ void conv3_reorder_pad_k(const float *w, int K, int C, int kp, __nv_bfloat16 *out)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)K * kp)
+        return;
+    const int k = (int)(e / kp), j = (int)(e % kp);
+    float v = 0.0f;
+    if (j < 9 * C)
+        v = w[((long)k * C + j % C) * 9 + j / C];
+    out[e] = __float2bfloat16_rn(v);
+}
+
+// Explicit im2col of a 3 x 3 / stride 1 / padding 1 convolution over a
+// channels-last bfloat16 map: row = pixel, column j = tap * C + c for
+// j < 9 C (zeros outside the map), zero up to kp.
+__global__ void im2col3_small_k(const __nv_bfloat16 *in, int H, int W, int C, int kp,
+                                __nv_bfloat16 *col)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long n = (long)H * W;
+    if (e >= n * kp)
+        return;
+    const long pix = e / kp;
+    const int j = (int)(e % kp);
+    __nv_bfloat16 v = __float2bfloat16_rn(0.0f);
+    if (j < 9 * C) {
+        const int t = j / C, c = j % C;
+        const int x = (int)(pix % W) + t % 3 - 1, y = (int)(pix / W) + t / 3 - 1;
+        if (x >= 0 && x < W && y >= 0 && y < H)
+            v = in[((long)y * W + x) * C + c];
+    }
+    col[e] = v;
+}
+
+namespace coreg {
+
+void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, int C, int kp,
+                       const __nv_bfloat16 *wk, const float *bias, int K, int act,
+                       float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count)
+{
+    const long n = (long)H * W;
+    im2col3_small_k<<<cdiv(n * kp, 256), 256, 0, st>>>(in, H, W, C, kp, col);
+    GemmArgs g = gemm_args((int)n, K, kp);
+    g.A = col;
+    g.lda = kp;
+    g.B = wk;
+    g.ldb = kp;
+    g.transb = 1;
+    g.C = out;
+    g.ldc = K;
+    g.bias = bias;
+    g.act = act;
+    g.slope = slope;
+    g.ab = DT_BF16;
+    g.c = ot;
+    if (!gemm_tc(st, g, sm_count))
+        gemm_simt(st, g);
+}
+
+}  // namespace coreg
+
 extern "C" void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C,
                                cl_mem w, cl_mem b, int K, int act, float slope,
                                cl_mem out)
@@ -358,6 +421,32 @@ extern "C" void ops_conv3x3_cl(struct ops *o, cl_mem in, int H, int W, int C,
         n <= 0 || K <= 0 || C <= 0)
         return;
     const bool tc = o->precision == OPS_BF16 && C % 64 == 0;
+    if (o->precision == OPS_BF16 && !tc && 9 * C <= 64) {
+        // Few channels: explicit im2col of kp columns, then the tensor
+        // cores.
+        const int kp = (9 * C + 15) / 16 * 16;
+        const size_t wb = ((size_t)K * kp * 2 + 255) / 256 * 256;
+        const size_t ib = ((size_t)n * C * 2 + 255) / 256 * 256;
+        const size_t bytes = wb + ib + (size_t)n * kp * 2;
+        if (bytes > o->scratch16_bytes) {
+            ocl_release(&o->scratch16);
+            o->scratch16 = ocl_alloc(o->ocl, bytes, "conv3x3 operands");
+            o->scratch16_bytes = bytes;
+            if (pending())
+                return;
+        }
+        char *base = (char *)o->scratch16->ptr;
+        __nv_bfloat16 *wk = (__nv_bfloat16 *)base, *a16 = (__nv_bfloat16 *)(base + wb);
+        __nv_bfloat16 *col = (__nv_bfloat16 *)(base + wb + ib);
+        cudaStream_t st = stream_of(o->ocl);
+        Prof p(o->ocl, "conv3x3_tc");
+        conv3_reorder_pad_k<<<cdiv((long)K * kp, 256), 256, 0, st>>>(fptr(w), K, C, kp, wk);
+        to_type_k<__nv_bfloat16><<<cdiv(n * C, 256), 256, 0, st>>>(fptr(in), n * C, a16);
+        conv3x3_im2col_tc(st, a16, H, W, C, kp, wk, fptr(b), K, act, slope, out->ptr, DT_F32,
+                          col, o->ocl->sm_count);
+        launch_ok("conv3x3_tc");
+        return;
+    }
     const size_t es = tc ? 2 : 4;
     const size_t wbytes = ((size_t)K * 9 * C * es + 255) / 256 * 256;
     const size_t bytes = wbytes + (tc ? (size_t)n * C * 2 : 0);

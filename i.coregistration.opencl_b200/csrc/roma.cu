@@ -84,7 +84,9 @@ struct roma_impl {
     // Weights.
     void *vgg_w[16];
     float *vgg_b[16];
-    int vgg_cin[16], vgg_cout[16];
+    // kp > 0: a few-channel layer stored as (cout, kp) rows for the
+    // explicit-im2col tensor-core path (bfloat16 mode).
+    int vgg_cin[16], vgg_cout[16], vgg_kp[16];
     void *patch_w;
     float *patch_b, *cls;
     std::vector<float> pos_raw; // (1 + 37 * 37) x 1024, host
@@ -98,7 +100,7 @@ struct roma_impl {
     Refiner ref[ROMA_SCALES], ref2[ROMA2_SCALES];
     void *vgg2_w[8];
     float *vgg2_b[8];
-    int vgg2_cin[8], vgg2_cout[8];
+    int vgg2_cin[8], vgg2_cout[8], vgg2_kp[8];
     void *proj2_w[ROMA2_SCALES];
     float *proj2_b[ROMA2_SCALES];
     // Geometry of the passes.
@@ -252,7 +254,7 @@ std::vector<float> conv3_reorder(const std::vector<float> &w, int co, int ci)
 
 // The first nblk blocks of VGG19-BN under <pre>.<index> (roma.c:217-239).
 bool load_vgg(roma_impl *I, struct pth_file *pf, const char *pre, int nblk,
-              void **w, float **b, int *cin_out, int *cout_out)
+              void **w, float **b, int *cin_out, int *cout_out, int *kp_out)
 {
     int l = 0, idx = 0, cin = 3;
     for (int blk = 0; blk < nblk; blk++) {
@@ -264,6 +266,18 @@ bool load_vgg(roma_impl *I, struct pth_file *pf, const char *pre, int nblk,
                               co, 4, shape, wv, bv))
                 return false;
             std::vector<float> r = conv3_reorder(wv, co, cin);
+            kp_out[l] = 0;
+            if (I->wt == DT_BF16 && 9 * cin <= 64) {
+                // Few input channels (the RGB layer): rows of kp columns,
+                // zero beyond 9 cin.
+                const int kp = (9 * cin + 15) / 16 * 16;
+                std::vector<float> rp((size_t)co * kp, 0.0f);
+                for (int o = 0; o < co; o++)
+                    for (int j = 0; j < 9 * cin; j++)
+                        rp[(size_t)o * kp + j] = r[(size_t)o * 9 * cin + j];
+                r.swap(rp);
+                kp_out[l] = kp;
+            }
             w[l] = upload(I, r.data(), r.size(), I->wt, "vgg");
             b[l] = upload_f(I, bv.data(), co, "vgg");
             cin_out[l] = cin;
@@ -630,7 +644,7 @@ extern "C" void roma_load(struct roma_model *m, struct ops *ops,
     // MatchAnything's Lightning checkpoint.
     pth_strip_prefix(pf, "matcher.model.");
     if (!load_vgg(I, pf, "encoder.cnn.layers", 4, I->vgg_w, I->vgg_b, I->vgg_cin,
-                  I->vgg_cout))
+                  I->vgg_cout, I->vgg_kp))
         return;
     // DINOv2 (roma.c:300-324).
     {
@@ -695,7 +709,7 @@ extern "C" void roma_load_v2(struct roma_model *m, struct pth_file *pf)
         return;
     cudaSetDevice(m->ocl->device);
     if (!load_vgg(I, pf, "refiner_features.layers", 3, I->vgg2_w, I->vgg2_b,
-                  I->vgg2_cin, I->vgg2_cout))
+                  I->vgg2_cin, I->vgg2_cout, I->vgg2_kp))
         return;
     for (int j = 0; j < ROMA2_SCALES; j++)
         if (!load_refiner2(I, pf, j))
@@ -933,9 +947,19 @@ void prepare(Ctx &c, const float *in, int H, int W, const PilDev &ax,
     launch_ok("roma_prepare");
 }
 
+// kp > 0: the few-channel path, with col (h w x kp elements) as its
+// im2col buffer.
 void conv3(Ctx &c, const void *in, int cin, int h, int w, const void *wt,
-           const float *b, int cout, void *out)
+           const float *b, int cout, void *out, int kp, void *col)
 {
+    if (kp) {
+        Prof p(c.m->ocl, "vgg_conv3x3");
+        conv3x3_im2col_tc(c.st, (const __nv_bfloat16 *)in, h, w, cin, kp,
+                          (const __nv_bfloat16 *)wt, b, cout, ACTF_RELU, 0.0f, out,
+                          c.I->at, (__nv_bfloat16 *)col, c.m->ocl->sm_count);
+        launch_ok("vgg_conv3x3");
+        return;
+    }
     GemmArgs g = gemm_args(h * w, cout, 9 * cin);
     g.A = in;
     g.amode = 1;
@@ -967,7 +991,7 @@ void vgg(Ctx &c, int H, int W, int k, const bool need[ROMA_SCALES])
         for (int j = 0; j < vgg_blocks[blk]; j++, l++) {
             void *out = in == I->v_a ? I->v_b : I->v_a;
             conv3(c, in, I->vgg_cin[l], h, w, I->vgg_w[l], I->vgg_b[l],
-                  I->vgg_cout[l], out);
+                  I->vgg_cout[l], out, I->vgg_kp[l], out == I->v_a ? I->v_b : I->v_a);
             in = out;
         }
         if (need[s])
@@ -997,7 +1021,7 @@ void vgg2(Ctx &c, int H, int W, int k)
         for (int j = 0; j < vgg_blocks[blk]; j++, l++) {
             void *out = in == I->v_a ? I->v_b : I->v_a;
             conv3(c, in, I->vgg2_cin[l], h, w, I->vgg2_w[l], I->vgg2_b[l],
-                  I->vgg2_cout[l], out);
+                  I->vgg2_cout[l], out, I->vgg2_kp[l], out == I->v_a ? I->v_b : I->v_a);
             in = out;
         }
         gemm_nt(c, "vgg2_proj", h * w, I->ref2[r].feat, ref2_in[r], in, ref2_in[r],

@@ -75,6 +75,10 @@ CONVS = [
     (35, 70, 128, 256),
     (72, 136, 64, 128),
     (17, 9, 256, 64),
+    # few input channels: explicit im2col + tensor cores in bfloat16 mode
+    (40, 40, 3, 64),
+    (35, 70, 3, 64),
+    (9, 13, 5, 96),
 ]
 
 
