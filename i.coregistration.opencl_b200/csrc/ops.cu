@@ -108,7 +108,7 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
     g.slope = slope;
     g.ab = DT_F32;
     g.c = DT_F32;
-    if (o->precision == OPS_BF16 && transb && M >= 64 && N >= 64 && K >= 16 &&
+    if (o->precision == OPS_BF16 && transb && M >= 64 && N >= 1 && K >= 16 &&
         K % 8 == 0) {
         // Pack both operands to bfloat16 (row-major, K contiguous), then
         // the tensor-core tiles.

@@ -75,6 +75,11 @@ struct Smem {
 
 constexpr int EPI_WARPS = NTHREADS / 32 - 2;
 
+// TMEM columns per accumulator: BN, at least the 32 that one tcgen05.ld of
+// the epilogue reads (the allocation granule).
+template <int BN>
+constexpr int acc_cols() { return BN < 32 ? 32 : BN; }
+
 // Output tile t: first row (dense) or pixel origin (convolution) and first
 // column.
 struct Tile {
@@ -126,7 +131,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         mbar_fence_init();
     }
     if (warp == 1)
-        tmem_alloc(&s.tmem, 2 * BN);
+        tmem_alloc(&s.tmem, 2 * acc_cols<BN>());
     fence_before();
     __syncthreads();
     fence_after();
@@ -170,7 +175,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                 if (use > 0 && !mbar_wait(&s.acc_empty[buf], (use - 1) & 1, 4))
                     break;
                 fence_after();
-                const uint32_t acc = tmem + (uint32_t)(buf * BN);
+                const uint32_t acc = tmem + (uint32_t)(buf * acc_cols<BN>());
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int st = it % STAGES;
                     // TMA completion through the mbarrier orders the tile
@@ -215,7 +220,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             if (!__all_sync(0xffffffffu, mbar_wait_backoff(&s.acc_full[buf], use & 1, 3)))
                 break;
             fence_after();
-            const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
+            const uint32_t acc =
+                tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * acc_cols<BN>());
             for (int c0 = 32 * half; c0 < BN && tl.n0 + c0 < p.N; c0 += 64) {
                 float v[32];
                 tmem_ld32(acc + c0, v);
@@ -225,7 +231,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                 __syncwarp();
                 // Lane = column from here on.
                 const int col = tl.n0 + c0 + lane;
-                const bool cok = col < p.N;
+                const bool cok = col < p.N && c0 + lane < BN;
                 const float bias = cok && p.bias ? p.bias[col] : 0.0f;
 #pragma unroll 4
                 for (int rr = 0; rr < 32; rr++) {
@@ -253,7 +259,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     __syncthreads();
     if (warp == 1) {
         fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        tmem_dealloc(tmem, 2 * acc_cols<BN>());
     }
 }
 
@@ -444,7 +450,7 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         return false;
     if (g.biasrow && g.bias)
         return false;
-    if (g.M < 64 || g.N < 64 || g.K < 16)
+    if (g.M < 64 || g.N < 1 || g.K < 16)
         return false;
     if (((uintptr_t)g.A & 15) || ((uintptr_t)g.B & 15) ||
         (g.amode == 0 && (g.lda & 7)) || (g.ldb & 7))
@@ -458,6 +464,12 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         if (r256 * 256 * 100 <= r128 * 128 * 115)
             return tc::launch_tc<256, 4>(st, g, sm_count);
     }
+    if (g.N <= 16)
+        return tc::launch_tc<16, 8>(st, g, sm_count);
+    if (g.N <= 32)
+        return tc::launch_tc<32, 8>(st, g, sm_count);
+    if (g.N <= 64)
+        return tc::launch_tc<64, 8>(st, g, sm_count);
     return tc::launch_tc<128, 6>(st, g, sm_count);
 }
 

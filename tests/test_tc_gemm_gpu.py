@@ -26,6 +26,12 @@ SHAPES = [
     (1601, 1024, 4096, 0, True),   # DINOv2 fc2 with the residual
     (1600, 4097, 1024, 0, False),  # decoder to_out (odd N)
     (4900, 1136, 1136, 0, False),  # refiner 1 x 1 at 1/8
+    # narrow outputs: 16-, 32- and 64-column tiles
+    (5000, 32, 32, 2, False),      # refiner pointwise at full size (32 channels)
+    (746, 6, 32, 0, True),         # refiner heads (warp 2 + confidence 4)
+    (300, 48, 128, 1, False),
+    (130, 64, 64, 0, True),
+    (2000, 12, 64, 0, False),
 ]
 
 
