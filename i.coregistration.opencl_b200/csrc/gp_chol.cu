@@ -33,98 +33,135 @@ __global__ void gp_init_k(const float *K, int n, double noise, double *A)
     A[e] = (double)K[e] + (i == j ? noise : 0.0);
 }
 
-// Factor the b x b diagonal block at (j0, j0) in place (right-looking
-// within the block) and write its inverse into Linv (GP_NB x GP_NB, zero
-// padded beyond b).
-__global__ void __launch_bounds__(256)
+// Factor the b x b diagonal block at (j0, j0) in place and write its
+// inverse into Linv (GP_NB x GP_NB, zero padded beyond b). 256 threads
+// stage the block through shared memory with coalesced accesses (identity
+// beyond b); threads i < 64 then hold row i in registers. Per column
+// k the pivot's owner publishes sqrt(L[k][k]) and its reciprocal, the rows
+// below scale their entry k and publish it, and every row updates its own
+// entries k < j <= i: two block barriers per column. The inverse is
+// computed column by column (thread c solves L x = e_c) in axpy order, so
+// that each step's multiply-adds are independent.
+constexpr int GP_POTRF_THREADS = 256;
+
+__global__ void __launch_bounds__(GP_POTRF_THREADS)
 gp_potrf_inv_k(double *A, int n, int j0, int b, double *Linv, int *flag)
 {
-    // Dynamic shared memory: the factor and its inverse (2 x 64 x 65
-    // doubles, above the static 48 KB).
-    extern __shared__ double gp_smem[];
-    double(*L)[GP_NB + 1] = reinterpret_cast<double(*)[GP_NB + 1]>(gp_smem);
-    double(*X)[GP_NB + 1] = reinterpret_cast<double(*)[GP_NB + 1]>(gp_smem + GP_NB * (GP_NB + 1));
-    const int t = threadIdx.x;
-    for (int e = t; e < GP_NB * GP_NB; e += blockDim.x) {
-        const int i = e / GP_NB, j = e % GP_NB;
-        L[i][j] = i < b && j < b ? A[(long)(j0 + i) * n + j0 + j] : (i == j ? 1.0 : 0.0);
-    }
+    __shared__ double Ls[GP_NB][GP_NB + 1];
+    __shared__ double colk[GP_NB], rdiag[GP_NB];
+    __shared__ double piv_r;
+    const int t = threadIdx.x, i = t % GP_NB, rq = t / GP_NB;
+    constexpr int RSTEP = GP_POTRF_THREADS / GP_NB;
+#pragma unroll
+    for (int row = rq; row < GP_NB; row += RSTEP)
+        Ls[row][i] = row < b && i < b ? A[(long)(j0 + row) * n + j0 + i] : (row == i ? 1.0 : 0.0);
     __syncthreads();
-    for (int k = 0; k < b; k++) {
-        if (t == 0) {
-            double d = L[k][k];
-            if (!(d > 0)) {
+    const bool own = t < GP_NB;
+    double r[GP_NB];
+#pragma unroll
+    for (int j = 0; j < GP_NB; j++)
+        r[j] = Ls[i][j];
+#pragma unroll
+    for (int k = 0; k < GP_NB; k++) {
+        if (own && i == k) {
+            double d = r[k];
+            if (!(d > 0.0)) {
                 *flag = 1;
                 d = 1.0;
             }
-            L[k][k] = sqrt(d);
+            const double rc = rsqrt(d);
+            r[k] = d * rc;
+            piv_r = rc;
+            rdiag[k] = rc;
         }
         __syncthreads();
-        const double dk = L[k][k];
-        for (int i = k + 1 + t; i < b; i += blockDim.x)
-            L[i][k] /= dk;
-        __syncthreads();
-        // Trailing lower triangle of the block: 16 x 16 threads stepping
-        // over rows and columns (no division in the loop).
-        const int ty = t / 16, tx = t % 16;
-        for (int i = k + 1 + ty; i < b; i += 16) {
-            const double lik = L[i][k];
-            for (int j = k + 1 + tx; j <= i; j += 16)
-                L[i][j] -= lik * L[j][k];
+        if (own && i > k) {
+            r[k] *= piv_r;
+            colk[i] = r[k];
         }
         __syncthreads();
+        if (own && i > k) {
+            const double lik = r[k];
+#pragma unroll
+            for (int j = k + 1; j < GP_NB; j++)
+                if (j <= i)
+                    r[j] = fma(-lik, colk[j], r[j]);
+        }
     }
-    // Inverse of the lower-triangular factor, column c by thread c
-    // (forward substitution L x = e_c).
-    if (t < GP_NB) {
-        const int c = t;
-        for (int i = 0; i < GP_NB; i++) {
-            double s = i == c ? 1.0 : 0.0;
-            for (int k = c; k < i; k++)
-                s -= L[i][k] * X[k][c];
-            X[i][c] = i < c ? 0.0 : s / L[i][i];
-        }
+    if (own) {
+#pragma unroll
+        for (int j = 0; j < GP_NB; j++)
+            Ls[i][j] = j <= i ? r[j] : 0.0;
     }
     __syncthreads();
-    for (int e = t; e < GP_NB * GP_NB; e += blockDim.x) {
-        const int i = e / GP_NB, j = e % GP_NB;
-        Linv[e] = X[i][j];
-        if (i < b && j < b)
-            A[(long)(j0 + i) * n + j0 + j] = j <= i ? L[i][j] : 0.0;
+#pragma unroll
+    for (int row = rq; row < GP_NB; row += RSTEP)
+        if (row < b && i < b)
+            A[(long)(j0 + row) * n + j0 + i] = Ls[row][i];
+    if (!own)
+        return;
+    // Column c of the inverse: x = e_c; for k = c, c + 1, ...: x_k /= L_kk,
+    // then x_m -= L_mk x_k for m > k.
+    const int c = i;
+    double x[GP_NB];
+#pragma unroll
+    for (int m = 0; m < GP_NB; m++)
+        x[m] = m == c ? 1.0 : 0.0;
+#pragma unroll
+    for (int k = 0; k < GP_NB; k++) {
+        if (k >= c) {
+            x[k] *= rdiag[k];
+            const double xk = x[k];
+#pragma unroll
+            for (int m = k + 1; m < GP_NB; m++)
+                x[m] = fma(-Ls[m][k], xk, x[m]);
+        }
     }
+    double *li = Linv + c;
+#pragma unroll
+    for (int m = 0; m < GP_NB; m++)
+        li[(long)m * GP_NB] = x[m];
 }
 
 // C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
-// sak], B(k, n) = B[k sbk + n sbn]; 64 x 64 tiles, 16 k per step, 4 x 4
-// per thread; lower_only skips tiles and elements above the diagonal.
+// sak], B(k, n) = B[k sbk + n sbn]; 64 x 64 tiles, 4 x 4 per thread. Each
+// CTA stages 64-deep K panels of both operands (dynamic shared memory,
+// loads along each operand's unit-stride dimension) and runs the panel
+// with no barrier inside; the blocked Cholesky's products have K <= 64, so
+// one panel and two barriers per tile. lower_only skips tiles and elements
+// above the diagonal.
+constexpr int DG_T = 64, DG_K = 64;
+constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(double);
+
 __global__ void __launch_bounds__(256)
 dgemm_k(int M, int N, int K, const double *A, long sam, long sak, const double *B,
         long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
 {
-    __shared__ double As[16][64 + 1];
-    __shared__ double Bs[16][64 + 1];
+    extern __shared__ double dg_smem[];
+    double(*As)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem);
+    double(*Bs)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem + DG_K * (DG_T + 1));
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-    if (lower_only && n0 > m0 + 63)
+    const int m0 = blockIdx.y * DG_T, n0 = blockIdx.x * DG_T;
+    if (lower_only && n0 > m0 + DG_T - 1)
         return;
     double acc[4][4] = {};
-    // Tile loads with consecutive threads along each operand's unit-stride
-    // dimension (coalesced whichever way the operand is stored).
     const bool a_k = sak == 1, b_n = sbn == 1;
-    for (int k0 = 0; k0 < K; k0 += 16) {
-        for (int e = threadIdx.x; e < 64 * 16; e += 256) {
-            int r = a_k ? e / 16 : e % 64, k = a_k ? e % 16 : e / 64;
+    for (int k0 = 0; k0 < K; k0 += DG_K) {
+#pragma unroll 4
+        for (int e = threadIdx.x; e < DG_T * DG_K; e += 256) {
+            int r = a_k ? e / DG_K : e % DG_T, k = a_k ? e % DG_K : e / DG_T;
             int m = m0 + r, kk = k0 + k;
             As[k][r] = m < M && kk < K ? A[m * sam + kk * sak] : 0.0;
-            r = b_n ? e % 64 : e / 16;
-            k = b_n ? e / 64 : e % 16;
+            r = b_n ? e % DG_T : e / DG_K;
+            k = b_n ? e / DG_T : e % DG_K;
             const int nn = n0 + r;
             kk = k0 + k;
             Bs[k][r] = nn < N && kk < K ? B[kk * sbk + nn * sbn] : 0.0;
         }
         __syncthreads();
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
+        const int kc = K - k0 < DG_K ? K - k0 : DG_K;
+#pragma unroll 8
+        for (int k = 0; k < kc; k++) {
             double a[4], bb[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
@@ -161,8 +198,8 @@ static void dgemm(cudaStream_t st, int M, int N, int K, const double *A, long sa
 {
     if (M <= 0 || N <= 0 || K <= 0)
         return;
-    dgemm_k<<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, st>>>(M, N, K, A, sam, sak, B, sbk, sbn,
-                                                           C, ldc, sub, lower_only);
+    dgemm_k<<<dim3(cdiv(N, DG_T), cdiv(M, DG_T)), 256, DG_SMEM, st>>>(
+        M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, sub, lower_only);
 }
 
 __global__ void gp_load_rhs_k(const float *F, long e_n, double *Z)
@@ -197,15 +234,13 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
     double *T = Linv + (size_t)nb * GP_NB * GP_NB;
     const long nn = (long)n * n, nd = (long)n * d;
 
-    const size_t potrf_smem = 2 * GP_NB * (GP_NB + 1) * sizeof(double);
     static unsigned opted = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(opted >> (dev & 31) & 1)) {
-        if (!cuda_ok(cudaFuncSetAttribute(gp_potrf_inv_k,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)potrf_smem),
-                     "gp_potrf_inv_k"))
+        if (!cuda_ok(cudaFuncSetAttribute(dgemm_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)DG_SMEM),
+                     "dgemm_k"))
             return;
         opted |= 1u << (dev & 31);
     }
@@ -214,7 +249,7 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
         const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const int rest = n - j0 - b;
         double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        gp_potrf_inv_k<<<1, 256, potrf_smem, st>>>(A, n, j0, b, Li, flag);
+        gp_potrf_inv_k<<<1, GP_POTRF_THREADS, 0, st>>>(A, n, j0, b, Li, flag);
         if (rest > 0) {
             double *P = A + (long)(j0 + b) * n + j0;
             // Panel: L21 = A21 Linv^T, through a copy of A21.
