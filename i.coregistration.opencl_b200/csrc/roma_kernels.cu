@@ -14,6 +14,20 @@
 
 namespace coreg {
 
+// Packed float32 pair FMA of sm_100 (a * b + c on both lanes).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
+{
+    unsigned long long aa, bb, cc, dd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c.x), "f"(c.y));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dd) : "l"(aa), "l"(bb), "l"(cc));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
+    return d;
+}
+
+
 template <typename T>
 __device__ __forceinline__ float at_map(const T *p, long cs, long ps, int c,
                                         long i)
@@ -271,11 +285,86 @@ local_corr_k(const TI *f1, long cs1, long ps1, const TI *f2, long cs2,
     }
 }
 
+// The same for bfloat16 channels-last maps with C a multiple of 8 (the
+// model's layout): one warp per cell, whose scaled f1 row sits in shared
+// memory as float; the lanes split the (2r + 2)^2 positions (and, when
+// there are fewer than 32, the channels into G groups), each taking a whole
+// dot product with 16-byte loads of f2 and packed FMAs, then one shuffle
+// reduction over its G lanes.
+template <typename TO>
+__global__ void __launch_bounds__(128)
+local_corr_bf16_k(const __nv_bfloat16 *f1, long ps1, const __nv_bfloat16 *f2, long ps2, int C,
+                  int H, int W, int r, const float *flow, TO *out, long ocs, long ops, int coff)
+{
+    __shared__ __align__(16) float a_s[4][CORR_MAXC];
+    __shared__ float S[4][CORR_MAXPS * CORR_MAXPS];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const long n = (long)H * W;
+    const long i = (long)blockIdx.x * 4 + w;
+    if (i >= n)
+        return;
+    const int side = 2 * r + 1, ps = 2 * r + 2, P = ps * ps;
+    const float rc = rsqrtf((float)C);
+    const float ix = ((flow[i] + 1.0f) * W - 1.0f) * 0.5f;
+    const float iy = ((flow[n + i] + 1.0f) * H - 1.0f) * 0.5f;
+    const bool ok = isfinite(ix) && isfinite(iy);
+    const int x0 = ok ? (int)floorf(ix) : 0, y0 = ok ? (int)floorf(iy) : 0;
+    const float fx = ok ? ix - x0 : 0.0f, fy = ok ? iy - y0 : 0.0f;
+    const __nv_bfloat16 *a = f1 + i * ps1;
+    for (int c = lane; c < C; c += 32)
+        a_s[w][c] = __bfloat162float(a[c]) * rc;
+    __syncwarp();
+    // G lanes per position (a power of two), positions per round 32 / G.
+    const int G = P >= 32 ? 1 : (P > 8 ? 2 : (P > 4 ? 4 : 8));
+    const int per = 32 / G, g = lane % G;
+    const int nv = C / 8;
+    for (int e0 = 0; e0 < P; e0 += per) {
+        const int e = e0 + lane / G;
+        const int yy = y0 - r + e / ps, xx = x0 - r + e % ps;
+        float2 acc = make_float2(0.0f, 0.0f);
+        if (e < P && ok && xx >= 0 && xx < W && yy >= 0 && yy < H) {
+            const __nv_bfloat16 *b = f2 + ((long)yy * W + xx) * ps2;
+            for (int v = g; v < nv; v += G) {
+                const uint4 u = *(const uint4 *)(b + 8 * v);
+                const float4 p0 = *(const float4 *)&a_s[w][8 * v];
+                const float4 p1 = *(const float4 *)&a_s[w][8 * v + 4];
+                acc = fma2(make_float2(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u)),
+                           make_float2(p0.x, p0.y), acc);
+                acc = fma2(make_float2(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u)),
+                           make_float2(p0.z, p0.w), acc);
+                acc = fma2(make_float2(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u)),
+                           make_float2(p1.x, p1.y), acc);
+                acc = fma2(make_float2(__uint_as_float(u.w << 16), __uint_as_float(u.w & 0xffff0000u)),
+                           make_float2(p1.z, p1.w), acc);
+            }
+        }
+        float s = acc.x + acc.y;
+        for (int o = G / 2; o > 0; o /= 2)
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (g == 0 && e < P)
+            S[w][e] = s;
+    }
+    __syncwarp();
+    for (int k = lane; k < side * side; k += 32) {
+        const int e0 = (k / side) * ps + k % side, e1 = e0 + ps;
+        const float v = (1.0f - fy) * ((1.0f - fx) * S[w][e0] + fx * S[w][e0 + 1]) +
+                        fy * ((1.0f - fx) * S[w][e1] + fx * S[w][e1 + 1]);
+        stf(out + (long)(coff + k) * ocs + i * ops, v);
+    }
+}
+
 template <typename TI, typename TO>
 static void local_corr_t(cudaStream_t st, Map f1, Map f2, int C, int H, int W,
                          int r, const float *flow, MapOut out, int coff)
 {
     const long n = (long)H * W;
+    if (sizeof(TI) == 2 && f1.cs == 1 && f2.cs == 1 && C % 8 == 0 && f1.ps % 8 == 0 &&
+        f2.ps % 8 == 0 && ((uintptr_t)f1.p & 15) == 0 && ((uintptr_t)f2.p & 15) == 0) {
+        local_corr_bf16_k<TO><<<cdiv(n, 4), 128, 0, st>>>(
+            (const __nv_bfloat16 *)f1.p, f1.ps, (const __nv_bfloat16 *)f2.p, f2.ps, C, H, W, r,
+            flow, (TO *)out.p, out.cs, out.ps, coff);
+        return;
+    }
     local_corr_k<TI, TO><<<cdiv(n, 4), 128, 0, st>>>(
         (const TI *)f1.p, f1.cs, f1.ps, (const TI *)f2.p, f2.cs, f2.ps, C, H, W,
         r, flow, (TO *)out.p, out.cs, out.ps, coff);
@@ -542,19 +631,6 @@ dwconv5_tm_k(const TI *in, long ps, int C, int H, int W, const float *wt,
             stf(out + ((long)y * W + x) * ops + cg, fmaxf(acc, 0.0f));
         }
     }
-}
-
-// Packed float32 pair FMA of sm_100 (a * b + c on both lanes).
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
-{
-    unsigned long long aa, bb, cc, dd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c.x), "f"(c.y));
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dd) : "l"(aa), "l"(bb), "l"(cc));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
-    return d;
 }
 
 // bfloat16 channels-last depthwise 5 x 5 (+ bias, ReLU) for maps whose

@@ -154,3 +154,36 @@ extern "C" void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, c
     copy2d(st, o16, DT_BF16, C, fptr(out), DT_F32, C, n, C);
     launch_ok("roma_dwconv5_cl");
 }
+
+extern "C" void roma_local_corr_cl(struct ops *o, cl_mem f1, cl_mem f2, int C, int H, int W,
+                                   int r, cl_mem flow, cl_mem out)
+{
+    if (!bufs_ok({f1, f2, flow, out}, "roma_local_corr_cl"))
+        return;
+    const long n = (long)H * W;
+    if (n <= 0 || C <= 0 || !count_ok(n * C, "roma_local_corr_cl map"))
+        return;
+    const int side = 2 * r + 1;
+    cudaStream_t st = stream_of(o->ocl);
+    Prof p(o->ocl, "roma_local_corr");
+    if (o->precision != OPS_BF16) {
+        roma_local_corr_l(st, tm_map(fptr(f1), C), tm_map(fptr(f2), C), C, H, W, r, fptr(flow),
+                          tm_out(fptr(out), side * side), 0);
+        launch_ok("roma_local_corr_cl");
+        return;
+    }
+    const size_t half = ((size_t)n * C * 2 + 255) / 256 * 256;
+    if (2 * half > o->scratch16_bytes) {
+        ocl_release(&o->scratch16);
+        o->scratch16 = ocl_alloc(o->ocl, 2 * half, "local_corr operands");
+        o->scratch16_bytes = 2 * half;
+        if (pending())
+            return;
+    }
+    char *a16 = (char *)o->scratch16->ptr, *b16 = a16 + half;
+    copy2d(st, fptr(f1), DT_F32, C, a16, DT_BF16, C, n, C);
+    copy2d(st, fptr(f2), DT_F32, C, b16, DT_BF16, C, n, C);
+    roma_local_corr_l(st, tm_map(a16, C, DT_BF16), tm_map(b16, C, DT_BF16), C, H, W, r,
+                      fptr(flow), tm_out(fptr(out), side * side), 0);
+    launch_ok("roma_local_corr_cl");
+}

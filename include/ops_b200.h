@@ -48,6 +48,15 @@ void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm, int heads,
 void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem wt,
                      cl_mem bias, cl_mem out);
 
+/* Local correlation of channels-last (H, W, C) float32 maps f1 and f2 at
+ * the warp flow ((2, H, W) normalized coordinates, channel-major as in
+ * the models) into out, channels-last (H, W, (2r + 1)^2): roma_local_corr
+ * (roma_kernels.cl:153-192) on the models' layout. With o->precision
+ * OPS_BF16 the maps are rounded to bfloat16 and the model's bfloat16
+ * kernel runs (float32 arithmetic), as inside roma_match. */
+void roma_local_corr_cl(struct ops *o, cl_mem f1, cl_mem f2, int C, int H, int W, int r,
+                        cl_mem flow, cl_mem out);
+
 /* ops_gemm that allocates no device memory; it has no counterpart in the
  * reference. Same arguments, meaning and results as ops_gemm. With
  * o->precision OPS_BF16, ops_gemm packs the operands to bfloat16 in a
