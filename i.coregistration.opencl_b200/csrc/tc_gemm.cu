@@ -98,6 +98,16 @@ __device__ __forceinline__ Tile tile_of(const TcParams &p, int t, int tiles_m)
     return r;
 }
 
+// First k-block of tile t: the tiles that share an A row block or a B
+// column block start their K loops at different k-blocks, so that the
+// CTAs running at one time do not all request the same operand tile from
+// L2 at once. Only the order of the float32 sums changes.
+__device__ __forceinline__ int k_rotation(int t, int tiles_m, int nk)
+{
+    const int mt = t % tiles_m, nt = t / tiles_m;
+    return (int)(((unsigned)mt * 5u + (unsigned)nt * 3u) % (unsigned)nk);
+}
+
 // The activation (ACT, or -1 for the run-time one of p.act) and the output
 // type are template parameters: a run-time switch would inline every
 // activation's math into the unrolled epilogue loop, and that code size
@@ -144,7 +154,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const Tile tl = tile_of<BN>(p, t, tiles_m);
-                for (int kb = 0; kb < nk; kb++, it++) {
+                const int k_off = k_rotation(t, tiles_m, nk);
+                for (int kk = 0; kk < nk; kk++, it++) {
+                    const int kb = kk + k_off < nk ? kk + k_off : kk + k_off - nk;
                     const int st = it % STAGES;
                     if (it >= STAGES && !mbar_wait(&s.empty[st], ((it / STAGES) - 1) & 1, 1)) {
                         ok = false;
@@ -176,7 +188,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     break;
                 fence_after();
                 const uint32_t acc = tmem + (uint32_t)(buf * acc_cols<BN>());
-                for (int kb = 0; kb < nk; kb++, it++) {
+                for (int kk = 0; kk < nk; kk++, it++) {
                     const int st = it % STAGES;
                     // TMA completion through the mbarrier orders the tile
                     // for the tensor cores; no tcgen05 fence is needed here.
@@ -189,7 +201,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++)
                         mma_bf16(acc, da + 2 * k, db + 2 * k, idesc,
-                                 (kb > 0 || k > 0) ? 1u : 0u);
+                                 (kk > 0 || k > 0) ? 1u : 0u);
                     mma_commit(&s.empty[st]);
                 }
                 if (ok)
