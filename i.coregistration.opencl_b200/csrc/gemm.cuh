@@ -84,11 +84,12 @@ void resize_planes(cudaStream_t st, const float *in, int C, int h, int w,
                    float *out, int H, int W, int coff, int align, float scale);
 void transpose_f32(cudaStream_t st, const float *in, float *out, int B, int R,
                    int C);
-// Fused attention of a token-major qkv buffer (N x 3 Dm, bfloat16) into
-// out (N rows of ldo, bfloat16) on tcgen05 tensor cores (tc_attention.cu);
-// false when the head size (64 or 128) or alignment is not supported.
+// Fused attention of a token-major qkv buffer (nimg images of N x 3 Dm,
+// bfloat16, one after the other) into out (per image N rows of ldo,
+// bfloat16) on tcgen05 tensor cores (tc_attention.cu); false when the head
+// size (64 or 128) or alignment is not supported.
 bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
-                  long ldo, float scale);
+                  long ldo, float scale, int nimg = 1);
 // 3 x 3 / stride 1 / padding 1 convolution of a channels-last bfloat16
 // (H, W, C) map with few channels (9 C <= kp, kp a multiple of 16) on the
 // tensor cores: an explicit im2col into col (H W x kp bfloat16), then the

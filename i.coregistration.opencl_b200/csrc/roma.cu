@@ -803,11 +803,12 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
                                      (I->wm / ref_scale[s]) * as,
                                  "projected features");
     }
-    I->t_x = (float *)dmalloc(I, ntok * D * 4, "tokens");
-    I->t_n = dmalloc(I, ntok * D * as, "tokens");
-    I->t_qkv = dmalloc(I, ntok * 3 * D * as, "qkv");
-    I->t_o = dmalloc(I, ntok * D * as, "attention");
-    I->t_h = dmalloc(I, ntok * MLP_RATIO * D * as, "mlp");
+    // Token buffers for both images' DINOv2 tokens.
+    I->t_x = (float *)dmalloc(I, 2 * ntok * D * 4, "tokens");
+    I->t_n = dmalloc(I, 2 * ntok * D * as, "tokens");
+    I->t_qkv = dmalloc(I, 2 * ntok * 3 * D * as, "qkv");
+    I->t_o = dmalloc(I, 2 * ntok * D * as, "attention");
+    I->t_h = dmalloc(I, 2 * ntok * MLP_RATIO * D * as, "mlp");
     I->t_out = (float *)dmalloc(I, n16 * (NCLS + 1) * 4, "anchor logits");
     I->g_nx = (float *)dmalloc(I, n16 * 4, "norms");
     I->g_ny = (float *)dmalloc(I, n16 * 4, "norms");
@@ -1047,79 +1048,97 @@ __global__ void cls_pos_k(float *x, const float *cls, const float *pos, int D)
 
 // Pre-norm transformer block on t_x (N x D) in place (roma.c:697-713),
 // attention without the score matrix.
-void block(Ctx &c, const Block &b, int N, int D, int heads, float eps)
+// One pre-norm transformer block over nimg images of N tokens each, stored
+// one after the other in the token buffers: every linear layer runs once
+// over all nimg N rows, attention per image.
+void block(Ctx &c, const Block &b, int N, int nimg, int D, int heads, float eps)
 {
     roma_impl *I = c.I;
     const DType at = I->at;
+    const int rows = N * nimg;
     {
         Prof p(c.m->ocl, "layernorm");
-        layernorm_rows(c.st, I->t_x, I->t_n, at, b.n1g, b.n1b, N, D, eps,
+        layernorm_rows(c.st, I->t_x, I->t_n, at, b.n1g, b.n1b, rows, D, eps,
                        ACTF_NONE, 0.0f);
     }
-    gemm_nt(c, "qkv", N, 3 * D, D, I->t_n, D, at, b.qkv_w, b.qkv_b, I->t_qkv,
+    gemm_nt(c, "qkv", rows, 3 * D, D, I->t_n, D, at, b.qkv_w, b.qkv_b, I->t_qkv,
             3 * D, at, ACTF_NONE, false);
     {
         const int hd = D / heads;
         const size_t es = dsize(at);
+        const float scale = 1.0f / sqrtf((float)hd);
         Prof p(c.m->ocl, "attention");
-        if (at != DT_BF16 || !attention_tc(c.st, I->t_qkv, N, D, heads, I->t_o, D,
-                                           1.0f / sqrtf((float)hd)))
-            attention_l(c.st, I->t_qkv, 3 * D, (const char *)I->t_qkv + D * es, 3 * D,
-                        (const char *)I->t_qkv + 2 * D * es, 3 * D, I->t_o, D, N, N,
-                        heads, hd, 1.0f / sqrtf((float)hd), nullptr, at);
+        if (at != DT_BF16 || !attention_tc(c.st, I->t_qkv, N, D, heads, I->t_o, D, scale,
+                                           nimg))
+            for (int k = 0; k < nimg; k++) {
+                const char *q = (const char *)I->t_qkv + (size_t)k * N * 3 * D * es;
+                attention_l(c.st, q, 3 * D, q + D * es, 3 * D, q + 2 * D * es, 3 * D,
+                            (char *)I->t_o + (size_t)k * N * D * es, D, N, N, heads, hd,
+                            scale, nullptr, at);
+            }
         launch_ok("attention");
     }
-    gemm_nt(c, "proj", N, D, D, I->t_o, D, at, b.proj_w, b.proj_b, I->t_x, D,
+    gemm_nt(c, "proj", rows, D, D, I->t_o, D, at, b.proj_w, b.proj_b, I->t_x, D,
             DT_F32, ACTF_NONE, true);
     {
         Prof p(c.m->ocl, "layernorm");
-        layernorm_rows(c.st, I->t_x, I->t_n, at, b.n2g, b.n2b, N, D, eps,
+        layernorm_rows(c.st, I->t_x, I->t_n, at, b.n2g, b.n2b, rows, D, eps,
                        ACTF_NONE, 0.0f);
     }
-    gemm_nt(c, "fc1", N, MLP_RATIO * D, D, I->t_n, D, at, b.fc1_w, b.fc1_b,
+    gemm_nt(c, "fc1", rows, MLP_RATIO * D, D, I->t_n, D, at, b.fc1_w, b.fc1_b,
             I->t_h, MLP_RATIO * D, at, ACTF_GELU, false);
-    gemm_nt(c, "fc2", N, D, MLP_RATIO * D, I->t_h, MLP_RATIO * D, at, b.fc2_w,
+    gemm_nt(c, "fc2", rows, D, MLP_RATIO * D, I->t_h, MLP_RATIO * D, at, b.fc2_w,
             b.fc2_b, I->t_x, D, DT_F32, ACTF_NONE, true);
 }
 
 // DINOv2 on img (Cs x Cs, channels-last): the normalized patch tokens,
 // projected (decoder.proj.16), into P[0][k] (roma.c:717-738).
-void dino(Ctx &c, int k)
+// Patch and position embedding of image k's prepared input (img) into
+// token rows k ntok .. of t_x: class token, then the 14 x 14 patches.
+void dino_embed(Ctx &c, int k)
+{
+    roma_impl *I = c.I;
+    const int D = ROMA_VIT_DIM, N16 = I->n16;
+    float *x = I->t_x + (size_t)k * I->ntok * D;
+    GemmArgs g = gemm_args(N16, D, 3 * ROMA_PATCH * ROMA_PATCH);
+    g.A = I->img;
+    g.amode = 2;
+    g.cH = I->Cs;
+    g.cW = I->Cs;
+    g.cC = 3;
+    g.cP = ROMA_PATCH;
+    g.B = I->patch_w;
+    g.ldb = 3 * ROMA_PATCH * ROMA_PATCH;
+    g.transb = 1;
+    g.C = x + D;
+    g.ldc = D;
+    g.bias = I->patch_b;
+    g.R = I->pos + D;
+    g.ab = I->at;
+    g.c = DT_F32;
+    gemm_run(c.m->ocl, g, "patch_embed");
+    cls_pos_k<<<cdiv(D, 256), 256, 0, c.st>>>(x, I->cls, I->pos, D);
+}
+
+// DINOv2's 24 blocks over both images' tokens at once, the final norm, and
+// per image the dump point and the projection into P[0] (roma.c:717-738).
+void dino(Ctx &c)
 {
     roma_impl *I = c.I;
     const int D = ROMA_VIT_DIM, N16 = I->n16, NT = I->ntok;
-    {
-        // Patch embedding + position embedding (rows 1 ..), class token.
-        GemmArgs g = gemm_args(N16, D, 3 * ROMA_PATCH * ROMA_PATCH);
-        g.A = I->img;
-        g.amode = 2;
-        g.cH = I->Cs;
-        g.cW = I->Cs;
-        g.cC = 3;
-        g.cP = ROMA_PATCH;
-        g.B = I->patch_w;
-        g.ldb = 3 * ROMA_PATCH * ROMA_PATCH;
-        g.transb = 1;
-        g.C = I->t_x + D;
-        g.ldc = D;
-        g.bias = I->patch_b;
-        g.R = I->pos + D;
-        g.ab = I->at;
-        g.c = DT_F32;
-        gemm_run(c.m->ocl, g, "patch_embed");
-        cls_pos_k<<<cdiv(D, 256), 256, 0, c.st>>>(I->t_x, I->cls, I->pos, D);
-    }
     for (int i = 0; i < ROMA_VIT_DEPTH; i++)
-        block(c, I->vit[i], NT, D, VIT_HEADS, EPS_LN_VIT);
+        block(c, I->vit[i], NT, 2, D, VIT_HEADS, EPS_LN_VIT);
     {
         Prof p(c.m->ocl, "layernorm");
-        layernorm_rows(c.st, I->t_x, I->t_n, I->at, I->norm_g, I->norm_b, NT, D,
+        layernorm_rows(c.st, I->t_x, I->t_n, I->at, I->norm_g, I->norm_b, 2 * NT, D,
                        EPS_LN_VIT, ACTF_NONE, 0.0f);
     }
-    const void *tok = (const char *)I->t_n + (size_t)D * dsize(I->at);
-    dump_dev(c, k ? "dino_1" : "dino_0", tok, I->at, (size_t)N16 * D, N16, D);
-    gemm_nt(c, "proj16", N16, GP_DIM, D, tok, D, I->at, I->proj_w[0], I->proj_b[0],
-            I->P[0][k], GP_DIM, DT_F32, ACTF_NONE, false);
+    for (int k = 0; k < 2; k++) {
+        const void *tok = (const char *)I->t_n + ((size_t)k * NT + 1) * D * dsize(I->at);
+        dump_dev(c, k ? "dino_1" : "dino_0", tok, I->at, (size_t)N16 * D, N16, D);
+        gemm_nt(c, "proj16", N16, GP_DIM, D, tok, D, I->at, I->proj_w[0], I->proj_b[0],
+                I->P[0][k], GP_DIM, DT_F32, ACTF_NONE, false);
+    }
 }
 
 // Gaussian-process posterior of A's 1/16 features given B's and the
@@ -1181,7 +1200,7 @@ void decoder(Ctx &c)
     roma_impl *I = c.I;
     const int n = I->n16, D = ROMA_DEC_DIM;
     for (int i = 0; i < ROMA_DEC_DEPTH; i++)
-        block(c, I->dec[i], n, D, DEC_HEADS, EPS_LN_DEC);
+        block(c, I->dec[i], n, 1, D, DEC_HEADS, EPS_LN_DEC);
     const void *x = I->t_x;
     if (I->at != DT_F32) {
         copy2d(c.st, I->t_x, DT_F32, D, I->t_n, I->at, D, n, D);
@@ -1357,8 +1376,9 @@ void run_tile(Ctx &c, const float *inA, const float *inB)
         vgg(c, Cs, Cs, k, need);
         if (m->v2)
             vgg2(c, Cs, Cs, k);
-        dino(c, k);
+        dino_embed(c, k);
     }
+    dino(c);
     gp(c);
     decoder(c);
     if (c.dump) {

@@ -54,7 +54,7 @@ struct AttnSmem {
 struct AttnParams {
     int N, Dm;
     __nv_bfloat16 *out;
-    long ldo;
+    long ldo, out_img;  // output row pitch; elements between images
     float scale_log2;
 };
 
@@ -73,7 +73,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
     AttnSmem<D> &s = *reinterpret_cast<AttnSmem<D> *>(
         (void *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int q0 = blockIdx.x * BQ, h = blockIdx.y;
+    const int q0 = blockIdx.x * BQ, h = blockIdx.y, img = blockIdx.z;
     const int nblk = (p.N + BKV - 1) / BKV;
 
     if (threadIdx.x == 0) {
@@ -101,17 +101,17 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
             const uint32_t tile = BQ * 64 * 2;
             mbar_expect_tx(&s.q_full, KA * tile);
             for (int a = 0; a < KA; a++)
-                tma_load_2d(s.q[a], &map, &s.q_full, h * D + a * 64, q0);
+                tma_load_3d(s.q[a], &map, &s.q_full, h * D + a * 64, q0, img);
             for (int j = 0; j < nblk; j++) {
                 const int st = j % ST;
                 if (j >= ST && !mbar_wait(&s.kv_empty[st], ((j / ST) - 1) & 1, 11))
                     break;
                 mbar_expect_tx(&s.kv_full[st], 2 * KA * tile);
                 for (int a = 0; a < KA; a++) {
-                    tma_load_2d(s.k[st][a], &map, &s.kv_full[st], p.Dm + h * D + a * 64,
-                                j * BKV);
-                    tma_load_2d(s.v[st][a], &map, &s.kv_full[st], 2 * p.Dm + h * D + a * 64,
-                                j * BKV);
+                    tma_load_3d(s.k[st][a], &map, &s.kv_full[st], p.Dm + h * D + a * 64,
+                                j * BKV, img);
+                    tma_load_3d(s.v[st][a], &map, &s.kv_full[st], 2 * p.Dm + h * D + a * 64,
+                                j * BKV, img);
                 }
             }
         }
@@ -255,7 +255,8 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
                 float o[32];
                 tmem_ld32(tO + lane_off + 32 * c, o);
                 if (q < p.N) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long)q * p.ldo + h * D +
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + img * p.out_img +
+                                                           (long)q * p.ldo + h * D +
                                                            32 * c);
 #pragma unroll
                     for (int t = 0; t < 4; t++) {
@@ -280,22 +281,25 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
 
 template <int D>
 bool launch_attn(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
-                 long ldo, float scale)
+                 long ldo, float scale, int nimg)
 {
+    // (columns, rows, image) over nimg row blocks of N: boxes of 64
+    // columns x BQ rows of one image, zeros past its last row.
     CUtensorMap map;
-    if (!make_map_2d(&map, qkv, N, 3L * Dm, 3L * Dm, BQ))
+    if (!make_map_conv(&map, qkv, nimg, N, 3 * Dm, BQ, 1))
         return false;
     AttnParams p;
     p.N = N;
     p.Dm = Dm;
     p.out = (__nv_bfloat16 *)out;
     p.ldo = ldo;
+    p.out_img = (long)N * ldo;
     p.scale_log2 = scale * 1.4426950408889634f;
     const size_t smem = sizeof(AttnSmem<D>) + 1024;
     static unsigned done = 0;
     if (!smem_opt_in((const void *)tc_attn_kernel<D>, smem, &done))
         return false;
-    tc_attn_kernel<D><<<dim3(cdiv(N, BQ), heads), 192, smem, st>>>(map, p);
+    tc_attn_kernel<D><<<dim3(cdiv(N, BQ), heads, nimg), 192, smem, st>>>(map, p);
     return true;
 }
 
@@ -317,16 +321,16 @@ int gemm_status();
 // Attention of the fused qkv buffer on tensor cores; false (nothing
 // launched) when the head size or alignment is not supported.
 bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
-                  long ldo, float scale)
+                  long ldo, float scale, int nimg)
 {
     const int d = Dm / heads;
-    if (N < 1 || d * heads != Dm || ((uintptr_t)qkv & 15) || ((uintptr_t)out & 15) ||
+    if (N < 1 || nimg < 1 || nimg > 65535 || d * heads != Dm || ((uintptr_t)qkv & 15) || ((uintptr_t)out & 15) ||
         (ldo & 7) || (Dm & 63))
         return false;
     if (d == 64)
-        return tc::launch_attn<64>(st, qkv, N, Dm, heads, out, ldo, scale);
+        return tc::launch_attn<64>(st, qkv, N, Dm, heads, out, ldo, scale, nimg);
     if (d == 128)
-        return tc::launch_attn<128>(st, qkv, N, Dm, heads, out, ldo, scale);
+        return tc::launch_attn<128>(st, qkv, N, Dm, heads, out, ldo, scale, nimg);
     return false;
 }
 
