@@ -3,19 +3,24 @@
 // The Gaussian-process solve of RoMa on the device, in double precision:
 // X = (K + noise I)^-1 F for the n x n kernel matrix K (float, symmetric)
 // and the n x d basis F, by a blocked right-looking Cholesky factorization
-// and two blocked triangular solves. Replaces the reference's host
-// gp_solve (roma.c:772-836: Cholesky in double, L Z = F then L^T X = Z),
-// whose device round trip (roma.c:885-888) disappears.
+// L L^T = K + noise I and the two triangular solves L Z = F, L^T X = Z.
+// Replaces the reference's host gp_solve (roma.c:772-836: Cholesky in
+// double, then the two substitutions), whose device round trip
+// (roma.c:885-888) disappears.
 //
-// Blocks of NB = 64. One CTA factors each diagonal block in shared memory
-// and also inverts it (Linv); with the inverses every other step is a
-// double-precision GEMM:
-//   panel      L21 = A21 Linv^T
-//   trailing   A22 -= L21 L21^T (lower triangle)
-//   forward    Z_j = Linv_j F'_j, then F'_below -= L_below,j Z_j
-//   backward   X_j = Linv_j^T Z'_j, then Z'_above -= L_j,above^T X_j
+// Blocks of NB = 64. One CTA factors each diagonal block and inverts it
+// (Linv_j), so that every other step is a double-precision GEMM. The
+// working matrix A, the factor L and the right-hand sides F, Z, X live in
+// separate buffers, so no step multiplies in place:
+//   step j     L_jj, Linv_j           from A_jj
+//              L_below = A_below Linv_j^T,  Z_j = Linv_j F_j     (one launch)
+//              A_trail -= L_below L_below^T (lower),
+//              F_below -= L_below Z_j                            (one launch)
+//   backward   X_j = Linv_j^T Z_j,  then Z_above -= L_j,above^T X_j
 // A non-positive pivot sets *flag (the reference stops with "kernel not
 // positive definite"); the host reads it after the tile.
+
+#include <initializer_list>
 
 #include "common.cuh"
 
@@ -23,7 +28,7 @@ namespace coreg {
 
 #define GP_NB 64
 
-// A = K + noise I in double (lower triangle used).
+// A = K + noise I in double.
 __global__ void gp_init_k(const float *K, int n, double noise, double *A)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -33,130 +38,200 @@ __global__ void gp_init_k(const float *K, int n, double noise, double *A)
     A[e] = (double)K[e] + (i == j ? noise : 0.0);
 }
 
-// Factor the b x b diagonal block at (j0, j0) in place and write its
-// inverse into Linv (GP_NB x GP_NB, zero padded beyond b). 256 threads
-// stage the block through shared memory with coalesced accesses (identity
-// beyond b); threads i < 64 then hold row i in registers. Per column
-// k the pivot's owner publishes sqrt(L[k][k]) and its reciprocal, the rows
-// below scale their entry k and publish it, and every row updates its own
-// entries k < j <= i: two block barriers per column. The inverse is
-// computed column by column (thread c solves L x = e_c) in axpy order, so
-// that each step's multiply-adds are independent.
-constexpr int GP_POTRF_THREADS = 256;
+constexpr int GP_P = GP_NB + 1;  // shared-memory pitch (doubles)
 
-__global__ void __launch_bounds__(GP_POTRF_THREADS)
-gp_potrf_inv_k(double *A, int n, int j0, int b, double *Linv, int *flag)
+// One warp: factor the 32 x 32 symmetric positive definite block S (pitch
+// GP_P) in place into its lower Cholesky factor (upper part zeroed) and
+// write the factor's inverse into Inv (pitch GP_P). Lane i holds row i in
+// registers; each column's entries are broadcast with shuffles (no block
+// barrier). The inverse is computed column by column (lane c solves
+// L x = e_c) in axpy order from the stored factor.
+__device__ void chol32_inv(double *S, double *Inv, int *flag, int lane)
 {
-    __shared__ double Ls[GP_NB][GP_NB + 1];
-    __shared__ double colk[GP_NB], rdiag[GP_NB];
-    __shared__ double piv_r;
-    const int t = threadIdx.x, i = t % GP_NB, rq = t / GP_NB;
-    constexpr int RSTEP = GP_POTRF_THREADS / GP_NB;
+    double r[32];
 #pragma unroll
-    for (int row = rq; row < GP_NB; row += RSTEP)
-        Ls[row][i] = row < b && i < b ? A[(long)(j0 + row) * n + j0 + i] : (row == i ? 1.0 : 0.0);
-    __syncthreads();
-    const bool own = t < GP_NB;
-    double r[GP_NB];
+    for (int j = 0; j < 32; j++)
+        r[j] = S[lane * GP_P + j];
 #pragma unroll
-    for (int j = 0; j < GP_NB; j++)
-        r[j] = Ls[i][j];
-#pragma unroll
-    for (int k = 0; k < GP_NB; k++) {
-        if (own && i == k) {
-            double d = r[k];
-            if (!(d > 0.0)) {
+    for (int k = 0; k < 32; k++) {
+        double d = __shfl_sync(0xffffffffu, r[k], k);
+        if (!(d > 0.0)) {
+            if (lane == 0)
                 *flag = 1;
-                d = 1.0;
-            }
-            const double rc = rsqrt(d);
+            d = 1.0;
+        }
+        const double rc = rsqrt(d);
+        if (lane == k)
             r[k] = d * rc;
-            piv_r = rc;
-            rdiag[k] = rc;
-        }
-        __syncthreads();
-        if (own && i > k) {
-            r[k] *= piv_r;
-            colk[i] = r[k];
-        }
-        __syncthreads();
-        if (own && i > k) {
-            const double lik = r[k];
+        else if (lane > k)
+            r[k] *= rc;
 #pragma unroll
-            for (int j = k + 1; j < GP_NB; j++)
-                if (j <= i)
-                    r[j] = fma(-lik, colk[j], r[j]);
+        for (int j = k + 1; j < 32; j++) {
+            const double ljk = __shfl_sync(0xffffffffu, r[k], j);
+            if (lane >= j)
+                r[j] = fma(-r[k], ljk, r[j]);
         }
     }
-    if (own) {
 #pragma unroll
-        for (int j = 0; j < GP_NB; j++)
-            Ls[i][j] = j <= i ? r[j] : 0.0;
-    }
-    __syncthreads();
+    for (int j = 0; j < 32; j++)
+        S[lane * GP_P + j] = j <= lane ? r[j] : 0.0;
+    __syncwarp();
+    const double my_rd = 1.0 / S[lane * GP_P + lane];
+    double x[32];
 #pragma unroll
-    for (int row = rq; row < GP_NB; row += RSTEP)
-        if (row < b && i < b)
-            A[(long)(j0 + row) * n + j0 + i] = Ls[row][i];
-    if (!own)
-        return;
-    // Column c of the inverse: x = e_c; for k = c, c + 1, ...: x_k /= L_kk,
-    // then x_m -= L_mk x_k for m > k.
-    const int c = i;
-    double x[GP_NB];
+    for (int m = 0; m < 32; m++)
+        x[m] = m == lane ? 1.0 : 0.0;
 #pragma unroll
-    for (int m = 0; m < GP_NB; m++)
-        x[m] = m == c ? 1.0 : 0.0;
-#pragma unroll
-    for (int k = 0; k < GP_NB; k++) {
-        if (k >= c) {
-            x[k] *= rdiag[k];
+    for (int k = 0; k < 32; k++) {
+        const double rdk = __shfl_sync(0xffffffffu, my_rd, k);
+        if (k >= lane) {
+            x[k] *= rdk;
             const double xk = x[k];
 #pragma unroll
-            for (int m = k + 1; m < GP_NB; m++)
-                x[m] = fma(-Ls[m][k], xk, x[m]);
+            for (int m = k + 1; m < 32; m++)
+                x[m] = fma(-S[m * GP_P + k], xk, x[m]);
         }
     }
-    double *li = Linv + c;
 #pragma unroll
-    for (int m = 0; m < GP_NB; m++)
-        li[(long)m * GP_NB] = x[m];
+    for (int m = 0; m < 32; m++)
+        Inv[m * GP_P + lane] = x[m];
+    __syncwarp();
 }
 
+// out = sum_k X(i, k) Y(k, j) for output row i = t / 8, columns (t % 8) 4
+// .. + 3 of a 32 x 32 product, X(i, k) = X[i xs + k xk], Y(k, j) = Y[k ys +
+// j yj]; 256 threads. Kept in registers until the caller's barrier.
+__device__ __forceinline__ void mm32(const double *X, int xs, int xk, const double *Y, int ys,
+                                     int yj, double out[4], int t)
+{
+    const int i = t / 8, j0 = (t % 8) * 4;
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        out[q] = 0.0;
+#pragma unroll 8
+    for (int k = 0; k < 32; k++) {
+        const double x = X[i * xs + k * xk];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            out[q] = fma(x, Y[k * ys + (j0 + q) * yj], out[q]);
+    }
+}
+
+// Factor the b x b diagonal block of A at (j0, j0) (b <= 64; identity beyond
+// b) as 2 x 2 blocks of 32: L11 and its inverse by one warp, L21 =
+// A21 L11^-T, A22 -= L21 L21^T, L22 and its inverse by one warp, and
+// Inv21 = -Inv22 L21 Inv11. Writes the lower factor into L (pitch n) and
+// the 64 x 64 inverse into Linv.
+__global__ void __launch_bounds__(256)
+gp_potrf_inv_k(const double *A, double *L, int n, int j0, int b, double *Linv, int *flag)
+{
+    extern __shared__ double gp_smem[];
+    double *M = gp_smem;                  // 64 x GP_P: the block, then L
+    double *Iv = gp_smem + GP_NB * GP_P;  // 64 x GP_P: the inverse
+    double *T = Iv + GP_NB * GP_P;        // 32 x GP_P: L21 Inv11
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+    // Staging loops unrolled, so that each thread's loads are all in flight.
+#pragma unroll
+    for (int e = t; e < GP_NB * GP_NB; e += 256) {
+        const int i = e / GP_NB, j = e % GP_NB;
+        M[i * GP_P + j] = i < b && j < b ? A[(long)(j0 + i) * n + j0 + j] : (i == j ? 1.0 : 0.0);
+        Iv[i * GP_P + j] = 0.0;
+    }
+    __syncthreads();
+    if (warp == 0)
+        chol32_inv(M, Iv, flag, lane);
+    __syncthreads();
+    double o[4];
+    const int oi = t / 8, oj = (t % 8) * 4;
+    // L21 = A21 Inv11^T.
+    mm32(M + 32 * GP_P, GP_P, 1, Iv, 1, GP_P, o, t);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        M[(32 + oi) * GP_P + oj + q] = o[q];
+    __syncthreads();
+    // A22 -= L21 L21^T.
+    mm32(M + 32 * GP_P, GP_P, 1, M + 32 * GP_P, 1, GP_P, o, t);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        M[(32 + oi) * GP_P + 32 + oj + q] -= o[q];
+    __syncthreads();
+    if (warp == 0)
+        chol32_inv(M + 32 * GP_P + 32, Iv + 32 * GP_P + 32, flag, lane);
+    // T = L21 Inv11 (reads only L21 and Inv11, untouched by warp 0 now).
+    mm32(M + 32 * GP_P, GP_P, 1, Iv, GP_P, 1, o, t);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        T[oi * GP_P + oj + q] = o[q];
+    __syncthreads();
+    // Inv21 = -Inv22 T.
+    mm32(Iv + 32 * GP_P + 32, GP_P, 1, T, GP_P, 1, o, t);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        Iv[(32 + oi) * GP_P + oj + q] = -o[q];
+    __syncthreads();
+#pragma unroll
+    for (int e = t; e < GP_NB * GP_NB; e += 256) {
+        const int i = e / GP_NB, j = e % GP_NB;
+        Linv[e] = Iv[i * GP_P + j];
+        if (i < b && j < b)
+            L[(long)(j0 + i) * n + j0 + j] = j <= i ? M[i * GP_P + j] : 0.0;
+    }
+}
+
+constexpr size_t GP_POTRF_SMEM = (2 * GP_NB + 32) * GP_P * sizeof(double);
+
 // C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
-// sak], B(k, n) = B[k sbk + n sbn]; 64 x 64 tiles, 4 x 4 per thread. Each
-// CTA stages 64-deep K panels of both operands (dynamic shared memory,
-// loads along each operand's unit-stride dimension) and runs the panel
-// with no barrier inside; the blocked Cholesky's products have K <= 64, so
-// one panel and two barriers per tile. lower_only skips tiles and elements
+// sak], B(k, n) = B[k sbk + n sbn]; lower_only skips tiles and elements
 // above the diagonal.
+struct DgProb {
+    int M, N, K;
+    const double *A;
+    long sam, sak;
+    const double *B;
+    long sbk, sbn;
+    double *C;
+    long ldc;
+    int sub, lower_only;
+};
+
+// Up to two independent products per launch (blockIdx.z).
+struct DgBatch {
+    DgProb p[2];
+};
+
+// 64 x 64 tiles, 4 x 4 per thread. Each CTA stages 64-deep K panels of
+// both operands (dynamic shared memory, loads along each operand's
+// unit-stride dimension) and runs the panel with no barrier inside; the
+// blocked Cholesky's products have K <= 64, so one panel and two barriers
+// per tile.
 constexpr int DG_T = 64, DG_K = 64;
 constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(double);
 
-__global__ void __launch_bounds__(256)
-dgemm_k(int M, int N, int K, const double *A, long sam, long sak, const double *B,
-        long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
+__global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
 {
     extern __shared__ double dg_smem[];
+    const DgProb &q = batch.p[blockIdx.z];
     double(*As)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem);
     double(*Bs)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem + DG_K * (DG_T + 1));
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const int m0 = blockIdx.y * DG_T, n0 = blockIdx.x * DG_T;
-    if (lower_only && n0 > m0 + DG_T - 1)
+    const int M = q.M, N = q.N, K = q.K;
+    if (m0 >= M || n0 >= N || (q.lower_only && n0 > m0 + DG_T - 1))
         return;
     double acc[4][4] = {};
-    const bool a_k = sak == 1, b_n = sbn == 1;
+    const bool a_k = q.sak == 1, b_n = q.sbn == 1;
     for (int k0 = 0; k0 < K; k0 += DG_K) {
 #pragma unroll 4
         for (int e = threadIdx.x; e < DG_T * DG_K; e += 256) {
             int r = a_k ? e / DG_K : e % DG_T, k = a_k ? e % DG_K : e / DG_T;
             int m = m0 + r, kk = k0 + k;
-            As[k][r] = m < M && kk < K ? A[m * sam + kk * sak] : 0.0;
+            As[k][r] = m < M && kk < K ? q.A[m * q.sam + kk * q.sak] : 0.0;
             r = b_n ? e % DG_T : e / DG_K;
             k = b_n ? e / DG_T : e % DG_K;
             const int nn = n0 + r;
             kk = k0 + k;
-            Bs[k][r] = nn < N && kk < K ? B[kk * sbk + nn * sbn] : 0.0;
+            Bs[k][r] = nn < N && kk < K ? q.B[kk * q.sbk + nn * q.sbn] : 0.0;
         }
         __syncthreads();
         const int kc = K - k0 < DG_K ? K - k0 : DG_K;
@@ -184,22 +259,35 @@ dgemm_k(int M, int N, int K, const double *A, long sam, long sak, const double *
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int nn = n0 + tx + 16 * j;
-            if (nn < N && (!lower_only || nn <= m)) {
-                double *c = C + (long)m * ldc + nn;
-                *c = sub ? *c - acc[i][j] : acc[i][j];
+            if (nn < N && (!q.lower_only || nn <= m)) {
+                double *c = q.C + (long)m * q.ldc + nn;
+                *c = q.sub ? *c - acc[i][j] : acc[i][j];
             }
         }
     }
 }
 
-static void dgemm(cudaStream_t st, int M, int N, int K, const double *A, long sam, long sak,
-                  const double *B, long sbk, long sbn, double *C, long ldc, int sub,
-                  int lower_only)
+static DgProb prob(int M, int N, int K, const double *A, long sam, long sak, const double *B,
+                   long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
 {
-    if (M <= 0 || N <= 0 || K <= 0)
-        return;
-    dgemm_k<<<dim3(cdiv(N, DG_T), cdiv(M, DG_T)), 256, DG_SMEM, st>>>(
-        M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, sub, lower_only);
+    DgProb p = {M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, sub, lower_only};
+    return p;
+}
+
+// One launch for the non-empty products among p0 and p1 (either may be
+// NULL).
+static void dgemm2(cudaStream_t st, const DgProb *p0, const DgProb *p1)
+{
+    DgBatch b;
+    int count = 0, gx = 0, gy = 0;
+    for (const DgProb *p : {p0, p1})
+        if (p && p->M > 0 && p->N > 0 && p->K > 0) {
+            b.p[count++] = *p;
+            gx = max(gx, (int)cdiv(p->N, DG_T));
+            gy = max(gy, (int)cdiv(p->M, DG_T));
+        }
+    if (count)
+        dgemm_k<<<dim3(gx, gy, count), 256, DG_SMEM, st>>>(b);
 }
 
 __global__ void gp_load_rhs_k(const float *F, long e_n, double *Z)
@@ -216,76 +304,73 @@ __global__ void gp_store_k(const double *Z, long e_n, float *X)
         X[e] = (float)Z[e];
 }
 
-// Work: n n + n d doubles (A, Z), cdiv(n, 64) 64 x 64 doubles (inverses)
-// and 64 max(n, d) doubles (the panel or right-hand-side block copy).
+// Work: A and L (n x n each), F, Z, X (n x d each) and cdiv(n, 64) 64 x 64
+// inverses, in doubles.
 size_t gp_work_doubles(int n, int d)
 {
     const size_t nb = (size_t)cdiv(n, GP_NB);
-    const size_t w = (size_t)(n > d ? n : d);
-    return (size_t)n * n + (size_t)n * d + nb * GP_NB * GP_NB + GP_NB * w;
+    return 2 * (size_t)n * n + 3 * (size_t)n * d + nb * GP_NB * GP_NB;
 }
 
-void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,
-                  double noise, float *X, double *work, int *flag)
+static bool opt_in(const void *fn, size_t bytes, unsigned *mask)
 {
-    const int nb = cdiv(n, GP_NB);
-    double *A = work, *Z = A + (size_t)n * n;
-    double *Linv = Z + (size_t)n * d;
-    double *T = Linv + (size_t)nb * GP_NB * GP_NB;
-    const long nn = (long)n * n, nd = (long)n * d;
-
-    static unsigned opted = 0;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(opted >> (dev & 31) & 1)) {
-        if (!cuda_ok(cudaFuncSetAttribute(dgemm_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)DG_SMEM),
-                     "dgemm_k"))
-            return;
-        opted |= 1u << (dev & 31);
-    }
+    if (*mask >> (dev & 31) & 1)
+        return true;
+    if (!cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)bytes),
+                 "gp kernels"))
+        return false;
+    *mask |= 1u << (dev & 31);
+    return true;
+}
+
+void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int d,
+                  double noise, float *X_out, double *work, int *flag)
+{
+    const int nb = cdiv(n, GP_NB);
+    double *A = work, *L = A + (size_t)n * n;
+    double *F = L + (size_t)n * n, *Z = F + (size_t)n * d, *X = Z + (size_t)n * d;
+    double *Linv = X + (size_t)n * d;
+    const long nn = (long)n * n, nd = (long)n * d;
+    static unsigned opted_g = 0, opted_p = 0;
+    if (!opt_in((const void *)dgemm_k, DG_SMEM, &opted_g) ||
+        !opt_in((const void *)gp_potrf_inv_k, GP_POTRF_SMEM, &opted_p))
+        return;
+
     gp_init_k<<<cdiv(nn, 256), 256, 0, st>>>(K, n, noise, A);
+    gp_load_rhs_k<<<cdiv(nd, 256), 256, 0, st>>>(F_in, nd, F);
     for (int j = 0; j < nb; j++) {
         const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const int rest = n - j0 - b;
         double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        gp_potrf_inv_k<<<1, GP_POTRF_THREADS, 0, st>>>(A, n, j0, b, Li, flag);
-        if (rest > 0) {
-            double *P = A + (long)(j0 + b) * n + j0;
-            // Panel: L21 = A21 Linv^T, through a copy of A21.
-            cudaMemcpy2DAsync(T, GP_NB * sizeof(double), P, n * sizeof(double),
-                              b * sizeof(double), rest, cudaMemcpyDeviceToDevice, st);
-            dgemm(st, rest, b, b, T, GP_NB, 1, Li, 1, GP_NB, P, n, 0, 0);
-            // Trailing lower triangle -= L21 L21^T.
-            dgemm(st, rest, rest, b, P, n, 1, P, 1, n, A + (long)(j0 + b) * n + j0 + b, n, 1,
-                  1);
-        }
+        gp_potrf_inv_k<<<1, 256, GP_POTRF_SMEM, st>>>(A, L, n, j0, b, Li, flag);
+        const long below = (long)(j0 + b) * n + j0;
+        // L_below = A_below Linv^T;  Z_j = Linv F_j.
+        const DgProb panel = prob(rest, b, b, A + below, n, 1, Li, 1, GP_NB, L + below, n, 0, 0);
+        const DgProb zj = prob(b, d, b, Li, GP_NB, 1, F + (long)j0 * d, d, 1, Z + (long)j0 * d,
+                               d, 0, 0);
+        dgemm2(st, &panel, &zj);
+        // A_trail -= L_below L_below^T (lower);  F_below -= L_below Z_j.
+        const DgProb trail = prob(rest, rest, b, L + below, n, 1, L + below, 1, n,
+                                  A + (long)(j0 + b) * n + j0 + b, n, 1, 1);
+        const DgProb fb = prob(rest, d, b, L + below, n, 1, Z + (long)j0 * d, d, 1,
+                               F + (long)(j0 + b) * d, d, 1, 0);
+        dgemm2(st, &trail, &fb);
     }
-    gp_load_rhs_k<<<cdiv(nd, 256), 256, 0, st>>>(F, nd, Z);
-    // L Z = F: Z_j = Linv_j F'_j, then the rows below.
-    for (int j = 0; j < nb; j++) {
-        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
-        const int rest = n - j0 - b;
-        const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        cudaMemcpyAsync(T, Z + (long)j0 * d, (size_t)b * d * sizeof(double),
-                        cudaMemcpyDeviceToDevice, st);
-        dgemm(st, b, d, b, Li, GP_NB, 1, T, d, 1, Z + (long)j0 * d, d, 0, 0);
-        if (rest > 0)
-            dgemm(st, rest, d, b, A + (long)(j0 + b) * n + j0, n, 1, Z + (long)j0 * d, d, 1,
-                  Z + (long)(j0 + b) * d, d, 1, 0);
-    }
-    // L^T X = Z: X_j = Linv_j^T Z'_j from the last block up, then
-    // Z'_above -= L_j,above^T X_j.
+    // L^T X = Z from the last block up.
     for (int j = nb - 1; j >= 0; j--) {
         const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        cudaMemcpyAsync(T, Z + (long)j0 * d, (size_t)b * d * sizeof(double),
-                        cudaMemcpyDeviceToDevice, st);
-        dgemm(st, b, d, b, Li, 1, GP_NB, T, d, 1, Z + (long)j0 * d, d, 0, 0);
-        if (j0 > 0)
-            dgemm(st, j0, d, b, A + (long)j0 * n, 1, n, Z + (long)j0 * d, d, 1, Z, d, 1, 0);
+        const DgProb xj = prob(b, d, b, Li, 1, GP_NB, Z + (long)j0 * d, d, 1, X + (long)j0 * d,
+                               d, 0, 0);
+        dgemm2(st, &xj, nullptr);
+        const DgProb up =
+            prob(j0, d, b, L + (long)j0 * n, 1, n, X + (long)j0 * d, d, 1, Z, d, 1, 0);
+        dgemm2(st, &up, nullptr);
     }
-    gp_store_k<<<cdiv(nd, 256), 256, 0, st>>>(Z, nd, X);
+    gp_store_k<<<cdiv(nd, 256), 256, 0, st>>>(X, nd, X_out);
 }
 
 }  // namespace coreg
