@@ -312,70 +312,99 @@ def gpu_arm(args, rank, world, local):
         synth.write_roma_weights(CACHE / "weights", 0)
     barrier(world)
     main, dino, v2 = synth.write_roma_weights(CACHE / "weights", 0)
-    dev = coreg.Device(local, precision=prec)
+    # S tile pipelines per GPU, each its own backend (stream), model and
+    # tile graph: tiles are independent, and a second pipeline fills the
+    # SMs that one tile's latency-bound stages (the Gaussian-process chain,
+    # launch gaps, last waves) leave idle.
+    S = max(1, args.streams)
+    devs = [coreg.Device(local, precision=prec) for _ in range(S)]
+    dev = devs[0]
     lib = dev.lib
-    net = Roma(dev, main, dino, v2, H=H, W=W, coarse=COARSE)
+    nets = [Roma(d, main, dino, v2, H=H, W=W, coarse=COARSE) for d in devs]
+    net = nets[0]
     ntiles = args.tiles
     tiles = make_tiles([rank * ntiles + i for i in range(ntiles)])
     hw3 = 3 * H * W
-    # Device-resident tiles, and the graph's fixed input buffers.
+    # Device-resident tiles, and each graph's fixed input buffers.
     dtiles = [(dev.upload(a), dev.upload(b)) for a, b in tiles]
-    inA, inB = dev.alloc(hw3 * 4), dev.alloc(hw3 * 4)
+    ins = [(d.alloc(hw3 * 4), d.alloc(hw3 * 4)) for d in devs]
 
-    def load_tile(i):
+    def load_tile(s, i):
         a, b = dtiles[i % ntiles]
-        lib.ocl_copy(dev.ocl_p, a.handle, 0, inA.handle, 0, hw3 * 4)
-        lib.ocl_copy(dev.ocl_p, b.handle, 0, inB.handle, 0, hw3 * 4)
+        lib.ocl_copy(devs[s].ocl_p, a.handle, 0, ins[s][0].handle, 0, hw3 * 4)
+        lib.ocl_copy(devs[s].ocl_p, b.handle, 0, ins[s][1].handle, 0, hw3 * 4)
 
-    kernels = net.graph_build(inA.ptr, inB.ptr)
-    for i in range(args.warmup):
-        load_tile(i)
-        net.graph_launch()
-    dev.finish()
-    net.sync()
+    kernels = [nets[s].graph_build(ins[s][0].ptr, ins[s][1].ptr) for s in range(S)]
+    for i in range(max(args.warmup, S)):
+        load_tile(i % S, i)
+        nets[i % S].graph_launch()
+    for d, n_ in zip(devs, nets):
+        d.finish()
+        n_.sync()
     barrier(world)
     with Clocks(local) as clk:
         lib.ocl_timer_start(dev.ocl_p)
+        for s in range(1, S):
+            lib.ocl_join(devs[s].ocl_p, dev.ocl_p)
         for i in range(args.steps):
-            load_tile(i)
-            net.graph_launch()
+            load_tile(i % S, i)
+            nets[i % S].graph_launch()
+        for s in range(1, S):
+            lib.ocl_join(dev.ocl_p, devs[s].ocl_p)
         ms = lib.ocl_timer_stop(dev.ocl_p)
     coreg.check(lib)
-    net.sync()
+    for n_ in nets:
+        n_.sync()
     ms_max = allmax(world, ms)
     value = world * args.steps / (ms_max / 1000.0)
 
     # End to end through the public API: host (pinned) images in, host
-    # results out, per step.
+    # results out, per step; one host thread per pipeline (roma_match is
+    # synchronous), wall clock.
+    import ctypes
+    import threading
+
     pin = []
     for a, b in tiles:
         pa = lib.coreg_host_alloc(hw3 * 4)
         pb = lib.coreg_host_alloc(hw3 * 4)
-        import ctypes
-
         ctypes.memmove(pa, a.ctypes.data, hw3 * 4)
         ctypes.memmove(pb, b.ctypes.data, hw3 * 4)
         pin.append((pa, pb))
-    for i in range(min(2, args.warmup)):
-        pa, pb = pin[i % ntiles]
-        lib.roma_match(net.mp, pa, pb, None, 1)
-    coreg.check(lib)
+    errors = []
+
+    def e2e_worker(s, count):
+        try:
+            for j in range(count):
+                pa, pb = pin[(s + S * j) % ntiles]
+                lib.roma_match(nets[s].mp, pa, pb, None, 1)
+            coreg.check(lib)
+        except Exception as e:  # reported on the main thread
+            errors.append(e)
+
+    def e2e_run(count_per):
+        th = [threading.Thread(target=e2e_worker, args=(s, count_per)) for s in range(S)]
+        for t_ in th:
+            t_.start()
+        for t_ in th:
+            t_.join()
+        if errors:
+            raise errors[0]
+
+    e2e_run(1)
     barrier(world)
-    e2e_steps = max(1, args.steps // 2)
-    lib.ocl_timer_start(dev.ocl_p)
-    for i in range(e2e_steps):
-        pa, pb = pin[i % ntiles]
-        lib.roma_match(net.mp, pa, pb, None, 1)
-    e2e_ms = lib.ocl_timer_stop(dev.ocl_p)
-    coreg.check(lib)
+    e2e_per = max(1, args.steps // (2 * S))
+    t0 = time.perf_counter()
+    e2e_run(e2e_per)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0
     e2e_max = allmax(world, e2e_ms)
-    e2e_value = world * e2e_steps / (e2e_max / 1000.0)
+    e2e_value = world * S * e2e_per / (e2e_max / 1000.0)
     for pa, pb in pin:
         lib.coreg_host_free(pa)
         lib.coreg_host_free(pb)
 
     # Roofline of the dominant kernel, from one profiled tile.
-    prof = profile_step(lib, dev, net, inA.ptr, inB.ptr)
+    prof = profile_step(lib, dev, net, ins[0][0].ptr, ins[0][1].ptr)
     fl, by = work_model(es=2 if prec else 4)
     hbm, bf16, peak_kind = peaks()
     # The dominant profiled operation that has a work model.
@@ -418,13 +447,15 @@ def gpu_arm(args, rank, world, local):
             "config": {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 "
                                    "(BASELINE configs[3])",
                        "tile_px": H, "coarse_px": COARSE, "tiles_per_rank": ntiles,
-                       "parallelism": f"tiles sharded over {world} GPU(s)",
+                       "pipelines_per_gpu": S,
+                       "parallelism": f"tiles sharded over {world} GPU(s), {S} concurrent "
+                                      "tile pipelines (streams) per GPU",
                        "l2": "no flush: every step streams the weights and activations "
                              "(> 1 GB) through the 126 MB L2"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * hw3 * 4,
                     "d2h_bytes_per_step": 4 * H * W * 4,
                     "api": "roma_match (host images in pinned memory, host results)"},
-            "gpu_launches": kernels * args.steps,
+            "gpu_launches": sum(kernels[i % S] for i in range(args.steps)),
             "roofline": roof,
             "path_tflops": flops_pair / (ms_max / args.steps / 1000.0) / 1e12,
             "time_shares": {k: round(v, 4) for k, v in shares},
@@ -432,8 +463,9 @@ def gpu_arm(args, rank, world, local):
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
-    net.close()
-    dev.close()
+    for n_, d in zip(nets, devs):
+        n_.close()
+        d.close()
 
 
 def main():
@@ -445,6 +477,8 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--tiles", type=int, default=4, help="distinct tile pairs per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--streams", type=int, default=3,
+                    help="concurrent tile pipelines (streams, models) per GPU")
     args = ap.parse_args()
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":

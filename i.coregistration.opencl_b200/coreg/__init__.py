@@ -95,6 +95,7 @@ SIGNATURES = {
     "ocl_copy": (None, [C.POINTER(OclBackend), P, SZ, P, SZ, SZ]),
     "ocl_zero": (None, [C.POINTER(OclBackend), P, SZ, SZ]),
     "ocl_finish": (None, [C.POINTER(OclBackend)]),
+    "ocl_join": (None, [C.POINTER(OclBackend), C.POINTER(OclBackend)]),
     "ocl_timer_start": (None, [C.POINTER(OclBackend)]),
     "ocl_timer_stop": (C.c_double, [C.POINTER(OclBackend)]),
     "ops_init": (None, [C.POINTER(Ops), C.POINTER(OclBackend)]),

@@ -444,6 +444,22 @@ extern "C" cl_int clFinish(cl_command_queue queue)
     return (cl_int)cudaStreamSynchronize((cudaStream_t)queue);
 }
 
+extern "C" void ocl_join(struct ocl_backend *dst, struct ocl_backend *src)
+{
+    if (pending())
+        return;
+    if (!dst || !src || dst->device != src->device) {
+        fail("ocl_join: backends of different devices");
+        return;
+    }
+    cudaEvent_t ev;
+    if (!cuda_ok(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate"))
+        return;
+    if (cuda_ok(cudaEventRecord(ev, stream_of(src)), "cudaEventRecord"))
+        cuda_ok(cudaStreamWaitEvent(stream_of(dst), ev, 0), "cudaStreamWaitEvent");
+    cudaEventDestroy(ev);
+}
+
 extern "C" void ocl_finish(struct ocl_backend *ocl)
 {
     if (pending())

@@ -83,6 +83,13 @@ void ocl_zero(struct ocl_backend *ocl, cl_mem m, size_t off, size_t n);
 /* Wait for every launch of the backend's stream. */
 void ocl_finish(struct ocl_backend *ocl);
 
+/* Later work on dst's stream waits for everything issued so far on src's
+ * stream (both backends on the same device); returns at once. Lets several
+ * backends of one device, each running its own tiles, be started and
+ * finished together (no counterpart in the reference, whose queue is one
+ * per device). */
+void ocl_join(struct ocl_backend *dst, struct ocl_backend *src);
+
 /* Device timing of the backend's stream: ocl_timer_start records a CUDA
  * event on it, ocl_timer_stop records a second one, waits for it and
  * returns the milliseconds between them. */

@@ -83,3 +83,42 @@ def test_roma_bf16_stages(tmp_path):
     flow = got[0]
     assert np.isfinite(flow).all() and np.abs(flow).max() <= 1.0
     dev.close()
+
+
+@pytest.mark.gpu
+def test_two_concurrent_pipelines_match_solo_runs():
+    """Two models on one device, each with its own backend (stream), run
+    roma_match at the same time from two host threads (the way bench.py
+    fills a GPU): each result equals the same model's solo result
+    bit for bit."""
+    import threading
+
+    H = W = 128
+    main, dino, v2p = weight_paths()
+    devs = [coreg.Device(0, precision=coreg.OPS_BF16) for _ in range(2)]
+    nets = [Roma(d, main, dino, v2p, H=H, W=W, coarse=224) for d in devs]
+    try:
+        pairs = [tile_pair(s, H, W)[:2] for s in (3, 4)]
+        solo = [tuple(np.copy(x) for x in nets[k].match(*pairs[k])) for k in range(2)]
+        out = [None, None]
+        errs = []
+
+        def run(k):
+            try:
+                out[k] = tuple(np.copy(x) for x in nets[k].match(*pairs[k]))
+            except Exception as e:
+                errs.append(e)
+
+        th = [threading.Thread(target=run, args=(k,)) for k in range(2)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert not errs, errs
+        for k in range(2):
+            for a, b in zip(out[k], solo[k]):
+                assert np.array_equal(a, b, equal_nan=True)
+    finally:
+        for n_, d in zip(nets, devs):
+            n_.close()
+            d.close()
