@@ -407,8 +407,13 @@ def gpu_arm(args, rank, world, local):
     prof = profile_step(lib, dev, net, ins[0][0].ptr, ins[0][1].ptr)
     fl, by = work_model(es=2 if prec else 4)
     hbm, bf16, peak_kind = peaks()
-    # The dominant profiled operation that has a work model.
-    dom = max((k for k in prof if k in fl or k in by), key=lambda k: prof[k][0])
+    # The dominant profiled operation that has a work model and a DRAM
+    # traffic figure from the committed ncu capture (operations whose
+    # kernels ncu can tell apart by name), else the dominant one with a
+    # work model.
+    modeled = [k for k in prof if k in fl or k in by]
+    traced = [k for k in modeled if traffic_from_profiles(k)]
+    dom = max(traced or modeled, key=lambda k: prof[k][0])
     roof = None
     if dom in fl and (dom not in by or fl[dom] / max(by[dom], 1) > 50):
         ms_d, calls = prof[dom]

@@ -362,24 +362,33 @@ __global__ void conv3_reorder_pad_k(const float *w, int K, int C, int kp, __nv_b
 
 // Explicit im2col of a 3 x 3 / stride 1 / padding 1 convolution over a
 // channels-last bfloat16 map: row = pixel, column j = tap * C + c for
-// j < 9 C (zeros outside the map), zero up to kp.
+// j < 9 C (zeros outside the map), zero up to kp (a multiple of 8). One
+// thread per 8 columns of a row: one 16-byte store.
 __global__ void im2col3_small_k(const __nv_bfloat16 *in, int H, int W, int C, int kp,
                                 __nv_bfloat16 *col)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int chunks = kp / 8;
     const long n = (long)H * W;
-    if (e >= n * kp)
+    if (e >= n * chunks)
         return;
-    const long pix = e / kp;
-    const int j = (int)(e % kp);
-    __nv_bfloat16 v = __float2bfloat16_rn(0.0f);
-    if (j < 9 * C) {
-        const int t = j / C, c = j % C;
-        const int x = (int)(pix % W) + t % 3 - 1, y = (int)(pix / W) + t / 3 - 1;
-        if (x >= 0 && x < W && y >= 0 && y < H)
-            v = in[((long)y * W + x) * C + c];
+    const long pix = e / chunks;
+    const int j0 = (int)(e % chunks) * 8;
+    const int px = (int)(pix % W), py = (int)(pix / W);
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int j = j0 + q;
+        __nv_bfloat16 x = __float2bfloat16_rn(0.0f);
+        if (j < 9 * C) {
+            const int t = j / C, c = j % C;
+            const int xx = px + t % 3 - 1, yy = py + t / 3 - 1;
+            if (xx >= 0 && xx < W && yy >= 0 && yy < H)
+                x = in[((long)yy * W + xx) * C + c];
+        }
+        v[q] = x;
     }
-    col[e] = v;
+    *(uint4 *)(col + pix * kp + j0) = *(const uint4 *)v;
 }
 
 namespace coreg {
@@ -389,7 +398,7 @@ void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, i
                        float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count)
 {
     const long n = (long)H * W;
-    im2col3_small_k<<<cdiv(n * kp, 256), 256, 0, st>>>(in, H, W, C, kp, col);
+    im2col3_small_k<<<cdiv(n * (kp / 8), 256), 256, 0, st>>>(in, H, W, C, kp, col);
     GemmArgs g = gemm_args((int)n, K, kp);
     g.A = col;
     g.lda = kp;

@@ -89,6 +89,11 @@ struct roma_impl {
     int vgg_cin[16], vgg_cout[16], vgg_kp[16];
     void *patch_w;
     float *patch_b, *cls;
+    // bfloat16 mode: patch weights as (1024, patch_kp) rows (zero padded),
+    // the patches gathered into patch_col (n16 x patch_kp) for the tensor
+    // cores.
+    int patch_kp = 0;
+    __nv_bfloat16 *patch_col = nullptr;
     std::vector<float> pos_raw; // (1 + 37 * 37) x 1024, host
     Block vit[ROMA_VIT_DEPTH], dec[ROMA_DEC_DEPTH];
     float *norm_g, *norm_b;
@@ -653,7 +658,20 @@ extern "C" void roma_load(struct roma_model *m, struct ops *ops,
         long v1[1] = {ROMA_VIT_DIM}, sc[3] = {1, 1, ROMA_VIT_DIM};
         long sp[3] = {1, VIT_GRID * VIT_GRID + 1, ROMA_VIT_DIM};
         (void)sw;
-        I->patch_w = load_dev(I, dino, "patch_embed.proj.weight", 4, sw4, I->wt);
+        if (I->wt == DT_BF16) {
+            const int K = 3 * ROMA_PATCH * ROMA_PATCH, kp = (K + 15) / 16 * 16;
+            HostT hw;
+            if (!read_host(dino, "patch_embed.proj.weight", 4, sw4, hw))
+                return;
+            std::vector<float> pad((size_t)ROMA_VIT_DIM * kp, 0.0f);
+            for (int o = 0; o < ROMA_VIT_DIM; o++)
+                for (int k = 0; k < K; k++)
+                    pad[(size_t)o * kp + k] = hw.v[(size_t)o * K + k];
+            I->patch_w = upload(I, pad.data(), pad.size(), DT_BF16, "patch_embed");
+            I->patch_kp = kp;
+        }
+        else
+            I->patch_w = load_dev(I, dino, "patch_embed.proj.weight", 4, sw4, I->wt);
         I->patch_b = (float *)load_dev(I, dino, "patch_embed.proj.bias", 1, v1, DT_F32);
         I->cls = (float *)load_dev(I, dino, "cls_token", 3, sc, DT_F32);
         HostT pos;
@@ -815,6 +833,8 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
     I->g_kyy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_kxy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_x = (float *)dmalloc(I, n16 * GP_DIM * 4, "GP solve");
+    if (I->patch_kp)
+        I->patch_col = (__nv_bfloat16 *)dmalloc(I, n16 * I->patch_kp * 2, "patches");
     I->gp_work = (double *)dmalloc(I, gp_work_doubles((int)n16, GP_DIM) * 8, "GP work");
     I->gp_flag = (int *)dmalloc(I, sizeof(int), "GP flag");
     size_t dmax = 0;
@@ -1093,6 +1113,36 @@ void block(Ctx &c, const Block &b, int N, int nimg, int D, int heads, float eps)
 
 // DINOv2 on img (Cs x Cs, channels-last): the normalized patch tokens,
 // projected (decoder.proj.16), into P[0][k] (roma.c:717-738).
+// The 14 x 14 patches of a channels-last (H, W, 3) bfloat16 image as rows
+// of kp columns, column k = (c, ky, kx) (the PyTorch weight order), zero
+// from 588 on. One thread per 8 columns: one 16-byte store.
+__global__ void patch_rows_k(const __nv_bfloat16 *img, int H, int W, int kp,
+                             __nv_bfloat16 *rows)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int chunks = kp / 8, pw = W / ROMA_PATCH;
+    const long np = (long)(H / ROMA_PATCH) * pw;
+    if (e >= np * chunks)
+        return;
+    const long m = e / chunks;
+    const int j0 = (int)(e % chunks) * 8;
+    const int py = (int)(m / pw), px = (int)(m % pw);
+    constexpr int PP = ROMA_PATCH * ROMA_PATCH;
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int k = j0 + q;
+        __nv_bfloat16 x = __float2bfloat16_rn(0.0f);
+        if (k < 3 * PP) {
+            const int ch = k / PP, r = k % PP;
+            const int yy = py * ROMA_PATCH + r / ROMA_PATCH, xx = px * ROMA_PATCH + r % ROMA_PATCH;
+            x = img[((long)yy * W + xx) * 3 + ch];
+        }
+        v[q] = x;
+    }
+    *(uint4 *)(rows + m * kp + j0) = *(const uint4 *)v;
+}
+
 // Patch and position embedding of image k's prepared input (img) into
 // token rows k ntok .. of t_x: class token, then the 14 x 14 patches.
 void dino_embed(Ctx &c, int k)
@@ -1100,6 +1150,27 @@ void dino_embed(Ctx &c, int k)
     roma_impl *I = c.I;
     const int D = ROMA_VIT_DIM, N16 = I->n16;
     float *x = I->t_x + (size_t)k * I->ntok * D;
+    if (I->patch_kp) {
+        // bfloat16: the patches gathered into rows, then the tensor cores.
+        const int kp = I->patch_kp;
+        patch_rows_k<<<cdiv((long)N16 * (kp / 8), 256), 256, 0, c.st>>>(
+            (const __nv_bfloat16 *)I->img, I->Cs, I->Cs, kp, I->patch_col);
+        GemmArgs g = gemm_args(N16, D, kp);
+        g.A = I->patch_col;
+        g.lda = kp;
+        g.B = I->patch_w;
+        g.ldb = kp;
+        g.transb = 1;
+        g.C = x + D;
+        g.ldc = D;
+        g.bias = I->patch_b;
+        g.R = I->pos + D;
+        g.ab = DT_BF16;
+        g.c = DT_F32;
+        gemm_run(c.m->ocl, g, "patch_embed");
+        cls_pos_k<<<cdiv(D, 256), 256, 0, c.st>>>(x, I->cls, I->pos, D);
+        return;
+    }
     GemmArgs g = gemm_args(N16, D, 3 * ROMA_PATCH * ROMA_PATCH);
     g.A = I->img;
     g.amode = 2;
