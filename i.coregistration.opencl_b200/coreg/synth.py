@@ -200,6 +200,40 @@ def write_roma_weights(folder, seed=0):
     return paths
 
 
+# DISK's U-Net (disk.c:23-31): input and output channels per layer.
+DISK_CIN = (3, 16, 32, 64, 64, 128, 128, 96, 80)
+DISK_COUT = (16, 32, 64, 64, 64, 64, 64, 64, 129)
+
+
+def disk_weights(seed=0):
+    """Seeded random-init DISK U-Net in the extractor state_dict names the
+    loader requires ("unet.path_down.{0..4}.1.{1,3}",
+    "unet.path_up.{0..3}.conv.{1,3}"): convolutions He-normal, biases
+    N(0, 0.01), PReLU slopes 0.25 + N(0, 0.02)."""
+    g = np.random.default_rng(seed)
+    d = {}
+    for l, (ci, co) in enumerate(zip(DISK_CIN, DISK_COUT)):
+        pre = f"unet.path_down.{l}.1" if l < 5 else f"unet.path_up.{l - 5}.conv"
+        d[f"{pre}.3.weight"] = (g.standard_normal((co, ci, 5, 5)) *
+                                math.sqrt(2.0 / (ci * 25))).astype(np.float32)
+        d[f"{pre}.3.bias"] = (0.01 * g.standard_normal(co)).astype(np.float32)
+        if l > 0:
+            d[f"{pre}.1.weight"] = (0.25 + 0.02 * g.standard_normal(ci)).astype(np.float32)
+    return d
+
+
+def write_disk_weights(folder, seed=0):
+    """Write the DISK weights as safetensors into folder; returns the path."""
+    folder = Path(folder)
+    folder.mkdir(parents=True, exist_ok=True)
+    p = folder / f"disk_seed{seed}.safetensors"
+    if not p.exists():
+        tmp = p.with_suffix(".tmp")
+        write_safetensors(tmp, disk_weights(seed))
+        tmp.rename(p)
+    return p
+
+
 # ----------------------------------------------------------------- images
 
 def band_limited(rng, h, w, sigma, mean=128.0, std=40.0):

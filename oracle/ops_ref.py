@@ -338,3 +338,32 @@ def run_case(c):
                          x["var"], p["eps"])
         return {"out": conv2d(x["x"], C, H, W, wf, bf, K, 3, 3, 1, 1, 1, 1)}
     raise ValueError(op)
+
+
+def vit_block(x, w, heads, eps=1e-6):
+    """One pre-norm DINOv2 block as the reference runs it (roma.c:679-713:
+    LayerNorm, fused qkv linear, attention with the full score matrix,
+    output projection, LayerNorm, GELU MLP; LayerScale folded into the
+    output projection and fc2, roma.c:191-201), float64. w holds the
+    transformers Dinov2Layer names. Returns every intermediate: ln1, q, k,
+    v, ctx, attn (output projection before LayerScale), ln2, fc1 (before
+    GELU), mlp (fc2 output before LayerScale), out."""
+    x = np.asarray(x, np.float64)
+    N, D = x.shape
+    d = D // heads
+    f = lambda k: np.asarray(w[k], np.float64)
+    lin = lambda a, W, b: a @ f(W).T + f(b)
+    r = {}
+    r["ln1"] = layernorm(x, N, D, f("norm1.weight"), f("norm1.bias"), eps)
+    pre = "attention.attention."
+    r["q"] = lin(r["ln1"], pre + "query.weight", pre + "query.bias")
+    r["k"] = lin(r["ln1"], pre + "key.weight", pre + "key.bias")
+    r["v"] = lin(r["ln1"], pre + "value.weight", pre + "value.bias")
+    r["ctx"] = attention(r["q"], r["k"], r["v"], N, N, heads, d, 1.0 / np.sqrt(d))
+    r["attn"] = lin(r["ctx"], "attention.output.dense.weight", "attention.output.dense.bias")
+    h = x + f("layer_scale1.lambda1") * r["attn"]
+    r["ln2"] = layernorm(h, N, D, f("norm2.weight"), f("norm2.bias"), eps)
+    r["fc1"] = lin(r["ln2"], "mlp.fc1.weight", "mlp.fc1.bias")
+    r["mlp"] = lin(act(r["fc1"], ACT_GELU), "mlp.fc2.weight", "mlp.fc2.bias")
+    r["out"] = h + f("layer_scale2.lambda1") * r["mlp"]
+    return r
