@@ -234,6 +234,70 @@ def write_disk_weights(folder, seed=0):
     return p
 
 
+def eloftr_weights(seed=0):
+    """Seeded random-init Efficient LoFTR in the names of
+    EfficientLoFTRForKeypointMatching (what the loader requires): RepVGG
+    backbone (3 x 3, 1 x 1 and identity branches with BatchNorms), the
+    aggregated-attention transformer, the fine fusion. Scales keep the
+    activations bounded through the 21 blocks."""
+    g = np.random.default_rng(seed)
+    d = {}
+    n = lambda *s_, std=1.0: (std * g.standard_normal(s_)).astype(np.float32)
+
+    def bn(pre, c, gain=1.0):
+        d[f"{pre}.weight"] = (gain * (1.0 + 0.1 * g.standard_normal(c))).astype(np.float32)
+        d[f"{pre}.bias"] = n(c, std=0.1)
+        d[f"{pre}.running_mean"] = n(c, std=0.1)
+        d[f"{pre}.running_var"] = g.uniform(0.5, 1.5, c).astype(np.float32)
+
+    cin = 1
+    for s_, (nb, co, st) in enumerate(zip((1, 2, 4, 14), (64, 64, 128, 256), (2, 1, 2, 2))):
+        for b in range(nb):
+            stride = st if b == 0 else 1
+            pre = f"efficientloftr.backbone.stages.{s_}.blocks.{b}"
+            gain = 1.0
+            d[f"{pre}.conv1.conv.weight"] = n(co, cin, 3, 3, std=0.5 * math.sqrt(2.0 / (9 * cin)))
+            bn(f"{pre}.conv1.norm", co, gain)
+            d[f"{pre}.conv2.conv.weight"] = n(co, cin, 1, 1, std=0.5 * math.sqrt(2.0 / cin))
+            bn(f"{pre}.conv2.norm", co, gain)
+            if cin == co and stride == 1:
+                bn(f"{pre}.identity", co, gain)
+            cin = co
+    D, M = 256, 512
+    for l in range(4):
+        for kind in ("self_attention", "cross_attention"):
+            pre = f"efficientloftr.local_feature_transformer.layers.{l}.{kind}."
+            d[pre + "aggregation.q_aggregation.weight"] = n(D, 1, 4, 4, std=0.25)
+            d[pre + "aggregation.norm.weight"] = (1.0 + 0.1 * g.standard_normal(D)).astype(np.float32)
+            d[pre + "aggregation.norm.bias"] = n(D, std=0.1)
+            for p in ("q", "k", "v", "o"):
+                d[pre + f"attention.{p}_proj.weight"] = n(D, D, std=1.0 / math.sqrt(D))
+            d[pre + "mlp.fc1.weight"] = n(M, 2 * D, std=math.sqrt(2.0 / (2 * D)))
+            d[pre + "mlp.fc2.weight"] = n(D, M, std=1.0 / math.sqrt(M))
+            d[pre + "mlp.layer_norm.weight"] = (1.0 + 0.1 * g.standard_normal(D)).astype(np.float32)
+            d[pre + "mlp.layer_norm.bias"] = n(D, std=0.1)
+    d["refinement_layer.out_conv.weight"] = n(256, 256, 1, 1, std=1.0 / 16)
+    for i, (hid, inter) in enumerate(((128, 256), (64, 128))):
+        pre = f"refinement_layer.out_conv_layers.{i}."
+        d[pre + "out_conv1.weight"] = n(inter, hid, 1, 1, std=1.0 / math.sqrt(hid))
+        d[pre + "out_conv2.weight"] = n(inter, inter, 3, 3, std=math.sqrt(2.0 / (9 * inter)))
+        bn(pre + "batch_norm", inter)
+        d[pre + "out_conv3.weight"] = n(hid, inter, 3, 3, std=1.0 / math.sqrt(9 * inter))
+    return d
+
+
+def write_eloftr_weights(folder, seed=0):
+    """Write the Efficient LoFTR weights as safetensors; returns the path."""
+    folder = Path(folder)
+    folder.mkdir(parents=True, exist_ok=True)
+    p = folder / f"eloftr_seed{seed}.safetensors"
+    if not p.exists():
+        tmp = p.with_suffix(".tmp")
+        write_safetensors(tmp, eloftr_weights(seed))
+        tmp.rename(p)
+    return p
+
+
 # ----------------------------------------------------------------- images
 
 def band_limited(rng, h, w, sigma, mean=128.0, std=40.0):
