@@ -6,7 +6,7 @@ import ctypes as C
 import numpy as np
 
 from . import EXTRA_SIGNATURES, OclBackend, Ops, check, load
-from .roma import PthFile
+from .roma import Matcher, PthFile
 
 ELOFTR_MULTIPLE, ELOFTR_DIM, ELOFTR_FINE_DIM = 32, 256, 64
 
@@ -31,6 +31,8 @@ EXTRA_SIGNATURES.update({
     "eloftr_match": (None, [C.POINTER(EloftrModel), C.c_void_p, C.c_void_p, C.c_char_p,
                             C.c_int]),
     "eloftr_free": (None, [C.POINTER(EloftrModel)]),
+    "matcher_eloftr_create": (None, [C.POINTER(Matcher), C.POINTER(Ops), C.POINTER(PthFile),
+                                     C.c_char_p, C.c_int]),
 })
 
 
