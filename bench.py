@@ -72,6 +72,13 @@ def allmax(world, v):
     return float(t.item())
 
 
+def rank_tile_seeds(rank, ntiles):
+    """Seeds of the tile pairs rank processes: a contiguous block of ntiles
+    per rank, disjoint across ranks (tiles are independent: no data-path
+    collective)."""
+    return [rank * ntiles + i for i in range(ntiles)]
+
+
 def make_tiles(seeds):
     """Synthetic 1024 x 1024 tile pairs of the configuration's scene
     generator, resampled to the 864 x 864 processing size (float32 in
@@ -323,7 +330,7 @@ def gpu_arm(args, rank, world, local):
     nets = [Roma(d, main, dino, v2, H=H, W=W, coarse=COARSE) for d in devs]
     net = nets[0]
     ntiles = args.tiles
-    tiles = make_tiles([rank * ntiles + i for i in range(ntiles)])
+    tiles = make_tiles(rank_tile_seeds(rank, ntiles))
     hw3 = 3 * H * W
     # Device-resident tiles, and each graph's fixed input buffers.
     dtiles = [(dev.upload(a), dev.upload(b)) for a, b in tiles]
