@@ -195,10 +195,16 @@ def work_model(Hp=H, Wp=W, Cs=COARSE, es=2):
             add(fl, "vgg2_proj", 2 * 2 * (hh // sc) * (ww // sc) * fin * fo)
 
     def refiner(n, cin, feat, r, nout):
-        add(fl, "refiner_pw", 9 * 2 * n * cin * cin)
         add(fl, "refiner_out", 2 * n * cin * nout)
-        add(fl, "roma_dwconv5", 9 * 2 * 25 * n * cin)
-        add(by, "roma_dwconv5", 9 * 2 * n * cin * es)
+        if es == 2 and cin in (32, 64, 128):
+            # The fused block kernel (bfloat16): the product and the
+            # depthwise taps; its input read and output written once.
+            add(fl, "refiner_block", 9 * (2 * n * cin * cin + 2 * 25 * n * cin))
+            add(by, "refiner_block", 9 * 2 * n * cin * es)
+        else:
+            add(fl, "refiner_pw", 9 * 2 * n * cin * cin)
+            add(fl, "roma_dwconv5", 9 * 2 * 25 * n * cin)
+            add(by, "roma_dwconv5", 9 * 2 * n * cin * es)
         if r:
             add(fl, "roma_local_corr", 2 * (2 * r + 2) ** 2 * feat * n)
 

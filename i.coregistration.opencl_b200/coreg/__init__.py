@@ -130,6 +130,7 @@ SIGNATURES = {
     "coreg_tc_status": (I, []),
     "ops_conv3x3_cl": (None, [C.POINTER(Ops), P, I, I, I, P, P, I, I, F, P]),
     "roma_dwconv5_cl": (None, [C.POINTER(Ops), P, I, I, I, P, P, P]),
+    "roma_refiner_block_cl": (None, [C.POINTER(Ops), P, I, I, I, P, P, P, P, P]),
     "roma_local_corr_cl": (None, [C.POINTER(Ops), P, P, I, I, I, I, P, P]),
     "ops_gemm_noalloc": (None, [C.POINTER(Ops), I, I, I, Opnd, Opnd, I, Opnd, I, I, P, I, P, L, F, I, F]),
     "ops_gemm_noalloc_max_bytes": (C.c_size_t, []),

@@ -99,6 +99,13 @@ bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, vo
 void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, int C, int kp,
                        const __nv_bfloat16 *wk, const float *bias, int K, int act,
                        float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count);
+// One hidden block of RoMa's refiners, out = W relu(dw5x5(in) + b_dw) + b_pw,
+// over a channels-last bfloat16 (H, W, C) map in one tensor-core kernel
+// (tc_dwpw.cu): dw_w (C x 25) and dw_b float32, pw_w (C x C, output-major)
+// bfloat16, pw_b float32; false (nothing launched) unless C is 32, 64 or
+// 128 and the pointers are 16-byte aligned.
+bool dwpw_tc(cudaStream_t st, const void *in, int H, int W, int C, const float *dw_w,
+             const float *dw_b, const void *pw_w, const float *pw_b, void *out, int sm_count);
 // Double-precision GP solve (gp_chol.cu); work holds gp_work_doubles(n, d).
 size_t gp_work_doubles(int n, int d);
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,

@@ -1316,18 +1316,34 @@ void refiner_body(Ctx &c, const Refiner &r, const void *fa, const void *fb,
                           2 * r.feat + r.emb);
         launch_ok("roma_local_corr");
     }
+    // Blocks: in bfloat16 mode at the widths the fused tensor-core kernel
+    // takes, one kernel per block ping-ponging between d_a and d_b;
+    // otherwise the depthwise kernel into d_b and the product back into d_a.
+    void *x = I->d_a, *y = I->d_b;
+    const bool fused = at == DT_BF16 && (r.cinp == 32 || r.cinp == 64 || r.cinp == 128);
     for (int b = 0; b <= ROMA_HIDDEN; b++) {
+        if (fused) {
+            Prof p(c.m->ocl, "refiner_block");
+            if (!dwpw_tc(c.st, x, hs, ws, r.cinp, r.dw_w[b], r.dw_b[b], r.pw_w[b], r.pw_b[b],
+                         y, c.m->ocl->sm_count)) {
+                fail("refiner block: the fused kernel could not be launched");
+                return;
+            }
+            launch_ok("refiner_block");
+            std::swap(x, y);
+            continue;
+        }
         {
             Prof p(c.m->ocl, "roma_dwconv5");
-            roma_dwconv5_l(c.st, {I->d_a, 1, r.cinp, at}, r.cinp, hs, ws, r.dw_w[b],
-                           r.dw_b[b], {I->d_b, 1, r.cinp, at});
+            roma_dwconv5_l(c.st, {x, 1, r.cinp, at}, r.cinp, hs, ws, r.dw_w[b], r.dw_b[b],
+                           {y, 1, r.cinp, at});
             launch_ok("roma_dwconv5");
         }
-        gemm_nt(c, "refiner_pw", (int)n, r.cinp, r.cinp, I->d_b, r.cinp, at, r.pw_w[b],
-                r.pw_b[b], I->d_a, r.cinp, at, ACTF_NONE, false);
+        gemm_nt(c, "refiner_pw", (int)n, r.cinp, r.cinp, y, r.cinp, at, r.pw_w[b], r.pw_b[b],
+                x, r.cinp, at, ACTF_NONE, false);
     }
-    gemm_nt(c, "refiner_out", (int)n, r.nout, r.cinp, I->d_a, r.cinp, at, r.out_w,
-            r.out_b, I->d_c, r.nout, DT_F32, ACTF_NONE, false);
+    gemm_nt(c, "refiner_out", (int)n, r.nout, r.cinp, x, r.cinp, at, r.out_w, r.out_b,
+            I->d_c, r.nout, DT_F32, ACTF_NONE, false);
 }
 
 // ConvRefiner s on an hs x ws grid of a pass of size Hf x Wf (scale

@@ -3,6 +3,7 @@
 // roma_ops.h: RoMa's kernels on channel-major float32 buffers, for
 // callers of the reference's kernel argument lists.
 
+#include "gemm.cuh"
 #include "roma_kernels.cuh"
 #include "ops_b200.h"
 #include "roma_ops.h"
@@ -153,6 +154,68 @@ extern "C" void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, c
                    tm_out(o16, C, DT_BF16));
     copy2d(st, o16, DT_BF16, C, fptr(out), DT_F32, C, n, C);
     launch_ok("roma_dwconv5_cl");
+}
+
+extern "C" void roma_refiner_block_cl(struct ops *o, cl_mem in, int H, int W, int C,
+                                      cl_mem dw_w, cl_mem dw_b, cl_mem pw_w, cl_mem pw_b,
+                                      cl_mem out)
+{
+    if (!bufs_ok({in, dw_w, dw_b, pw_w, pw_b, out}, "roma_refiner_block_cl"))
+        return;
+    const long n = (long)H * W;
+    if (n <= 0 || C <= 0 || !count_ok(n * C, "roma_refiner_block_cl map"))
+        return;
+    cudaStream_t st = stream_of(o->ocl);
+    Prof p(o->ocl, "refiner_block");
+    const bool bf = o->precision == OPS_BF16;
+    const size_t es = bf ? 2 : 4;
+    const size_t mapb = ((size_t)n * C * es + 255) / 256 * 256;
+    const size_t wb = ((size_t)C * C * 2 + 255) / 256 * 256;
+    const size_t need = bf ? 3 * mapb + wb : mapb;
+    if (need > o->scratch16_bytes) {
+        ocl_release(&o->scratch16);
+        o->scratch16 = ocl_alloc(o->ocl, need, "refiner block operands");
+        o->scratch16_bytes = need;
+        if (pending())
+            return;
+    }
+    char *mid = (char *)o->scratch16->ptr;
+    GemmArgs g = gemm_args((int)n, C, C);
+    g.lda = C;
+    g.ldb = C;
+    g.transb = 1;
+    g.ldc = C;
+    g.bias = fptr(pw_b);
+    if (!bf) {
+        // float32: the depthwise kernel, then the float32 product.
+        roma_dwconv5_l(st, tm_map(fptr(in), C), C, H, W, fptr(dw_w), fptr(dw_b),
+                       tm_out(mid, C));
+        g.A = mid;
+        g.B = fptr(pw_w);
+        g.C = fptr(out);
+        gemm_run(o->ocl, g, "refiner_pw");
+        launch_ok("roma_refiner_block_cl");
+        return;
+    }
+    // bfloat16: the map and the weights rounded to bfloat16, the fused
+    // kernel (or, for other widths, the model's two kernels), the result
+    // widened back.
+    char *a16 = mid + mapb, *o16 = a16 + mapb, *w16 = o16 + mapb;
+    copy2d(st, fptr(in), DT_F32, C, a16, DT_BF16, C, n, C);
+    copy2d(st, fptr(pw_w), DT_F32, C, w16, DT_BF16, C, C, C);
+    if (!dwpw_tc(st, a16, H, W, C, fptr(dw_w), fptr(dw_b), w16, fptr(pw_b), o16,
+                 o->ocl->sm_count)) {
+        roma_dwconv5_l(st, tm_map(a16, C, DT_BF16), C, H, W, fptr(dw_w), fptr(dw_b),
+                       tm_out(mid, C, DT_BF16));
+        g.A = mid;
+        g.B = w16;
+        g.C = o16;
+        g.ab = DT_BF16;
+        g.c = DT_BF16;
+        gemm_run(o->ocl, g, "refiner_pw");
+    }
+    copy2d(st, o16, DT_BF16, C, fptr(out), DT_F32, C, n, C);
+    launch_ok("roma_refiner_block_cl");
 }
 
 extern "C" void roma_local_corr_cl(struct ops *o, cl_mem f1, cl_mem f2, int C, int H, int W,

@@ -315,6 +315,7 @@ int attn_status()
 }  // namespace
 
 int gemm_status();
+int dwpw_status();
 
 }  // namespace tc
 
@@ -340,5 +341,6 @@ extern "C" int coreg_tc_status(void)
 {
     const int a = coreg::tc::gemm_status();
     const int b = coreg::tc::attn_status();
-    return a ? a : b;
+    const int c = coreg::tc::dwpw_status();
+    return a ? a : b ? b : c;
 }

@@ -20,7 +20,8 @@
 //               4 tcgen05.mma (K = 16 each) per stage into one of two
 //               128 x BN float32 accumulators in TMEM (tiles alternate),
 //               commits each stage to empty[s] (the producer's refill
-//               signal) and each finished tile to acc_full[buffer];
+//               signal) and each finished tile to acc_full[buffer]
+//               (two accumulators, four for tiles of at most 64 columns);
 //   warps 2..9  epilogue, two warps per TMEM lane quadrant (alternate
 //               32-column chunks): each reads its 32 lanes (rows) with
 //               tcgen05.ld, transposes them through a padded shared-memory
@@ -29,8 +30,8 @@
 //               the way, then frees the accumulator (acc_empty[buffer]).
 //               Stores of one row per thread would make 32 separate memory
 //               requests per instruction.
-// With two accumulators the epilogue of a tile overlaps the main loop of
-// the next one.
+// With two or four accumulators the epilogue of a tile overlaps the main
+// loops of the next ones.
 // Every mbarrier wait is bounded (about two seconds); a wait that runs out
 // records an error code (coreg_tc_status) and the CTA leaves its loops,
 // frees its tensor memory and returns.
@@ -69,7 +70,7 @@ template <int BN, int STAGES>
 struct Smem {
     alignas(1024) __nv_bfloat16 a[STAGES][BM * BK];
     alignas(1024) __nv_bfloat16 b[STAGES][BN * BK];
-    uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
+    uint64_t full[STAGES], empty[STAGES], acc_full[4], acc_empty[4];
     uint32_t tmem;
 };
 
@@ -79,6 +80,16 @@ constexpr int EPI_WARPS = NTHREADS / 32 - 2;
 // the epilogue reads (the allocation granule).
 template <int BN>
 constexpr int acc_cols() { return BN < 32 ? 32 : BN; }
+
+// Tiles of at most 64 columns end after a few k-blocks, so that one
+// epilogue per tile cannot keep up: the two epilogue warp groups (warps
+// 2..5, 6..9) take alternate tiles whole, over four accumulators. Wider
+// tiles: both groups on every tile (alternate 32-column chunks), two
+// accumulators.
+template <int BN>
+constexpr bool split_epi() { return BN <= 64; }
+template <int BN>
+constexpr int n_acc() { return split_epi<BN>() ? 4 : 2; }
 
 // Output tile t: first row (dense) or pixel origin (convolution) and first
 // column.
@@ -134,14 +145,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < n_acc<BN>(); i++) {
             mbar_init(&s.acc_full[i], 1);
-            mbar_init(&s.acc_empty[i], EPI_WARPS);
+            mbar_init(&s.acc_empty[i], split_epi<BN>() ? 4 : EPI_WARPS);
         }
         mbar_fence_init();
     }
     if (warp == 1)
-        tmem_alloc(&s.tmem, 2 * acc_cols<BN>());
+        tmem_alloc(&s.tmem, n_acc<BN>() * acc_cols<BN>());
     fence_before();
     __syncthreads();
     fence_after();
@@ -182,7 +193,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             int it = 0, lt = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
-                const int buf = lt & 1, use = lt >> 1;
+                const int buf = lt % n_acc<BN>(), use = lt / n_acc<BN>();
                 // The epilogue has read this accumulator's previous tile.
                 if (use > 0 && !mbar_wait(&s.acc_empty[buf], (use - 1) & 1, 4))
                     break;
@@ -210,10 +221,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         }
     }
     else {
-        // Epilogue: warp w owns TMEM lanes (rows) 32 (w % 4) ..., and of
-        // their columns the 32-column chunks of parity (w - 2) / 4: two
+        // Epilogue: warp w owns TMEM lanes (rows) 32 (w % 4) ...; of wide
+        // tiles it takes the 32-column chunks of parity (w - 2) / 4 (two
         // warps per lane quadrant, so that each scheduler interleaves two
-        // epilogue warps.
+        // epilogue warps), of narrow ones (split_epi) every column of the
+        // tiles of parity (w - 2) / 4.
         const int q = warp % 4, half = (warp - 2) / 4;
         const int r = 32 * q + lane;
         float(*stage)[33] = stage_all[warp - 2];
@@ -221,7 +233,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         const TC *R = (const TC *)p.R;
         int lt = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
-            const int buf = lt & 1, use = lt >> 1;
+            if (split_epi<BN>() && (lt & 1) != half)
+                continue;
+            const int buf = lt % n_acc<BN>(), use = lt / n_acc<BN>();
             const Tile tl = tile_of<BN>(p, t, tiles_m);
             int row = tl.m0 + r;
             if (p.conv) {
@@ -234,7 +248,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             fence_after();
             const uint32_t acc =
                 tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * acc_cols<BN>());
-            for (int c0 = 32 * half; c0 < BN && tl.n0 + c0 < p.N; c0 += 64) {
+            const int cs = split_epi<BN>() ? 0 : 32 * half, cstep = split_epi<BN>() ? 32 : 64;
+            for (int c0 = cs; c0 < BN && tl.n0 + c0 < p.N; c0 += cstep) {
                 float v[32];
                 tmem_ld32(acc + c0, v);
 #pragma unroll
@@ -271,7 +286,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     __syncthreads();
     if (warp == 1) {
         fence_after();
-        tmem_dealloc(tmem, 2 * acc_cols<BN>());
+        tmem_dealloc(tmem, n_acc<BN>() * acc_cols<BN>());
     }
 }
 
@@ -412,6 +427,27 @@ bool make_map_conv(CUtensorMap *map, const void *base, int H, int W, int C, int 
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D bfloat16 tensor map of a channels-last (H, W, C) map for TMA
+// stores (or loads) of box_c x box_w x box_h boxes, swizzle_bytes 0, 64 or
+// 128.
+bool make_map_hwc(CUtensorMap *map, void *base, int H, int W, int C, int box_c, int box_w,
+                  int box_h, int swizzle_bytes)
+{
+    EncodeTiled enc = encoder();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H};
+    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2};
+    cuuint32_t box[3] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                        : CU_TENSOR_MAP_SWIZZLE_NONE;
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -48,6 +48,18 @@ void ops_attention_qkv(struct ops *o, cl_mem qkv, int N, int Dm, int heads,
 void roma_dwconv5_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem wt,
                      cl_mem bias, cl_mem out);
 
+/* One hidden block of a RoMa refiner on a channels-last (H, W, C)
+ * float32 map: out = W_pw relu(dw5x5(in) + b_dw) + b_pw, the depthwise
+ * 5 x 5 convolution of roma_dwconv5_cl followed by the 1 x 1 convolution
+ * the reference runs after it (roma.c:970-985, 1080-1094). pw_w is
+ * (C, C) output-major, pw_b C floats. With o->precision OPS_BF16 and C
+ * 32, 64 or 128 the model's fused tensor-core kernel runs (the depthwise
+ * result rounded to bfloat16 in shared memory, float32 accumulation,
+ * bfloat16 result); otherwise the two steps run one after the other. No
+ * reference counterpart. */
+void roma_refiner_block_cl(struct ops *o, cl_mem in, int H, int W, int C, cl_mem dw_w,
+                           cl_mem dw_b, cl_mem pw_w, cl_mem pw_b, cl_mem out);
+
 /* Local correlation of channels-last (H, W, C) float32 maps f1 and f2 at
  * the warp flow ((2, H, W) normalized coordinates, channel-major as in
  * the models) into out, channels-last (H, W, (2r + 1)^2): roma_local_corr
