@@ -64,17 +64,24 @@ struct TcParams {
     // cH x cW x cC, cC a multiple of 64): the tile is TW x TH output pixels
     // (TW TH = 128), k-block kb = (tap, 64-channel chunk).
     int conv, cH, cW, cC, TW, TH, tiles_x, tiles_y;
+    // Epilogue through TMA stores (output tensor map tma_c); else one
+    // coalesced store per row.
+    int tma_out;
 };
 
 template <int BN, int STAGES>
 struct Smem {
     alignas(1024) __nv_bfloat16 a[STAGES][BM * BK];
     alignas(1024) __nv_bfloat16 b[STAGES][BN * BK];
+    // Per epilogue warp: the staging block of its TMA stores (32 x 32
+    // values, swizzled), or of its transposes.
+    alignas(1024) unsigned char cst[8][4096];
     uint64_t full[STAGES], empty[STAGES], acc_full[4], acc_empty[4];
     uint32_t tmem;
 };
 
 constexpr int EPI_WARPS = NTHREADS / 32 - 2;
+static_assert(EPI_WARPS == 8, "one staging block per epilogue warp");
 
 // TMEM columns per accumulator: BN, at least the 32 that one tcgen05.ld of
 // the epilogue reads (the allocation granule).
@@ -119,6 +126,74 @@ __device__ __forceinline__ int k_rotation(int t, int tiles_m, int nk)
     return (int)(((unsigned)mt * 5u + (unsigned)nt * 3u) % (unsigned)nk);
 }
 
+// v[j] += R[j] for the j < n (at most 32) columns of a residual row.
+__device__ __forceinline__ void add_row(float v[32], const float *R, int n)
+{
+    if (n >= 32 && ((uintptr_t)R & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float4 x = __ldg((const float4 *)R + j);
+            v[4 * j] += x.x;
+            v[4 * j + 1] += x.y;
+            v[4 * j + 2] += x.z;
+            v[4 * j + 3] += x.w;
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+        if (j < n)
+            v[j] += R[j];
+}
+
+__device__ __forceinline__ void add_row(float v[32], const __nv_bfloat16 *R, int n)
+{
+    if (n >= 32 && ((uintptr_t)R & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint4 x = __ldg((const uint4 *)R + j);
+            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                v[8 * j + 2 * k] += __uint_as_float(w[k] << 16);
+                v[8 * j + 2 * k + 1] += __uint_as_float(w[k] & 0xffff0000u);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+        if (j < n)
+            v[j] += __bfloat162float(R[j]);
+}
+
+// Row l of a 32-column staging block in the layout of the output tensor
+// map's box: float rows of 128 bytes, 16-byte chunk c at c ^ (l % 8)
+// (128-byte swizzle); bfloat16 rows of 64 bytes, chunk c at c ^ ((l / 2) %
+// 4) (64-byte swizzle).
+__device__ __forceinline__ void stage_row(unsigned char *blk, int l, const float v[32], float *)
+{
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        *(float4 *)(blk + l * 128 + ((c ^ (l & 7)) << 4)) =
+            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+__device__ __forceinline__ void stage_row(unsigned char *blk, int l, const float v[32],
+                                          __nv_bfloat16 *)
+{
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * k], v[8 * c + 2 * k + 1]);
+            w[k] = *(const uint32_t *)&h;
+        }
+        *(uint4 *)(blk + l * 64 + ((c ^ ((l >> 1) & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // The activation (ACT, or -1 for the run-time one of p.act) and the output
 // type are template parameters: a run-time switch would inline every
 // activation's math into the unrolled epilogue loop, and that code size
@@ -126,15 +201,12 @@ __device__ __forceinline__ int k_rotation(int t, int tiles_m, int nk)
 template <int BN, int STAGES, int ACT, typename TC>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-               const __grid_constant__ CUtensorMap tma_b, TcParams p)
+               const __grid_constant__ CUtensorMap tma_b,
+               const __grid_constant__ CUtensorMap tma_c, TcParams p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // Epilogue transposes, per epilogue warp 32 rows x 32 columns: a
-    // statically declared shared array, so that its accesses compile to
-    // shared-memory instructions.
-    __shared__ float stage_all[EPI_WARPS][32][33];
     Smem<BN, STAGES> &s = *reinterpret_cast<Smem<BN, STAGES> *>(
-        (void *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023));
+        smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int nk = (p.K + BK - 1) / BK;
     const int tiles_m = p.conv ? p.tiles_x * p.tiles_y : (p.M + BM - 1) / BM;
@@ -228,7 +300,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
         // tiles of parity (w - 2) / 4.
         const int q = warp % 4, half = (warp - 2) / 4;
         const int r = 32 * q + lane;
-        float(*stage)[33] = stage_all[warp - 2];
+        unsigned char *cst = s.cst[warp - 2];
+        float *stage = (float *)cst;
         TC *C = (TC *)p.C;
         const TC *R = (const TC *)p.R;
         int lt = 0;
@@ -252,9 +325,40 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             for (int c0 = cs; c0 < BN && tl.n0 + c0 < p.N; c0 += cstep) {
                 float v[32];
                 tmem_ld32(acc + c0, v);
+                if (p.tma_out) {
+                    // Lane = row: bias, activation and residual on this
+                    // row's 32 values, then one TMA store of the warp's 32 x
+                    // 32 block (clipped at the matrix or map edges).
+                    const int col0 = tl.n0 + c0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float b = p.bias && col0 + j < p.N ? __ldg(p.bias + col0 + j) : 0.0f;
+                        v[j] = apply_act(p.alpha * v[j] + b, ACT >= 0 ? ACT : p.act, p.slope);
+                    }
+                    if (R && row < p.M)
+                        add_row(v, R + (long)row * p.ldc + col0, p.N - col0);
+                    // The previous store has read the staging block.
+                    if (lane == 0)
+                        bulk_wait_read<0>();
+                    __syncwarp();
+                    stage_row(cst, lane, v, (TC *)nullptr);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (p.conv)
+                            tma_store_3d(&tma_c, cst, col0, tl.cx0 + (32 * q) % p.TW,
+                                         tl.cy0 + (32 * q) / p.TW);
+                        else
+                            tma_store_2d(&tma_c, cst, col0, tl.m0 + 32 * q);
+                        bulk_commit();
+                    }
+                    continue;
+                }
+                // Transpose through the staging block (rotated rows: no bank
+                // conflicts either way).
 #pragma unroll
                 for (int j = 0; j < 32; j++)
-                    stage[lane][j] = v[j];
+                    stage[lane * 32 + ((j + lane) & 31)] = v[j];
                 __syncwarp();
                 // Lane = column from here on.
                 const int col = tl.n0 + c0 + lane;
@@ -265,7 +369,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const int grow = __shfl_sync(0xffffffffu, row, rr);
                     if (grow < p.M && cok) {
                         const long idx = (long)grow * p.ldc + col;
-                        float x = p.alpha * stage[rr][lane] + bias;
+                        float x = p.alpha * stage[rr * 32 + ((lane + rr) & 31)] + bias;
                         x = apply_act(x, ACT >= 0 ? ACT : p.act, p.slope);
                         if (R)
                             x += ldf(R + idx);
@@ -281,6 +385,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
             if (lane == 0)
                 mbar_arrive(&s.acc_empty[buf]);
         }
+        // This warp's TMA stores have written global memory.
+        if (lane == 0)
+            bulk_wait_all();
     }
     fence_before();
     __syncthreads();
@@ -309,20 +416,22 @@ int conv_tile_width(int H, int W)
 
 template <int BN, int STAGES, int ACT, typename TC>
 bool run_tc(cudaStream_t st, int grid, const CUtensorMap &ma, const CUtensorMap &mb,
-            const TcParams &p)
+            const CUtensorMap &mc, const TcParams &p)
 {
     const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
     static unsigned done = 0;
     if (!smem_opt_in((const void *)tc_gemm_kernel<BN, STAGES, ACT, TC>, smem, &done))
         return false;
-    tc_gemm_kernel<BN, STAGES, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, p);
+    tc_gemm_kernel<BN, STAGES, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, mc, p);
     return true;
 }
+
+bool make_map_c(CUtensorMap *map, void *base, int es, const TcParams &p, long ldc);
 
 template <int BN, int STAGES>
 bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mc;
     TcParams p;
     memset(&p, 0, sizeof(p));
     long tiles_m = cdiv(g.M, BM);
@@ -357,20 +466,24 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     const long ntiles = tiles_m * cdiv(g.N, BN);
     if (ntiles >= (1L << 31))
         return false;
+    // TMA-store epilogue where the output allows a tensor map (tiles of at
+    // least 32 columns, 16-byte aligned rows).
+    memset(&mc, 0, sizeof(mc));
+    p.tma_out = BN >= 32 && make_map_c(&mc, g.C, g.c == DT_BF16 ? 2 : 4, p, g.ldc);
     // Persistent: at most one CTA per SM (the shared memory allows one).
     const int grid = (int)(ntiles < sm_count ? ntiles : sm_count);
     if (p.c_bf16) {
         if (g.act == ACTF_NONE)
-            return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, p);
+            return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, mc, p);
         if (g.act == ACTF_GELU)
-            return run_tc<BN, STAGES, ACTF_GELU, __nv_bfloat16>(st, grid, ma, mb, p);
+            return run_tc<BN, STAGES, ACTF_GELU, __nv_bfloat16>(st, grid, ma, mb, mc, p);
         if (g.act == ACTF_RELU)
-            return run_tc<BN, STAGES, ACTF_RELU, __nv_bfloat16>(st, grid, ma, mb, p);
-        return run_tc<BN, STAGES, -1, __nv_bfloat16>(st, grid, ma, mb, p);
+            return run_tc<BN, STAGES, ACTF_RELU, __nv_bfloat16>(st, grid, ma, mb, mc, p);
+        return run_tc<BN, STAGES, -1, __nv_bfloat16>(st, grid, ma, mb, mc, p);
     }
     if (g.act == ACTF_NONE)
-        return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, p);
-    return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, p);
+        return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, mc, p);
+    return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, mc, p);
 }
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -394,6 +507,37 @@ EncodeTiled encoder()
             cudaGetLastError();
     });
     return fn;
+}
+
+// Tensor map of the GEMM output C for the epilogue's TMA stores: 2-D
+// (N columns x M rows, row pitch ldc) or, in convolution mode, 3-D
+// channels-last (N, cW, cH); box 32 columns x 32 rows (pixels), 128-byte
+// (float) or 64-byte (bfloat16) swizzle. False when C's alignment or pitch
+// does not allow one.
+bool make_map_c(CUtensorMap *map, void *base, int es, const TcParams &p, long ldc)
+{
+    EncodeTiled enc = encoder();
+    if (!enc || ((uintptr_t)base & 15) || (ldc * es) % 16)
+        return false;
+    const CUtensorMapDataType dt =
+        es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapSwizzle sw = es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (p.conv) {
+        const int bw = p.TW < 32 ? p.TW : 32;
+        cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.cW, (cuuint64_t)p.cH};
+        cuuint64_t strides[2] = {(cuuint64_t)ldc * es, (cuuint64_t)p.cW * ldc * es};
+        cuuint32_t box[3] = {32, (cuuint32_t)bw, (cuuint32_t)(32 / bw)};
+        return enc(map, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)p.N, (cuuint64_t)p.M};
+    cuuint64_t strides[1] = {(cuuint64_t)ldc * es};
+    cuuint32_t box[2] = {32, 32};
+    return enc(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
