@@ -14,12 +14,20 @@
 //               and the D-column output) and MMA issue: S(j) = Q K(j)^T
 //               (K-major operands), O += P(j) V(j) (P from shared memory,
 //               V as an MN-major operand), S computed two blocks ahead;
-//   warps 2..5  softmax, one thread per query row: S(j) from TMEM, masked
-//               keys, online maximum (O and the row sum rescaled in tensor
-//               memory only when the maximum grows by more than 2^8, else
-//               the stale maximum is kept), P(j) = exp2 as bfloat16 into
-//               the 128-byte swizzled shared-memory tile of the second MMA;
-//               at the end O / l to global memory.
+//   warps 2..17 softmax, four warps per query row: warp w takes the rows
+//               of TMEM lane quadrant w % 4 and key quarter (w - 2) / 4 of
+//               each block (32 keys) and the same quarter of O's columns.
+//               S(j) from TMEM, masked keys, the row maximum of the four
+//               quarters through shared memory (one barrier of the softmax
+//               warps per block), online maximum (O and the row sum
+//               rescaled in tensor memory only when the maximum grows by
+//               more than 2^8, else the stale maximum is kept), P(j) = exp2
+//               as bfloat16 into the 128-byte swizzled shared-memory tile
+//               of the second MMA (two tiles for D 64, so that P(j) is
+//               written while the tensor cores read P(j - 1)); at the end
+//               O / l to global memory. Four warps per scheduler, packed
+//               float pairs and independent partial maxima and sums keep
+//               the exponential unit busy.
 // Every wait is bounded as in tc_gemm.cu.
 
 #include <math.h>
@@ -33,21 +41,33 @@ namespace tc {
 namespace {
 
 constexpr int BQ = 128, BKV = 128;
+constexpr int SPLIT = 4;                       // softmax warps per query row
+constexpr int SOFT_THREADS = 4 * SPLIT * 32;
+constexpr int ATT_THREADS = 64 + SOFT_THREADS;  // TMA warp, MMA warp, softmax warps
 
 template <int D>
 struct AttnCfg {
     static constexpr int KA = D / 64;            // 64-wide atoms along D
     static constexpr int ST = D == 64 ? 3 : 2;   // K / V stages
+    // P tiles: two for D 64, so that the softmax of block j writes P(j)
+    // while the tensor cores still read P(j - 1); one for D 128 (shared
+    // memory).
+    static constexpr int PB = D == 64 ? 2 : 1;
 };
 
 template <int D>
 struct AttnSmem {
-    static constexpr int KA = AttnCfg<D>::KA, ST = AttnCfg<D>::ST;
+    static constexpr int KA = AttnCfg<D>::KA, ST = AttnCfg<D>::ST, PB = AttnCfg<D>::PB;
     alignas(1024) __nv_bfloat16 q[KA][BQ * 64];
     alignas(1024) __nv_bfloat16 k[ST][KA][BKV * 64];
     alignas(1024) __nv_bfloat16 v[ST][KA][BKV * 64];
-    alignas(1024) __nv_bfloat16 p[2][BQ * 64];
-    uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[2], p_full, pv_done;
+    alignas(1024) __nv_bfloat16 p[PB][2][BQ * 64];
+    float red[2][SPLIT][BQ];  // per block parity and key quarter: row maxima, then sums
+    // Softmax abort flags by block parity: a failed wait in block j sets
+    // abort[j % 2] before the block's barrier, or abort[(j + 1) % 2] after
+    // it; every softmax warp reads abort[j % 2] after barrier j.
+    int abort[2];
+    uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[2], p_full, pv_done[PB];
     uint32_t tmem;
 };
 
@@ -64,11 +84,44 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Packed float32 pairs (sm_100a): one instruction for both values.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    unsigned long long aa, bb, cc, dd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c.x), "f"(c.y));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dd) : "l"(aa), "l"(bb), "l"(cc));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
+{
+    unsigned long long aa, bb, dd;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(dd) : "l"(aa), "l"(bb));
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
+    return d;
+}
+
+// The hardware base-2 exponential (results below 2^-126 flush to zero,
+// negligible next to the row maximum's 1).
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(ATT_THREADS, 1)
 tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
 {
-    constexpr int KA = AttnCfg<D>::KA, ST = AttnCfg<D>::ST;
+    constexpr int KA = AttnCfg<D>::KA, ST = AttnCfg<D>::ST, PB = AttnCfg<D>::PB;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     AttnSmem<D> &s = *reinterpret_cast<AttnSmem<D> *>(
         (void *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023));
@@ -84,8 +137,10 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
         }
         mbar_init(&s.s_full[0], 1);
         mbar_init(&s.s_full[1], 1);
-        mbar_init(&s.p_full, 128);
-        mbar_init(&s.pv_done, 1);
+        mbar_init(&s.p_full, SOFT_THREADS);
+        for (int i = 0; i < PB; i++)
+            mbar_init(&s.pv_done[i], 1);
+        s.abort[0] = s.abort[1] = 0;
         mbar_fence_init();
     }
     if (warp == 1)
@@ -148,7 +203,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
                 const uint32_t vbase = su32(s.v[st][0]);
 #pragma unroll
                 for (int a = 0; a < 2; a++) {
-                    const uint64_t dp = sw128_desc(su32(s.p[a]));
+                    const uint64_t dp = sw128_desc(su32(s.p[j % PB][a]));
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         // 16 keys from key a 64 + 16 k: V rows of 128 bytes,
@@ -159,7 +214,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
                         mma_bf16(tO, dp + 2 * k, dv, id_o, (j | a | k) ? 1u : 0u);
                     }
                 }
-                mma_commit(&s.pv_done);
+                mma_commit(&s.pv_done[j % PB]);
                 mma_commit(&s.kv_empty[st]);
                 if (j + 2 < nblk)
                     ok = issue_s(j + 2);
@@ -167,106 +222,161 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
         }
     }
     else {
-        const int qd = warp % 4, r = 32 * qd + lane;
+        constexpr int KW = BKV / SPLIT, OW = D / SPLIT;  // keys and O columns per warp
+        const int qd = warp % 4, part = (warp - 2) / 4, r = 32 * qd + lane;
         const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
+        // O columns of this warp: load, store.
+        auto o_ld = [&](float *o) {
+            if (OW == 16)
+                tmem_ld16(tO + lane_off + OW * part, o);
+            else
+                tmem_ld32(tO + lane_off + OW * part, o);
+        };
+        auto o_st = [&](const float *o) {
+            if (OW == 16)
+                tmem_st16(tO + lane_off + OW * part, o);
+            else
+                tmem_st32(tO + lane_off + OW * part, o);
+        };
         for (int j = 0; j < nblk; j++) {
             // Waits decided per warp, so that the warp-collective TMEM
             // accesses below never see a partial warp.
-            if (!__all_sync(0xffffffffu, mbar_wait(&s.s_full[j & 1], (j >> 1) & 1, 15))) {
+            const bool sok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[j & 1], (j >> 1) & 1, 15));
+            if (!sok && lane == 0)
+                s.abort[j & 1] = 1;
+            float sv[KW];
+            float mx = -INFINITY;
+            if (sok) {
+                fence_after();
+                tmem_ld32(tmem + lane_off + (j & 1) * 128 + KW * part, sv);
+                const int kvalid = p.N - j * BKV - KW * part;
+                if (kvalid < KW) {
+#pragma unroll
+                    for (int i = 0; i < KW; i++)
+                        if (i >= kvalid)
+                            sv[i] = -INFINITY;
+                }
+                float m8[8];
+#pragma unroll
+                for (int t = 0; t < 8; t++)
+                    m8[t] = sv[t];
+#pragma unroll
+                for (int i = 8; i < KW; i++)
+                    m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    m8[t] = fmaxf(m8[t], m8[t + 4]);
+                mx = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
+            }
+            // The quarters' maxima (raw scores; the scale is positive).
+            s.red[j & 1][part][r] = mx;
+            named_bar(1, SOFT_THREADS);
+            if (s.abort[j & 1]) {
                 ok = false;
                 break;
             }
-            fence_after();
-            float sv[BKV];
 #pragma unroll
-            for (int c = 0; c < BKV / 32; c++)
-                tmem_ld32(tmem + lane_off + (j & 1) * 128 + 32 * c, sv + 32 * c);
-            const int kvalid = p.N - j * BKV;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < BKV; i++) {
-                sv[i] = i < kvalid ? sv[i] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sv[i]);
-            }
-            if (j > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&s.pv_done, (j - 1) & 1, 16))) {
-                    ok = false;
-                    break;
-                }
-                fence_after();
-            }
+            for (int o = 1; o < SPLIT; o++)
+                mx = fmaxf(mx, s.red[j & 1][(part + o) % SPLIT][r]);
+            mx *= p.scale_log2;
+            // PV(i) has completed (pv_done[i % PB] phase i / PB).
+            auto pv_wait = [&](int i) {
+                return __all_sync(0xffffffffu, mbar_wait(&s.pv_done[i % PB], (i / PB) & 1, 16));
+            };
             const float m_new = fmaxf(m_used, mx);
+            // The tensor-memory loads and stores are warp-collective: the
+            // whole warp rescales when one of its rows needs it, the other
+            // rows by 1. The warps of a row decide alike.
+            const bool need = j > 0 && m_new > m_used + 8.0f;
+            const bool rescale = __any_sync(0xffffffffu, need);
+            // O is final up to PV(j - 1) before a rescale; P(j)'s tiles are
+            // free once PV(j - PB) has read them.
+            if ((rescale && !pv_wait(j - 1)) || (j >= PB && !pv_wait(j - PB))) {
+                ok = false;
+                if (lane == 0)
+                    s.abort[(j + 1) & 1] = 1;
+                continue;
+            }
+            fence_after();
             if (j == 0)
                 m_used = m_new;
-            else {
-                // The tensor-memory loads and stores are warp-collective:
-                // the whole warp rescales when one of its rows needs it,
-                // the other rows by 1.
-                const bool need = m_new > m_used + 8.0f;
-                if (__any_sync(0xffffffffu, need)) {
-                    const float corr = need ? exp2f(m_used - m_new) : 1.0f;
-                    l *= corr;
+            else if (rescale) {
+                const float corr = need ? exp2f(m_used - m_new) : 1.0f;
+                l *= corr;
+                float o[OW];
+                o_ld(o);
 #pragma unroll
-                    for (int c = 0; c < D / 32; c++) {
-                        float o[32];
-                        tmem_ld32(tO + lane_off + 32 * c, o);
-#pragma unroll
-                        for (int i = 0; i < 32; i++)
-                            o[i] *= corr;
-                        tmem_st32(tO + lane_off + 32 * c, o);
-                    }
-                    if (need)
-                        m_used = m_new;
-                }
+                for (int i = 0; i < OW; i++)
+                    o[i] *= corr;
+                o_st(o);
+                if (need)
+                    m_used = m_new;
             }
-            float sum = 0.0f;
+            float2 s4[4];
 #pragma unroll
-            for (int a = 0; a < 2; a++) {
-                unsigned char *row = (unsigned char *)s.p[a] + r * 128;
+            for (int t = 0; t < 4; t++)
+                s4[t] = make_float2(0.0f, 0.0f);
+            const float2 sc = make_float2(p.scale_log2, p.scale_log2);
+            const float2 mm = make_float2(-m_used, -m_used);
+            // Keys KW part .. of the block: 64-key tile part / 2, 16-byte
+            // chunks from 4 (part % 2).
+            unsigned char *row = (unsigned char *)s.p[j % PB][part >> 1] + r * 128;
 #pragma unroll
-                for (int cc = 0; cc < 8; cc++) {
-                    float e[8];
+            for (int cc = 0; cc < KW / 8; cc++) {
+                float e[8];
 #pragma unroll
-                    for (int t = 0; t < 8; t++) {
-                        e[t] = exp2f(sv[a * 64 + cc * 8 + t] - m_used);
-                        sum += e[t];
-                    }
-                    uint4 w;
-                    w.x = pack_bf16(e[0], e[1]);
-                    w.y = pack_bf16(e[2], e[3]);
-                    w.z = pack_bf16(e[4], e[5]);
-                    w.w = pack_bf16(e[6], e[7]);
-                    *reinterpret_cast<uint4 *>(row + ((cc ^ (r & 7)) << 4)) = w;
+                for (int t = 0; t < 4; t++) {
+                    const float2 a =
+                        ffma2(make_float2(sv[cc * 8 + 2 * t], sv[cc * 8 + 2 * t + 1]), sc, mm);
+                    e[2 * t] = ex2(a.x);
+                    e[2 * t + 1] = ex2(a.y);
+                    s4[t] = fadd2(s4[t], make_float2(e[2 * t], e[2 * t + 1]));
                 }
+                uint4 w;
+                w.x = pack_bf16(e[0], e[1]);
+                w.y = pack_bf16(e[2], e[3]);
+                w.z = pack_bf16(e[4], e[5]);
+                w.w = pack_bf16(e[6], e[7]);
+                const int chunk = 4 * (part & 1) + cc;
+                *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = w;
             }
-            l += sum;
+            const float2 s2 = fadd2(fadd2(s4[0], s4[1]), fadd2(s4[2], s4[3]));
+            l += s2.x + s2.y;
             fence_async_smem();
             fence_before();
             mbar_arrive(&s.p_full);
         }
-        if (ok && __all_sync(0xffffffffu, mbar_wait(&s.pv_done, (nblk - 1) & 1, 17))) {
+        if (ok && __all_sync(0xffffffffu, mbar_wait(&s.pv_done[(nblk - 1) % PB],
+                                                    ((nblk - 1) / PB) & 1, 17)))
             fence_after();
+        else
+            ok = false;
+        // Row sums of the quarters (added in one order by every warp of a
+        // row); every softmax warp reaches this barrier.
+        s.red[nblk & 1][part][r] = l;
+        named_bar(1, SOFT_THREADS);
+        if (__all_sync(0xffffffffu, ok)) {
+            l = 0.0f;
+#pragma unroll
+            for (int o = 0; o < SPLIT; o++)
+                l += s.red[nblk & 1][o][r];
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             const int q = q0 + r;
+            float o[OW];
+            o_ld(o);
+            if (q < p.N) {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + img * p.out_img + (long)q * p.ldo +
+                                                       h * D + OW * part);
 #pragma unroll
-            for (int c = 0; c < D / 32; c++) {
-                float o[32];
-                tmem_ld32(tO + lane_off + 32 * c, o);
-                if (q < p.N) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + img * p.out_img +
-                                                           (long)q * p.ldo + h * D +
-                                                           32 * c);
-#pragma unroll
-                    for (int t = 0; t < 4; t++) {
-                        uint4 w;
-                        w.x = pack_bf16(o[8 * t] * inv, o[8 * t + 1] * inv);
-                        w.y = pack_bf16(o[8 * t + 2] * inv, o[8 * t + 3] * inv);
-                        w.z = pack_bf16(o[8 * t + 4] * inv, o[8 * t + 5] * inv);
-                        w.w = pack_bf16(o[8 * t + 6] * inv, o[8 * t + 7] * inv);
-                        dst[t] = w;
-                    }
+                for (int t = 0; t < OW / 8; t++) {
+                    uint4 w;
+                    w.x = pack_bf16(o[8 * t] * inv, o[8 * t + 1] * inv);
+                    w.y = pack_bf16(o[8 * t + 2] * inv, o[8 * t + 3] * inv);
+                    w.z = pack_bf16(o[8 * t + 4] * inv, o[8 * t + 5] * inv);
+                    w.w = pack_bf16(o[8 * t + 6] * inv, o[8 * t + 7] * inv);
+                    dst[t] = w;
                 }
             }
         }
@@ -299,7 +409,7 @@ bool launch_attn(cudaStream_t st, const void *qkv, int N, int Dm, int heads, voi
     static unsigned done = 0;
     if (!smem_opt_in((const void *)tc_attn_kernel<D>, smem, &done))
         return false;
-    tc_attn_kernel<D><<<dim3(cdiv(N, BQ), heads, nimg), 192, smem, st>>>(map, p);
+    tc_attn_kernel<D><<<dim3(cdiv(N, BQ), heads, nimg), ATT_THREADS, smem, st>>>(map, p);
     return true;
 }
 
