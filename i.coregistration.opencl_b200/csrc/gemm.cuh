@@ -106,6 +106,11 @@ void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, i
 // 128 and the pointers are 16-byte aligned.
 bool dwpw_tc(cudaStream_t st, const void *in, int H, int W, int C, const float *dw_w,
              const float *dw_b, const void *pw_w, const float *pw_b, void *out, int sm_count);
+// The depthwise 5 x 5 convolution + bias + ReLU of a refiner block alone
+// (tc_dwpw.cu), channels-last bfloat16 in and out, C a multiple of 64;
+// false (nothing launched) otherwise.
+bool dw5_tc(cudaStream_t st, const void *in, int H, int W, int C, const float *dw_w,
+            const float *dw_b, void *out, int sm_count);
 // Double-precision GP solve (gp_chol.cu); work holds gp_work_doubles(n, d).
 size_t gp_work_doubles(int n, int d);
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F, int d,

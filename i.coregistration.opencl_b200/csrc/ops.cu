@@ -723,6 +723,77 @@ __global__ void layernorm_kernel(const float *X, TO *Y, const float *g,
     }
 }
 
+// The same for rows of C = 128 nv floats (nv <= 16): one warp per row,
+// held in registers (lane l takes float4 l, l + 32, ...), both passes
+// from registers with warp reductions, 8 rows per block. Y may alias X.
+__device__ __forceinline__ void store4(float *y, float4 v) { *(float4 *)y = v; }
+
+__device__ __forceinline__ void store4(__nv_bfloat16 *y, float4 v)
+{
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *(const uint32_t *)&a;
+    u.y = *(const uint32_t *)&b;
+    *(uint2 *)y = u;
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(256)
+layernorm_warp_k(const float *X, TO *Y, const float *g, const float *bt, long rows, int nv,
+                 float eps, int act, float slope)
+{
+    constexpr int NVMAX = 16;
+    const int lane = threadIdx.x % 32;
+    const long row = (long)blockIdx.x * 8 + threadIdx.x / 32;
+    if (row >= rows)
+        return;
+    const int C = 128 * nv;
+    const float4 *x = (const float4 *)(X + row * C);
+    float4 v[NVMAX];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NVMAX; i++)
+        if (i < nv) {
+            v[i] = x[lane + 32 * i];
+            s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / C;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NVMAX; i++)
+        if (i < nv) {
+            const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean,
+                        d = v[i].w - mean;
+            q = fmaf(a, a, q);
+            q = fmaf(b, b, q);
+            q = fmaf(c, c, q);
+            q = fmaf(d, d, q);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float r = rsqrtf(q / C + eps);
+    TO *y = Y + row * C;
+#pragma unroll
+    for (int i = 0; i < NVMAX; i++)
+        if (i < nv) {
+            const int c = 4 * (lane + 32 * i);
+            float4 o = make_float4((v[i].x - mean) * r, (v[i].y - mean) * r,
+                                   (v[i].z - mean) * r, (v[i].w - mean) * r);
+            if (g) {
+                const float4 gg = *(const float4 *)(g + c), bb = *(const float4 *)(bt + c);
+                o = make_float4(o.x * gg.x + bb.x, o.y * gg.y + bb.y, o.z * gg.z + bb.z,
+                                o.w * gg.w + bb.w);
+            }
+            o = make_float4(apply_act(o.x, act, slope), apply_act(o.y, act, slope),
+                            apply_act(o.z, act, slope), apply_act(o.w, act, slope));
+            store4(y + c, o);
+        }
+}
+
 namespace coreg {
 void layernorm_rows(cudaStream_t st, const float *X, void *Y, DType ty,
                     const float *g, const float *b, long rows, int C, float eps,
@@ -731,6 +802,17 @@ void layernorm_rows(cudaStream_t st, const float *X, void *Y, DType ty,
     const int t = C >= 512 ? 256 : C >= 128 ? 128 : 32;
     if (rows <= 0)
         return;
+    if (C % 128 == 0 && C <= 2048 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)Y & 15) == 0 &&
+        (!g || (((uintptr_t)g & 15) == 0 && ((uintptr_t)b & 15) == 0))) {
+        const unsigned blocks = (unsigned)((rows + 7) / 8);
+        if (ty == DT_BF16)
+            layernorm_warp_k<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+                X, (__nv_bfloat16 *)Y, g, b, rows, C / 128, eps, act, slope);
+        else
+            layernorm_warp_k<float><<<blocks, 256, 0, st>>>(X, (float *)Y, g, b, rows, C / 128,
+                                                            eps, act, slope);
+        return;
+    }
     if (ty == DT_BF16)
         layernorm_kernel<__nv_bfloat16><<<(unsigned)rows, t, 0, st>>>(
             X, (__nv_bfloat16 *)Y, g, b, C, eps, act, slope);

@@ -10,6 +10,7 @@
 
 #include <math.h>
 
+#include "gemm.cuh"
 #include "roma_kernels.cuh"
 
 namespace coreg {
@@ -703,6 +704,11 @@ template <typename TI, typename TO>
 static void dwconv5_t(cudaStream_t st, Map in, int C, int H, int W,
                       const float *w, const float *b, MapOut out)
 {
+    // Dense bfloat16 maps of a multiple of 64 channels: the TMA-fed kernel
+    // (tc_dwpw.cu).
+    if (sizeof(TI) == 2 && sizeof(TO) == 2 && in.cs == 1 && out.cs == 1 && in.ps == C &&
+        out.ps == C && C % 64 == 0 && dw5_tc(st, in.p, H, W, C, w, b, out.p, 0))
+        return;
     if (sizeof(TI) == 2 && sizeof(TO) == 2 && in.cs == 1 && out.cs == 1 && C % 8 == 0 &&
         in.ps % 8 == 0 && out.ps % 2 == 0 && ((uintptr_t)in.p & 15) == 0 &&
         ((uintptr_t)out.p & 3) == 0) {
@@ -762,12 +768,41 @@ __global__ void maxpool2_tm_k(const T *in, int H, int W, int C, T *out)
     stf(out + e, v);
 }
 
+// bfloat16 with C a multiple of 8: one thread per output pixel and 8
+// channels, 16-byte loads and store (max of bfloat16 values is exact in
+// bfloat16).
+__global__ void maxpool2_tm8_k(const uint4 *in, int H, int W, int C8, uint4 *out)
+{
+    const int w2 = W / 2, h2 = H / 2;
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)h2 * w2 * C8)
+        return;
+    const int c = (int)(e % C8);
+    const long o = e / C8;
+    const int x = (int)(o % w2), y = (int)(o / w2);
+    const uint4 *p = in + ((long)(2 * y) * W + 2 * x) * C8 + c;
+    const uint4 a = p[0], b = p[C8], d = p[(long)W * C8], f = p[(long)W * C8 + C8];
+    const __nv_bfloat162 *pa = (const __nv_bfloat162 *)&a, *pb = (const __nv_bfloat162 *)&b,
+                         *pd = (const __nv_bfloat162 *)&d, *pf = (const __nv_bfloat162 *)&f;
+    uint4 r;
+    __nv_bfloat162 *pr = (__nv_bfloat162 *)&r;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        pr[i] = __hmax2(__hmax2(pa[i], pb[i]), __hmax2(pd[i], pf[i]));
+    out[e] = r;
+}
+
 void maxpool2_tm(cudaStream_t st, const void *in, DType t, int H, int W, int C,
                  void *out)
 {
     const long tot = (long)(H / 2) * (W / 2) * C;
     if (tot <= 0)
         return;
+    if (t == DT_BF16 && C % 8 == 0 && ((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+        maxpool2_tm8_k<<<cdiv(tot / 8, 256), 256, 0, st>>>((const uint4 *)in, H, W, C / 8,
+                                                          (uint4 *)out);
+        return;
+    }
     if (t == DT_BF16)
         maxpool2_tm_k<__nv_bfloat16><<<cdiv(tot, 256), 256, 0, st>>>(
             (const __nv_bfloat16 *)in, H, W, C, (__nv_bfloat16 *)out);

@@ -108,6 +108,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
                  : "memory");
 }
 
+// Untiled bulk copy of bytes (a multiple of 16, both addresses 16-byte
+// aligned) from global memory, completing on the mbarrier.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(bar))
+                 : "memory");
+}
+
 // 3-D box (innermost coordinate x first); coordinates outside the tensor
 // (negative ones included) read zeros.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,

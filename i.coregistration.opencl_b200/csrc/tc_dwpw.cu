@@ -100,16 +100,44 @@ struct DwParams {
     const float *dw_w, *dw_b, *pw_b;
 };
 
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
+// Float32 pairs packed in one 64-bit register pair for the sm_100a f32x2
+// FMA; the accumulators and weights stay packed through the convolution,
+// so that no moves split and rejoin them around each instruction.
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 pk2(float lo, float hi)
 {
-    unsigned long long aa, bb, cc, dd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(cc) : "f"(c.x), "f"(c.y));
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dd) : "l"(aa), "l"(bb), "l"(cc));
+    u64 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ float2 upk2(u64 v)
+{
     float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(v));
     return d;
+}
+
+__device__ __forceinline__ u64 fma2p(u64 a, u64 b, u64 c)
+{
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// A bfloat16 pair (low half first) as packed floats.
+__device__ __forceinline__ u64 bf2(uint32_t u)
+{
+    return pk2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+// relu of a packed pair, rounded to a bfloat16 pair.
+__device__ __forceinline__ uint32_t relu_bf2(u64 v)
+{
+    const float2 f = upk2(v);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(fmaxf(f.x, 0.0f), fmaxf(f.y, 0.0f));
+    return *(const uint32_t *)&h;
 }
 
 template <int C>
@@ -183,28 +211,26 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
                 break;
             const uint32_t *pb = s.patch[i % G::NH];
             const int kb = i % G::NKB, c = kb * G::CK + 2 * pair;
-            float2 acc[G::SPX];
-            const float2 bb = *(const float2 *)&s.dwb[c];
+            u64 acc[G::SPX];
+            const u64 bb = *(const u64 *)&s.dwb[c];
 #pragma unroll
             for (int o = 0; o < G::SPX; o++)
                 acc[o] = bb;
 #pragma unroll
             for (int a = 0; a < 5; a++) {
-                float2 w[5];
+                u64 w[5];
 #pragma unroll
                 for (int k = 0; k < 5; k++)
-                    w[k] = s.dw[kb][a * 5 + k][pair];
+                    w[k] = *(const u64 *)&s.dw[kb][a * 5 + k][pair];
                 const uint32_t *rp = pb + (row + a) * G::RPW + px0 * G::NP + pair;
 #pragma unroll
                 for (int x = 0; x < G::SPX + 4; x++) {
-                    const uint32_t u = rp[x * G::NP];
-                    const float2 v =
-                        make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+                    const u64 v = bf2(rp[x * G::NP]);
 #pragma unroll
                     for (int k = 0; k < 5; k++) {
                         const int ox = x - k;
                         if (ox >= 0 && ox < G::SPX)
-                            acc[ox] = fma2(v, w[k], acc[ox]);
+                            acc[ox] = fma2p(v, w[k], acc[ox]);
                     }
                 }
             }
@@ -216,9 +242,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
 #pragma unroll
             for (int o = 0; o < G::SPX; o++) {
                 const int m = row * TX + px0 + o;
-                const __nv_bfloat162 h =
-                    __floats2bfloat162_rn(fmaxf(acc[o].x, 0.0f), fmaxf(acc[o].y, 0.0f));
-                ab[m * 32 + ((chunk ^ (m & 7)) << 2) + sub] = *(const uint32_t *)&h;
+                ab[m * 32 + ((chunk ^ (m & 7)) << 2) + sub] = relu_bf2(acc[o]);
             }
             fence_async_smem();
             __syncwarp();
@@ -387,6 +411,173 @@ bool launch_dwpw(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, const f
     return true;
 }
 
+// ------------------------------------------------ depthwise convolution
+//
+// The depthwise 5 x 5 convolution + bias + ReLU alone, for the refiners too
+// wide for the fused kernel (C a multiple of 64). Output tiles of 16 x 16
+// pixels x 64 channels; the 20 x 20-pixel input patch of each (tile,
+// k-block) arrives by TMA in a ring of three buffers. Each producer thread
+// computes two adjacent output rows of 8 pixels for one channel pair, so
+// that every patch value it loads feeds up to ten packed FMAs (float32, the
+// taps in the reference's order), and writes the bfloat16 result straight
+// to global memory (a warp stores the 64 channels of one pixel, 128
+// contiguous bytes). The weights are staged once per CTA in shared memory,
+// tap-major with channel pairs innermost, and a thread's 25 weight pairs
+// are reloaded from there (conflict-free) when the k-block changes; items
+// (tile, k-block) go in k-block-major order over all CTAs. For maps of at
+// least one tile per CTA: smaller ones spend more on the staging than it
+// saves.
+
+constexpr int DW5_WARPS = 16;                    // producer warps (thread 0 loads)
+constexpr int DW5_THREADS = DW5_WARPS * 32;
+constexpr int DW5_NHMAX = 3;
+constexpr int DW5_TY = 16, DW5_PY = DW5_TY + 4;  // tile rows, patch rows
+constexpr int DW5_PATCH_WORDS = DW5_PY * PX * 32;  // 64 channels: 32 words a pixel
+
+// Dynamic shared memory: nh patch buffers, then the weights (C / 64
+// k-blocks x 25 taps x 32 channel pairs, float pairs), then the barriers.
+struct Dw5Layout {
+    int nh;
+    size_t w_off, bar_off, bytes;
+};
+
+__host__ __device__ inline Dw5Layout dw5_layout(int C)
+{
+    Dw5Layout l;
+    l.nh = C <= 512 ? 3 : 2;
+    l.w_off = (size_t)l.nh * DW5_PATCH_WORDS * 4;
+    l.bar_off = l.w_off + (size_t)C * 25 * 4;
+    l.bytes = l.bar_off + 2 * DW5_NHMAX * 8;
+    return l;
+}
+
+struct Dw5Params {
+    __nv_bfloat16 *out;
+    const float *dw_w, *dw_b;
+    int H, W, C, tiles_x, ntiles;
+};
+
+__global__ void __launch_bounds__(DW5_THREADS, 1)
+dw5_kernel(const __grid_constant__ CUtensorMap tma_in, Dw5Params p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+    const Dw5Layout L = dw5_layout(p.C);
+    const int NH = L.nh;
+    uint32_t *patch = (uint32_t *)base;
+    float2 *wsm = (float2 *)(base + L.w_off);
+    uint64_t *pfull = (uint64_t *)(base + L.bar_off), *pempty = pfull + DW5_NHMAX;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const long nall = (long)p.ntiles * (p.C / 64);
+    const int nitems =
+        nall > (long)blockIdx.x ? (int)((nall - (long)blockIdx.x + gridDim.x - 1) / gridDim.x) : 0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NH; i++) {
+            mbar_init(&pfull[i], 1);
+            mbar_init(&pempty[i], DW5_WARPS);
+        }
+        mbar_fence_init();
+    }
+    // Weights [c][25] -> [c / 64][tap][(c % 64) / 2], coalesced reads.
+    for (int e = threadIdx.x; e < p.C * 25; e += DW5_THREADS) {
+        const int c = e / 25, tap = e - c * 25;
+        float *d = (float *)&wsm[((c >> 6) * 25 + tap) * 32 + ((c & 63) >> 1)];
+        d[c & 1] = __ldg(p.dw_w + e);
+    }
+    __syncthreads();
+    auto item = [&](int i, int *t, int *kb) {
+        const int g = (int)blockIdx.x + i * (int)gridDim.x;
+        *kb = g / p.ntiles;
+        *t = g - *kb * p.ntiles;
+    };
+    // Thread 0 loads item i into buffer i % NH once every warp has released
+    // the buffer's previous item.
+    auto fetch = [&](int i) -> bool {
+        const int buf = i % NH, use = i / NH;
+        if (use > 0 && !mbar_wait(&pempty[buf], (use - 1) & 1, 31))
+            return false;
+        int t, kb;
+        item(i, &t, &kb);
+        const int ty = t / p.tiles_x, x0 = (t - ty * p.tiles_x) * TX - 2;
+        const int y0 = ty * DW5_TY - 2;
+        mbar_expect_tx(&pfull[buf], (uint32_t)(DW5_PATCH_WORDS * 4));
+        tma_load_3d(patch + (size_t)buf * DW5_PATCH_WORDS, &tma_in, &pfull[buf], kb * 64, x0, y0);
+        return true;
+    };
+    bool loading = true;
+    if (threadIdx.x == 0)
+        for (int i = 0; i < NH - 1 && i < nitems && loading; i++)
+            loading = fetch(i);
+    {
+        const int row = 2 * (warp >> 1), px0 = 8 * (warp & 1), pair = lane;
+        int cur = -1;
+        u64 w[25], bb = 0;
+        for (int i = 0; i < nitems; i++) {
+            int t, kb;
+            item(i, &t, &kb);
+            const int c = kb * 64 + 2 * pair;
+            if (kb != cur) {
+#pragma unroll
+                for (int k = 0; k < 25; k++)
+                    w[k] = *(const u64 *)&wsm[(kb * 25 + k) * 32 + pair];
+                bb = pk2(__ldg(p.dw_b + c), __ldg(p.dw_b + c + 1));
+                cur = kb;
+            }
+            if (threadIdx.x == 0 && loading && i + NH - 1 < nitems)
+                loading = fetch(i + NH - 1);
+            const int buf = i % NH;
+            if (!__all_sync(0xffffffffu, mbar_wait(&pfull[buf], (i / NH) & 1, 32)))
+                break;
+            const uint32_t *pb = patch + (size_t)buf * DW5_PATCH_WORDS;
+            // Output rows row (acc0) and row + 1 (acc1) from patch rows
+            // row .. row + 5: patch row j is tap row j of the first and j - 1
+            // of the second.
+            u64 acc0[8], acc1[8];
+#pragma unroll
+            for (int o = 0; o < 8; o++)
+                acc0[o] = acc1[o] = bb;
+#pragma unroll
+            for (int j = 0; j < 6; j++) {
+                const uint32_t *rp = pb + (row + j) * (PX * 32) + px0 * 32 + pair;
+#pragma unroll
+                for (int x = 0; x < 12; x++) {
+                    const u64 v = bf2(rp[x * 32]);
+#pragma unroll
+                    for (int k = 0; k < 5; k++) {
+                        const int ox = x - k;
+                        if (ox >= 0 && ox < 8) {
+                            if (j < 5)
+                                acc0[ox] = fma2p(v, w[j * 5 + k], acc0[ox]);
+                            if (j > 0)
+                                acc1[ox] = fma2p(v, w[(j - 1) * 5 + k], acc1[ox]);
+                        }
+                    }
+                }
+            }
+            // This warp is done with the patch.
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&pempty[buf]);
+            const int ty = t / p.tiles_x;
+            const int y = ty * DW5_TY + row, xb = (t - ty * p.tiles_x) * TX + px0;
+            if (y < p.H) {
+                __nv_bfloat16 *o = p.out + ((long)y * p.W + xb) * p.C + c;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (xb + k < p.W)
+                        *(uint32_t *)(o + (long)k * p.C) = relu_bf2(acc0[k]);
+            }
+            if (y + 1 < p.H) {
+                __nv_bfloat16 *o = p.out + ((long)(y + 1) * p.W + xb) * p.C + c;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (xb + k < p.W)
+                        *(uint32_t *)(o + (long)k * p.C) = relu_bf2(acc1[k]);
+            }
+        }
+    }
+}
+
 }  // namespace
 
 int dwpw_status()
@@ -399,6 +590,42 @@ int dwpw_status()
 }
 
 }  // namespace tc
+
+bool dw5_tc(cudaStream_t st, const void *in, int H, int W, int C, const float *dw_w,
+            const float *dw_b, void *out, int sm_count)
+{
+    if (sm_count <= 0)
+        sm_count = 148;
+    if (H < 1 || W < 1 || C < 64 || C % 64 || ((uintptr_t)in & 15) || ((uintptr_t)out & 3) ||
+        ((uintptr_t)dw_w & 15))
+        return false;
+    CUtensorMap mi;
+    if (!tc::make_map_hwc(&mi, const_cast<void *>(in), H, W, C, 64, tc::PX, tc::DW5_PY, 0))
+        return false;
+    tc::Dw5Params p;
+    p.out = (__nv_bfloat16 *)out;
+    p.dw_w = dw_w;
+    p.dw_b = dw_b;
+    p.H = H;
+    p.W = W;
+    p.C = C;
+    p.tiles_x = cdiv(W, tc::TX);
+    const long ntiles = (long)p.tiles_x * cdiv(H, tc::DW5_TY);
+    const long nall = ntiles * (C / 64);
+    if (nall >= (1L << 30) || ntiles < sm_count)
+        return false;
+    p.ntiles = (int)ntiles;
+    const size_t smem = tc::dw5_layout(C).bytes + 1024;
+    if (smem > 227 * 1024)
+        return false;
+    // The opt-in covers the largest layout once per device.
+    static unsigned done = 0;
+    if (!tc::smem_opt_in((const void *)tc::dw5_kernel, 227 * 1024, &done))
+        return false;
+    const int grid = (int)(nall < sm_count ? nall : sm_count);
+    tc::dw5_kernel<<<grid, tc::DW5_THREADS, smem, st>>>(mi, p);
+    return true;
+}
 
 bool dwpw_tc(cudaStream_t st, const void *in, int H, int W, int C, const float *dw_w,
              const float *dw_b, const void *pw_w, const float *pw_b, void *out, int sm_count)

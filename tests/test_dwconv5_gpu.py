@@ -17,6 +17,8 @@ SHAPES = [
     # H, W, C
     (40, 40, 32),
     (37, 53, 128),   # ragged pixel tiles
+    (45, 70, 512),   # eight 64-channel k-blocks
+    (200, 208, 128), # at least one 16 x 16 tile per SM: the TMA-fed bfloat16 kernel
     (16, 20, 48),    # a partial 32-channel block
     (9, 9, 8),
     (11, 13, 12),    # C not a multiple of 8: the generic kernel
