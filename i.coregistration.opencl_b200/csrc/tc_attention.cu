@@ -67,7 +67,10 @@ struct AttnSmem {
     // abort[j % 2] before the block's barrier, or abort[(j + 1) % 2] after
     // it; every softmax warp reads abort[j % 2] after barrier j.
     int abort[2];
-    uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[2], p_full, pv_done[PB];
+    // p_full and pv_done per P tile: the softmax may finish block j + 1
+    // before the MMA warp has seen block j, so one barrier for both would
+    // run two phases ahead of its waiter.
+    uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[2], p_full[PB], pv_done[PB];
     uint32_t tmem;
 };
 
@@ -137,7 +140,8 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
         }
         mbar_init(&s.s_full[0], 1);
         mbar_init(&s.s_full[1], 1);
-        mbar_init(&s.p_full, SOFT_THREADS);
+        for (int i = 0; i < PB; i++)
+            mbar_init(&s.p_full[i], SOFT_THREADS);
         for (int i = 0; i < PB; i++)
             mbar_init(&s.pv_done[i], 1);
         s.abort[0] = s.abort[1] = 0;
@@ -196,7 +200,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
             if (ok)
                 ok = issue_s(0) && (nblk < 2 || issue_s(1));
             for (int j = 0; j < nblk && ok; j++) {
-                if (!mbar_wait(&s.p_full, j & 1, 14))
+                if (!mbar_wait(&s.p_full[j % PB], (j / PB) & 1, 14))
                     break;
                 fence_after();
                 const int st = j % ST;
@@ -346,7 +350,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
             l += s2.x + s2.y;
             fence_async_smem();
             fence_before();
-            mbar_arrive(&s.p_full);
+            mbar_arrive(&s.p_full[j % PB]);
         }
         if (ok && __all_sync(0xffffffffu, mbar_wait(&s.pv_done[(nblk - 1) % PB],
                                                     ((nblk - 1) / PB) & 1, 17)))
