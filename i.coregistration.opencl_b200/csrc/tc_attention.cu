@@ -393,6 +393,287 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
     }
 }
 
+// ---------------------------------------------------------- two tiles
+//
+// Head size 64: one CTA per 256 queries (two 128-query tiles t = 0, 1) of
+// one head. Each tile has its own softmax warpgroup, one thread per query
+// row with the block's 128 scores in registers, so that no warps exchange
+// row maxima; the two groups drift half a block apart, and while one
+// exponentiates (the exponential unit is the bound) the other loads and
+// reduces its scores and the tensor cores work for both.
+//   warp 0      TMA: both Q tiles once, K and V blocks into a ring;
+//   warp 1      tensor memory (S_t: 128 columns at 128 t, O_t: 64 at
+//               256 + 64 t) and MMA issue, per block j in the order the
+//               groups get there: S_0(j + 1) once softmax 0 has read S_0(j)
+//               (s_free), S_1(j + 1) likewise, PV_0(j) once P_0(j) is in
+//               shared memory (p_full), PV_1(j);
+//   warps 2..5  softmax of tile 0, warps 6..9 of tile 1: S_t(j) from
+//               tensor memory, masked keys, online maximum (O_t and the row
+//               sum rescaled in tensor memory only when the maximum grows
+//               by more than 2^8), P_t(j) = exp2 as bfloat16 into the tile's
+//               128-byte swizzled P buffer (free once PV_t(j - 1) is done);
+//               at the end O_t / l to global memory.
+constexpr int ATT2_THREADS = 320;
+
+struct Attn2Smem {
+    alignas(1024) __nv_bfloat16 q[2][BQ * 64];
+    alignas(1024) __nv_bfloat16 k[3][BKV * 64];
+    alignas(1024) __nv_bfloat16 v[3][BKV * 64];
+    alignas(1024) __nv_bfloat16 p[2][2][BQ * 64];  // tile, 64-key half
+    uint64_t q_full, kv_full[3], kv_empty[3], s_full[2], s_free[2], p_full[2], pv_done[2];
+    uint32_t tmem;
+};
+
+__global__ void __launch_bounds__(ATT2_THREADS, 1)
+tc_attn2_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
+{
+    constexpr int ST = 3;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Attn2Smem &s = *reinterpret_cast<Attn2Smem *>(smem_raw +
+                                                  ((1024u - (su32(smem_raw) & 1023u)) & 1023u));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int q0 = blockIdx.x * 2 * BQ, h = blockIdx.y, img = blockIdx.z;
+    const int nblk = (p.N + BKV - 1) / BKV;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&s.q_full, 1);
+        for (int i = 0; i < ST; i++) {
+            mbar_init(&s.kv_full[i], 1);
+            mbar_init(&s.kv_empty[i], 1);
+        }
+        for (int t = 0; t < 2; t++) {
+            mbar_init(&s.s_full[t], 1);
+            mbar_init(&s.s_free[t], 4);
+            mbar_init(&s.p_full[t], 128);
+            mbar_init(&s.pv_done[t], 1);
+        }
+        mbar_fence_init();
+    }
+    if (warp == 1)
+        tmem_alloc(&s.tmem, 512);
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = s.tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t tile = BQ * 64 * 2;
+            mbar_expect_tx(&s.q_full, 2 * tile);
+            for (int t = 0; t < 2; t++)
+                tma_load_3d(s.q[t], &map, &s.q_full, h * 64, q0 + t * BQ, img);
+            for (int j = 0; j < nblk; j++) {
+                const int st = j % ST;
+                if (j >= ST && !mbar_wait(&s.kv_empty[st], ((j / ST) - 1) & 1, 11))
+                    break;
+                mbar_expect_tx(&s.kv_full[st], 2 * tile);
+                tma_load_3d(s.k[st], &map, &s.kv_full[st], p.Dm + h * 64, j * BKV, img);
+                tma_load_3d(s.v[st], &map, &s.kv_full[st], 2 * p.Dm + h * 64, j * BKV, img);
+            }
+        }
+    }
+    else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_bf16(BQ, BKV, 0);
+            constexpr uint32_t id_o = idesc_bf16(BQ, 64, 1);
+            bool ok = mbar_wait(&s.q_full, 0, 12);
+            // S_t(j) = Q_t K(j)^T once softmax t has read S_t(j - 1).
+            auto issue_s = [&](int t, int j) -> bool {
+                const int st = j % ST;
+                if (t == 0 && !mbar_wait(&s.kv_full[st], (j / ST) & 1, 13))
+                    return false;
+                if (j > 0 && !mbar_wait(&s.s_free[t], (j - 1) & 1, 18))
+                    return false;
+                fence_after();
+                const uint64_t dq = sw128_desc(su32(s.q[t]));
+                const uint64_t dk = sw128_desc(su32(s.k[st]));
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    mma_bf16(tmem + 128 * t, dq + 2 * k, dk + 2 * k, id_s, k ? 1u : 0u);
+                mma_commit(&s.s_full[t]);
+                return true;
+            };
+            // O_t += P_t(j) V(j) once P_t(j) is in shared memory.
+            auto issue_pv = [&](int t, int j) -> bool {
+                if (!mbar_wait(&s.p_full[t], j & 1, 14))
+                    return false;
+                fence_after();
+                const uint32_t vbase = su32(s.v[j % ST]);
+#pragma unroll
+                for (int a = 0; a < 2; a++) {
+                    const uint64_t dp = sw128_desc(su32(s.p[t][a]));
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        // 16 keys from key a 64 + 16 k: V rows of 128 bytes.
+                        const uint64_t dv =
+                            sw128_desc(vbase + (uint32_t)(a * 64 + k * 16) * 128, BKV * 128, 1024);
+                        mma_bf16(tmem + 256 + 64 * t, dp + 2 * k, dv, id_o,
+                                 (j | a | k) ? 1u : 0u);
+                    }
+                }
+                mma_commit(&s.pv_done[t]);
+                return true;
+            };
+            if (ok)
+                ok = issue_s(0, 0) && issue_s(1, 0);
+            for (int j = 0; j < nblk && ok; j++) {
+                if (j + 1 < nblk)
+                    ok = issue_s(0, j + 1) && issue_s(1, j + 1);
+                ok = ok && issue_pv(0, j) && issue_pv(1, j);
+                if (ok)
+                    mma_commit(&s.kv_empty[j % ST]);
+            }
+        }
+    }
+    else {
+        const int t = (warp - 2) / 4, qd = warp % 4, r = 32 * qd + lane;
+        const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+        const uint32_t tS = tmem + lane_off + 128 * t, tO = tmem + lane_off + 256 + 64 * t;
+        float m_used = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nblk; j++) {
+            // Waits decided per warp: the TMEM accesses are warp-collective.
+            if (!__all_sync(0xffffffffu, mbar_wait(&s.s_full[t], j & 1, 15))) {
+                ok = false;
+                break;
+            }
+            fence_after();
+            float sv[BKV];
+#pragma unroll
+            for (int c = 0; c < BKV / 32; c++)
+                tmem_ld32(tS + 32 * c, sv + 32 * c);
+            // S_t's columns are free for S_t(j + 1).
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&s.s_free[t]);
+            const int kvalid = p.N - j * BKV;
+            if (kvalid < BKV) {
+#pragma unroll
+                for (int i = 0; i < BKV; i++)
+                    if (i >= kvalid)
+                        sv[i] = -INFINITY;
+            }
+            float m4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                m4[i] = sv[i];
+#pragma unroll
+            for (int i = 4; i < BKV; i++)
+                m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
+            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
+            const float m_new = fmaxf(m_used, mx);
+            const bool need = j > 0 && m_new > m_used + 8.0f;
+            const bool rescale = __any_sync(0xffffffffu, need);
+            // PV_t(j - 1) is done: O_t final up to block j - 1, the P
+            // buffer free.
+            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&s.pv_done[t], (j - 1) & 1, 16))) {
+                ok = false;
+                break;
+            }
+            fence_after();
+            if (j == 0)
+                m_used = m_new;
+            else if (rescale) {
+                // The whole warp rescales (warp-collective TMEM access),
+                // the rows that keep their maximum by 1.
+                const float corr = need ? exp2f(m_used - m_new) : 1.0f;
+                l *= corr;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    float o[16];
+                    tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        o[i] *= corr;
+                    tmem_st16(tO + 16 * c, o);
+                }
+                if (need)
+                    m_used = m_new;
+            }
+            float2 s2 = make_float2(0.0f, 0.0f);
+            const float2 sc = make_float2(p.scale_log2, p.scale_log2);
+            const float2 mm = make_float2(-m_used, -m_used);
+#pragma unroll
+            for (int a = 0; a < 2; a++) {
+                unsigned char *row = (unsigned char *)s.p[t][a] + r * 128;
+#pragma unroll
+                for (int cc = 0; cc < 8; cc++) {
+                    float e[8];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int i = a * 64 + cc * 8 + 2 * u;
+                        const float2 x = ffma2(make_float2(sv[i], sv[i + 1]), sc, mm);
+                        e[2 * u] = ex2(x.x);
+                        e[2 * u + 1] = ex2(x.y);
+                        s2 = fadd2(s2, make_float2(e[2 * u], e[2 * u + 1]));
+                    }
+                    uint4 w;
+                    w.x = pack_bf16(e[0], e[1]);
+                    w.y = pack_bf16(e[2], e[3]);
+                    w.z = pack_bf16(e[4], e[5]);
+                    w.w = pack_bf16(e[6], e[7]);
+                    *reinterpret_cast<uint4 *>(row + ((cc ^ (r & 7)) << 4)) = w;
+                }
+            }
+            l += s2.x + s2.y;
+            fence_async_smem();
+            fence_before();
+            mbar_arrive(&s.p_full[t]);
+        }
+        if (ok && __all_sync(0xffffffffu, mbar_wait(&s.pv_done[t], (nblk - 1) & 1, 17))) {
+            fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const int q = q0 + t * BQ + r;
+#pragma unroll 1
+            for (int c = 0; c < 4; c++) {
+                float o[16];
+                tmem_ld16(tO + 16 * c, o);
+                if (q < p.N) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + img * p.out_img +
+                                                           (long)q * p.ldo + h * 64 + 16 * c);
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        uint4 w;
+                        w.x = pack_bf16(o[8 * u] * inv, o[8 * u + 1] * inv);
+                        w.y = pack_bf16(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
+                        w.z = pack_bf16(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
+                        w.w = pack_bf16(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
+                        dst[u] = w;
+                    }
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+bool launch_attn2(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
+                  long ldo, float scale, int nimg)
+{
+    CUtensorMap map;
+    if (!make_map_conv(&map, qkv, nimg, N, 3 * Dm, BQ, 1))
+        return false;
+    AttnParams p;
+    p.N = N;
+    p.Dm = Dm;
+    p.out = (__nv_bfloat16 *)out;
+    p.ldo = ldo;
+    p.out_img = (long)N * ldo;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    const size_t smem = sizeof(Attn2Smem) + 1024;
+    static unsigned done = 0;
+    if (!smem_opt_in((const void *)tc_attn2_kernel, smem, &done))
+        return false;
+    tc_attn2_kernel<<<dim3(cdiv(N, 2 * BQ), heads, nimg), ATT2_THREADS, smem, st>>>(map, p);
+    return true;
+}
+
 template <int D>
 bool launch_attn(cudaStream_t st, const void *qkv, int N, int Dm, int heads, void *out,
                  long ldo, float scale, int nimg)
@@ -443,7 +724,7 @@ bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, vo
         (ldo & 7) || (Dm & 63))
         return false;
     if (d == 64)
-        return tc::launch_attn<64>(st, qkv, N, Dm, heads, out, ldo, scale, nimg);
+        return tc::launch_attn2(st, qkv, N, Dm, heads, out, ldo, scale, nimg);
     if (d == 128)
         return tc::launch_attn<128>(st, qkv, N, Dm, heads, out, ldo, scale, nimg);
     return false;
