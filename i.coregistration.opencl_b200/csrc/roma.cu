@@ -77,6 +77,10 @@ struct PilDev {
 
 }  // namespace
 
+// Row pitch (floats) of the refiners' output d_c (3 or 6 values a cell):
+// 32-byte rows, which the tensor-core GEMM writes with TMA stores.
+constexpr int DC_PITCH = 8;
+
 struct roma_impl {
     DType wt = DT_F32; // GEMM weights
     DType at = DT_F32; // activations that feed GEMMs
@@ -853,7 +857,7 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
             }
     I->d_a = dmalloc(I, dmax * as, "refiner");
     I->d_b = dmalloc(I, dmax * as, "refiner");
-    I->d_c = (float *)dmalloc(I, 6 * hm * 4, "refiner");
+    I->d_c = (float *)dmalloc(I, (size_t)DC_PITCH * hm * 4, "refiner");
     for (int k = 0; k < 2; k++) {
         I->fl[k] = (float *)dmalloc(I, 2 * hm * 4, "warp");
         I->ce[k] = (float *)dmalloc(I, hm * 4, "certainty");
@@ -1343,7 +1347,7 @@ void refiner_body(Ctx &c, const Refiner &r, const void *fa, const void *fb,
                 x, r.cinp, at, ACTF_NONE, false);
     }
     gemm_nt(c, "refiner_out", (int)n, r.nout, r.cinp, x, r.cinp, at, r.out_w, r.out_b,
-            I->d_c, r.nout, DT_F32, ACTF_NONE, false);
+            I->d_c, DC_PITCH, DT_F32, ACTF_NONE, false);
 }
 
 // ConvRefiner s on an hs x ws grid of a pass of size Hf x Wf (scale
@@ -1357,7 +1361,7 @@ void refine(Ctx &c, int s, int hs, int ws, int Hf, int Wf, float sf, float *fl,
     const DType tf = s == 0 ? DT_F32 : I->at;
     refiner_body(c, r, I->P[s][0], I->P[s][1], tf, hs, ws, fac, fac, fl);
     Prof p(c.m->ocl, "roma_update");
-    roma_update_l(c.st, fl, ce, {I->d_c, 1, r.nout, DT_F32}, hs * ws,
+    roma_update_l(c.st, fl, ce, {I->d_c, 1, DC_PITCH, DT_F32}, hs * ws,
                   (float)r.scale, (float)Wf, (float)Hf);
     launch_ok("roma_update");
 }
@@ -1370,7 +1374,7 @@ void refine2(Ctx &c, int j, int hs, int ws, int Hp, int Wp, float *fl, float *cf
     refiner_body(c, r, I->P2[j][0], I->P2[j][1], I->at, hs, ws,
                  (float)Wp / ROMA2_ANCHOR, (float)Hp / ROMA2_ANCHOR, fl);
     Prof p(c.m->ocl, "roma2_update");
-    roma2_update_l(c.st, fl, cf, {I->d_c, 1, r.nout, DT_F32}, hs * ws, (float)ws,
+    roma2_update_l(c.st, fl, cf, {I->d_c, 1, DC_PITCH, DT_F32}, hs * ws, (float)ws,
                    (float)hs);
     launch_ok("roma2_update");
 }

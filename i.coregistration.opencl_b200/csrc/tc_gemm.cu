@@ -656,7 +656,10 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         if (r256 * 256 * 100 <= r128 * 128 * 115)
             return tc::launch_tc<256, 4>(st, g, sm_count);
     }
-    if (g.N <= 16)
+    // At most 16 columns: 32-wide tiles where the output takes the TMA-store
+    // epilogue (16-byte aligned rows), else 16-wide ones.
+    const int ces = g.c == DT_BF16 ? 2 : 4;
+    if (g.N <= 16 && (((uintptr_t)g.C & 15) || (g.ldc * ces) % 16))
         return tc::launch_tc<16, 8>(st, g, sm_count);
     if (g.N <= 32)
         return tc::launch_tc<32, 8>(st, g, sm_count);
