@@ -443,7 +443,7 @@ def gpu_arm(args, rank, world, local):
                 "traffic": traffic_from_profiles(dom), "launches_per_step": calls,
                 "algorithmic_per_launch": by[dom] / calls}
     tot_ms = sum(v[0] for v in prof.values())
-    shares = sorted(((k, v[0] / tot_ms) for k, v in prof.items()), key=lambda x: -x[1])[:8]
+    shares = sorted(((k, v[0] / tot_ms) for k, v in prof.items()), key=lambda x: -x[1])[:14]
     flops_pair = sum(fl.values())
 
     cpu = None

@@ -405,11 +405,120 @@ local_corr_bf16_k(const __nv_bfloat16 *f1, long ps1, const __nv_bfloat16 *f2, lo
     }
 }
 
+// The same with the channel count (NV 8-channel groups) and the lanes per
+// position (G) fixed at compile time: the G lanes of a position read
+// consecutive 16-byte pieces of its f2 row (coalesced), a few each,
+// unrolled; bfloat16 (one 16-byte load a group) or float (two) maps, dense
+// rows.
+__device__ __forceinline__ void load8(const __nv_bfloat16 *b, float v[8])
+{
+    const uint4 u = *(const uint4 *)b;
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+}
+
+__device__ __forceinline__ void load8(const float *b, float v[8])
+{
+    const float4 x = *(const float4 *)b, y = *(const float4 *)(b + 4);
+    v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+    v[4] = y.x, v[5] = y.y, v[6] = y.z, v[7] = y.w;
+}
+
+template <typename TI, typename TO, int NV, int G>
+__global__ void __launch_bounds__(128)
+local_corr_v_k(const TI *f1, long ps1, const TI *f2, long ps2, int H, int W, int r,
+               const float *flow, TO *out, long ocs, long ops, int coff)
+{
+    constexpr int C = 8 * NV;
+    __shared__ __align__(16) float a_s[4][C];
+    __shared__ float S[4][CORR_MAXPS * CORR_MAXPS];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const long n = (long)H * W;
+    const long i = (long)blockIdx.x * 4 + w;
+    if (i >= n)
+        return;
+    const int side = 2 * r + 1, ps = 2 * r + 2, P = ps * ps;
+    const float rc = rsqrtf((float)C);
+    const float ix = ((flow[i] + 1.0f) * W - 1.0f) * 0.5f;
+    const float iy = ((flow[n + i] + 1.0f) * H - 1.0f) * 0.5f;
+    const bool ok = isfinite(ix) && isfinite(iy);
+    const int x0 = ok ? (int)floorf(ix) : 0, y0 = ok ? (int)floorf(iy) : 0;
+    const float fx = ok ? ix - x0 : 0.0f, fy = ok ? iy - y0 : 0.0f;
+    const TI *a = f1 + i * ps1;
+    for (int c = lane; c < C; c += 32)
+        a_s[w][c] = ldf(a + c) * rc;
+    __syncwarp();
+    constexpr int per = 32 / G;
+    const int g = lane % G;
+    for (int e0 = 0; e0 < P; e0 += per) {
+        const int e = e0 + lane / G;
+        const int yy = y0 - r + e / ps, xx = x0 - r + e % ps;
+        float2 acc = make_float2(0.0f, 0.0f);
+        if (e < P && ok && xx >= 0 && xx < W && yy >= 0 && yy < H) {
+            const TI *b = f2 + ((long)yy * W + xx) * ps2;
+#pragma unroll
+            for (int v = g; v < NV; v += G) {
+                float x[8];
+                load8(b + 8 * v, x);
+                const float4 p0 = *(const float4 *)&a_s[w][8 * v];
+                const float4 p1 = *(const float4 *)&a_s[w][8 * v + 4];
+                acc = fma2(make_float2(x[0], x[1]), make_float2(p0.x, p0.y), acc);
+                acc = fma2(make_float2(x[2], x[3]), make_float2(p0.z, p0.w), acc);
+                acc = fma2(make_float2(x[4], x[5]), make_float2(p1.x, p1.y), acc);
+                acc = fma2(make_float2(x[6], x[7]), make_float2(p1.z, p1.w), acc);
+            }
+        }
+        float sum = acc.x + acc.y;
+#pragma unroll
+        for (int o = G / 2; o > 0; o /= 2)
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (g == 0 && e < P)
+            S[w][e] = sum;
+    }
+    __syncwarp();
+    for (int k = lane; k < side * side; k += 32) {
+        const int e0 = (k / side) * ps + k % side, e1 = e0 + ps;
+        const float v = (1.0f - fy) * ((1.0f - fx) * S[w][e0] + fx * S[w][e0 + 1]) +
+                        fy * ((1.0f - fx) * S[w][e1] + fx * S[w][e1 + 1]);
+        stf(out + (long)(coff + k) * ocs + i * ops, v);
+    }
+}
+
+// The compiled (channels, lanes per position) pairs of local_corr_v_k.
+template <typename TI, typename TO>
+static bool local_corr_v(cudaStream_t st, Map f1, Map f2, int C, int H, int W, int r,
+                         const float *flow, MapOut out, int coff)
+{
+    if (r + 1 > CORR_MAXPS / 2 || f1.cs != 1 || f2.cs != 1 || f1.ps % 8 || f2.ps % 8 || ((uintptr_t)f1.p & 15) ||
+        ((uintptr_t)f2.p & 15))
+        return false;
+    const long n = (long)H * W;
+#define LCV(NV_, G_)                                                                          \
+    if (C == 8 * NV_) {                                                            \
+        local_corr_v_k<TI, TO, NV_, G_><<<cdiv(n, 4), 128, 0, st>>>(                          \
+            (const TI *)f1.p, f1.ps, (const TI *)f2.p, f2.ps, H, W, r, flow, (TO *)out.p,      \
+            out.cs, out.ps, coff);                                                            \
+        return true;                                                                          \
+    }
+    LCV(64, 32)
+    LCV(32, 16)
+    LCV(24, 8)
+    LCV(6, 2)
+#undef LCV
+    return false;
+}
+
 template <typename TI, typename TO>
 static void local_corr_t(cudaStream_t st, Map f1, Map f2, int C, int H, int W,
                          int r, const float *flow, MapOut out, int coff)
 {
     const long n = (long)H * W;
+    if (local_corr_v<TI, TO>(st, f1, f2, C, H, W, r, flow, out, coff))
+        return;
     if (sizeof(TI) == 2 && f1.cs == 1 && f2.cs == 1 && C % 8 == 0 && f1.ps % 8 == 0 &&
         f2.ps % 8 == 0 && ((uintptr_t)f1.p & 15) == 0 && ((uintptr_t)f2.p & 15) == 0) {
         local_corr_bf16_k<TO><<<cdiv(n, 4), 128, 0, st>>>(
