@@ -208,6 +208,14 @@ struct DgBatch {
 constexpr int DG_T = 64, DG_K = 64;
 constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(double);
 
+__device__ __forceinline__ void cp_async8(double *dst, const double *src, bool in)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(in ? 8 : 0)
+                 : "memory");
+}
+
 __global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
 {
     extern __shared__ double dg_smem[];
@@ -222,17 +230,23 @@ __global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
     double acc[4][4] = {};
     const bool a_k = q.sak == 1, b_n = q.sbn == 1;
     for (int k0 = 0; k0 < K; k0 += DG_K) {
+        // Element-wise asynchronous copies (8 bytes, zero fill outside the
+        // operands): every load of the panel in flight at once, no register
+        // staging.
 #pragma unroll 4
         for (int e = threadIdx.x; e < DG_T * DG_K; e += 256) {
             int r = a_k ? e / DG_K : e % DG_T, k = a_k ? e % DG_K : e / DG_T;
             int m = m0 + r, kk = k0 + k;
-            As[k][r] = m < M && kk < K ? q.A[m * q.sam + kk * q.sak] : 0.0;
+            bool in = m < M && kk < K;
+            cp_async8(&As[k][r], in ? q.A + (long)m * q.sam + (long)kk * q.sak : q.A, in);
             r = b_n ? e % DG_T : e / DG_K;
             k = b_n ? e / DG_T : e % DG_K;
             const int nn = n0 + r;
             kk = k0 + k;
-            Bs[k][r] = nn < N && kk < K ? q.B[kk * q.sbk + nn * q.sbn] : 0.0;
+            in = nn < N && kk < K;
+            cp_async8(&Bs[k][r], in ? q.B + (long)kk * q.sbk + (long)nn * q.sbn : q.B, in);
         }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
         __syncthreads();
         const int kc = K - k0 < DG_K ? K - k0 : DG_K;
 #pragma unroll 8
