@@ -495,7 +495,7 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--tiles", type=int, default=4, help="distinct tile pairs per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--streams", type=int, default=3,
+    ap.add_argument("--streams", type=int, default=4,
                     help="concurrent tile pipelines (streams, models) per GPU")
     args = ap.parse_args()
     rank, world, local = dist_setup(args.gpus)
