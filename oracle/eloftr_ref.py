@@ -9,8 +9,10 @@ Follows i.coregistration.opencl's eloftr.c (folding :103-230, RoPE table
 convolutions, oracle/ops_ref.py's pinned LayerNorm, attention, RoPE and
 resize for the rest. The reference's own model-level compare script runs
 against transformers' EfficientLoFTRForKeypointMatching; this restatement
-is pinned to that model through the coarse stage by
-tests/test_eloftr_gpu.py's CPU test, where it is available.
+is pinned to that model through the coarse stage (backbone, aggregated
+attention with RoPE, coarse matches) by tests/test_eloftr_oracle.py against
+the fixture of tests/golden/make_eloftr_golden.py. The fine stage follows
+eloftr_kernels.cl and is not pinned.
 """
 
 import math
