@@ -11,12 +11,17 @@ function cites the lines it restates. The coarse-pass side is a parameter
 (roma.c fixes it at ROMA_COARSE = 560) so that the parity tests can run
 small.
 
-Parity unpinned at model level: the reference's own RoMa path needs an
-OpenCL platform to run and its model-level compare scripts need the
-upstream romatch / RoMaV2 packages, none of which is available, so this
-restatement is checked only through the generic ops it shares with
-oracle/ops_ref.py (pinned to the reference's ops_compare.py) and by
-reading the cited lines.
+Parity pinned for the encoders, unpinned after them: the reference's own
+RoMa path needs an OpenCL platform to run and its model-level compare
+scripts need the upstream romatch / RoMaV2 packages, none of which is
+available. The two encoders are pinned to the libraries RoMa builds them
+from, on the same seeded weights (tests/test_roma_oracle_pins.py): the
+DINOv2 encoder with its position interpolation to transformers' Dinov2Model
+and DINOv2's original interpolation call, the VGG19-BN pyramid to
+torchvision's vgg19_bn. The decoder, Gaussian-process embedding and
+refiners are checked through the generic ops they share with
+oracle/ops_ref.py (pinned to the reference's ops_compare.py) and by reading
+the cited lines.
 """
 
 import math
