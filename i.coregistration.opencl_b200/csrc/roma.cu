@@ -62,6 +62,7 @@ struct Block {
 struct Refiner {
     int scale, feat, emb, radius, cin, nout;
     int cinp; // cin padded (row stride of the refiner maps)
+    int fpitch; // row stride of the input feature maps (feat, padded to 8 for RoMa v2's)
     float *dw_w[ROMA_HIDDEN + 1], *dw_b[ROMA_HIDDEN + 1];
     void *pw_w[ROMA_HIDDEN + 1];
     float *pw_b[ROMA_HIDDEN + 1];
@@ -416,6 +417,7 @@ bool load_refiner(roma_impl *I, struct pth_file *pf, int s)
     const int corr = r->radius ? (2 * r->radius + 1) * (2 * r->radius + 1) : 0;
     r->cin = 2 * r->feat + r->emb + corr;
     r->cinp = pad16(r->cin);
+    r->fpitch = r->feat;
     r->nout = 3;
     const std::string pre = fmt("decoder.conv_refiner.%d", r->scale);
     if (!load_ref_blocks(I, pf, r, pre, false))
@@ -447,6 +449,8 @@ bool load_refiner2(roma_impl *I, struct pth_file *pf, int j)
     const int corr = r->radius ? (2 * r->radius + 1) * (2 * r->radius + 1) : 0;
     r->cin = 2 * r->feat + r->emb + corr;
     r->cinp = pad16(r->cin);
+    // 16-byte rows (bfloat16) for the projection's TMA-store epilogue.
+    r->fpitch = (r->feat + 7) / 8 * 8;
     r->nout = 6;
     const std::string pre = fmt("refiners.%d", r->scale);
     long sp[2] = {ref2_feat[j], ref2_in[j]}, spb[1] = {ref2_feat[j]};
@@ -867,7 +871,7 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
         for (int k = 0; k < 2; k++)
             for (int s = 0; s < ROMA2_SCALES; s++)
                 I->P2[s][k] = dmalloc(I,
-                                      (size_t)ref2_feat[s] * (I->hm / ref2_scale[s]) *
+                                      (size_t)I->ref2[s].fpitch * (I->hm / ref2_scale[s]) *
                                           (I->wm / ref2_scale[s]) * as,
                                       "projected features");
     I->cert16 = (float *)dmalloc(I, n16 * 4, "coarse certainty");
@@ -1050,7 +1054,7 @@ void vgg2(Ctx &c, int H, int W, int k)
             in = out;
         }
         gemm_nt(c, "vgg2_proj", h * w, I->ref2[r].feat, ref2_in[r], in, ref2_in[r],
-                I->at, I->proj2_w[r], I->proj2_b[r], I->P2[r][k], I->ref2[r].feat,
+                I->at, I->proj2_w[r], I->proj2_b[r], I->P2[r][k], I->ref2[r].fpitch,
                 I->at, ACTF_NONE, false);
         if (blk < 2) {
             void *out = in == I->v_a ? I->v_b : I->v_a;
@@ -1306,8 +1310,8 @@ void refiner_body(Ctx &c, const Refiner &r, const void *fa, const void *fb,
             cudaMemset2DAsync((char *)I->d_a + r.cin * es, r.cinp * es, 0,
                               (r.cinp - r.cin) * es, n, c.st);
         }
-        copy2d(c.st, fa, tf, r.feat, I->d_a, at, r.cinp, n, r.feat);
-        roma_warp_sample_l(c.st, {fb, 1, r.feat, tf}, r.feat, hs, ws, flow,
+        copy2d(c.st, fa, tf, r.fpitch, I->d_a, at, r.cinp, n, r.feat);
+        roma_warp_sample_l(c.st, {fb, 1, r.fpitch, tf}, r.feat, hs, ws, flow,
                            {I->d_a, 1, r.cinp, at}, r.feat);
         roma_disp_emb_l(c.st, flow, hs, ws, dfx, dfy, r.emb_w, r.emb_b, r.emb,
                         {I->d_a, 1, r.cinp, at}, 2 * r.feat);
@@ -1315,7 +1319,7 @@ void refiner_body(Ctx &c, const Refiner &r, const void *fa, const void *fb,
     }
     if (r.radius) {
         Prof p(c.m->ocl, "roma_local_corr");
-        roma_local_corr_l(c.st, {fa, 1, r.feat, tf}, {fb, 1, r.feat, tf}, r.feat, hs,
+        roma_local_corr_l(c.st, {fa, 1, r.fpitch, tf}, {fb, 1, r.fpitch, tf}, r.feat, hs,
                           ws, r.radius, flow, {I->d_a, 1, r.cinp, at},
                           2 * r.feat + r.emb);
         launch_ok("roma_local_corr");
