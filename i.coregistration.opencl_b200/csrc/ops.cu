@@ -391,6 +391,35 @@ __global__ void im2col3_small_k(const __nv_bfloat16 *in, int H, int W, int C, in
     *(uint4 *)(col + pix * kp + j0) = *(const uint4 *)v;
 }
 
+// The same for a compile-time channel count: one thread per pixel writes
+// its whole row (9 C values, zeros up to KP) with 16-byte stores, the 3 x 3
+// neighbourhood read once.
+template <int C, int KP>
+__global__ void im2col3_row_k(const __nv_bfloat16 *in, int H, int W, __nv_bfloat16 *col)
+{
+    const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+    if (pix >= H * W)
+        return;
+    const int px = pix % W, py = pix / W;
+    __align__(16) __nv_bfloat16 v[KP];
+#pragma unroll
+    for (int t = 0; t < 9; t++) {
+        const int xx = px + t % 3 - 1, yy = py + t / 3 - 1;
+        const bool in_map = xx >= 0 && xx < W && yy >= 0 && yy < H;
+        const __nv_bfloat16 *p = in + ((long)yy * W + xx) * C;
+#pragma unroll
+        for (int c = 0; c < C; c++)
+            v[t * C + c] = in_map ? p[c] : __float2bfloat16_rn(0.0f);
+    }
+#pragma unroll
+    for (int j = 9 * C; j < KP; j++)
+        v[j] = __float2bfloat16_rn(0.0f);
+    uint4 *dst = (uint4 *)(col + (long)pix * KP);
+#pragma unroll
+    for (int q = 0; q < KP / 8; q++)
+        dst[q] = ((const uint4 *)v)[q];
+}
+
 namespace coreg {
 
 void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, int C, int kp,
@@ -398,7 +427,10 @@ void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, i
                        float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count)
 {
     const long n = (long)H * W;
-    im2col3_small_k<<<cdiv(n * (kp / 8), 256), 256, 0, st>>>(in, H, W, C, kp, col);
+    if (C == 3 && kp == 32 && n < (1L << 31))
+        im2col3_row_k<3, 32><<<cdiv(n, 256), 256, 0, st>>>(in, H, W, col);
+    else
+        im2col3_small_k<<<cdiv(n * (kp / 8), 256), 256, 0, st>>>(in, H, W, C, kp, col);
     GemmArgs g = gemm_args((int)n, K, kp);
     g.A = col;
     g.lda = kp;
