@@ -5,8 +5,8 @@ Writes the inputs of every case of oracle/ops_cases.py (the reference's
 tests/ops_check.c cases and generator) in the folder format that
 ops_check.c produces, then runs the reference's tests/ops_compare.py
 reference functions (torch float64) on them and stores their outputs as
-float32. Needs the reference checkout (default /root/reference, or
-$COREG_REFERENCE) and torch; run from the repository root:
+float32. Needs the reference checkout ($COREG_REFERENCE, else the build
+container's copy) and torch; run from the repository root:
 
     python tests/golden/make_ops_golden.py
 """
