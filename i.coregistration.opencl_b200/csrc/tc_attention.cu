@@ -8,7 +8,10 @@
 // (N x 3 Dm bfloat16: queries, keys, values, head h at columns h D of
 // each), the output goes to the token-major (N x Dm) bfloat16 buffer.
 //
-// One CTA per 128 queries of one head; keys in blocks of 128:
+// Head size 64 (DINOv2) runs tc_attn2_kernel below: two 128-query tiles
+// per CTA with one softmax warpgroup each. Head size 128 (the RoMa decoder)
+// runs tc_attn_kernel, one CTA per 128 queries of one head; keys in blocks
+// of 128:
 //   warp 0      TMA: Q once, K and V blocks into a ring of stages;
 //   warp 1      tensor memory (512 columns: two 128-column score buffers
 //               and the D-column output) and MMA issue: S(j) = Q K(j)^T
@@ -23,8 +26,9 @@
 //               rescaled in tensor memory only when the maximum grows by
 //               more than 2^8, else the stale maximum is kept), P(j) = exp2
 //               as bfloat16 into the 128-byte swizzled shared-memory tile
-//               of the second MMA (two tiles for D 64, so that P(j) is
-//               written while the tensor cores read P(j - 1)); at the end
+//               of the second MMA (two tiles when shared memory allows, so
+//               that P(j) is written while the tensor cores read P(j - 1));
+//               at the end
 //               O / l to global memory. Four warps per scheduler, packed
 //               float pairs and independent partial maxima and sums keep
 //               the exponential unit busy.
