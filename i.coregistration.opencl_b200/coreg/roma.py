@@ -8,11 +8,29 @@ import numpy as np
 
 from . import EXTRA_SIGNATURES, OclBackend, Ops, check, load
 
-P, I, F = C.c_void_p, C.c_int, C.c_float
+P, I, F, L = C.c_void_p, C.c_int, C.c_float, C.c_long
+
+
+PTH_F32, PTH_F16, PTH_BF16, PTH_OTHER = range(4)
+PTH_MAX_DIMS = 8
+
+
+class PthTensor(C.Structure):
+    _fields_ = [
+        ("name", C.c_char_p),
+        ("ndim", I),
+        ("shape", L * PTH_MAX_DIMS),
+        ("stride", L * PTH_MAX_DIMS),
+        ("storage_offset", L),
+        ("dtype", I),
+        ("data_offset", C.c_int64),
+        ("storage_bytes", C.c_size_t),
+    ]
 
 
 class PthFile(C.Structure):
-    _fields_ = [("fp", P), ("path", C.c_char_p), ("ntensors", I), ("tensors", P)]
+    _fields_ = [("fp", P), ("path", C.c_char_p), ("ntensors", I),
+                ("tensors", C.POINTER(PthTensor))]
 
 
 class RomaModel(C.Structure):
@@ -72,6 +90,9 @@ EXTRA_SIGNATURES.update({
     "pth_find": (P, [C.POINTER(PthFile), C.c_char_p]),
     "pth_strip_prefix": (I, [C.POINTER(PthFile), C.c_char_p]),
     "pth_bytes": (C.c_double, [C.POINTER(PthFile), C.c_char_p]),
+    "pth_require": (C.POINTER(PthTensor), [C.POINTER(PthFile), C.c_char_p, I, C.POINTER(L)]),
+    "pth_numel": (L, [C.POINTER(PthTensor)]),
+    "pth_read_f32": (C.POINTER(C.c_float), [C.POINTER(PthFile), C.POINTER(PthTensor)]),
     "roma_load": (None, [C.POINTER(RomaModel), C.POINTER(Ops), C.POINTER(PthFile),
                          C.POINTER(PthFile)]),
     "roma_load_v2": (None, [C.POINTER(RomaModel), C.POINTER(PthFile)]),

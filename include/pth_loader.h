@@ -1,11 +1,13 @@
 /* SPDX-License-Identifier: Unlicense */
 
 /* Weight files of the B200 build: the reference's pth_loader.h API
- * (pth_loader.h:38-61 of i.coregistration.opencl) over safetensors files
- * (the format of the reference's Efficient LoFTR weights, and the one this
- * build's seeded weight generator writes with the reference's tensor
- * names). The torch.save zip/pickle format of the reference's other
- * checkpoints is recognised and refused with an error naming it.
+ * (pth_loader.h:38-61 of i.coregistration.opencl) over the formats the
+ * reference reads: torch.save zip archives (stored entries, zip64 aware),
+ * the legacy torch.save stream, and safetensors. The state_dict is the
+ * saved dict, or its "model" / "state_dict" entry, or its only dict of
+ * tensors; float32, float16 and bfloat16 tensors are indexed (views keep
+ * their strides and storage offsets), other dtypes are left out. Errors go
+ * through the library's fatal / recording mode (ocl_backend.h).
  *
  *   pth_open          replaces pth_loader.c:1148
  *   pth_find          replaces pth_loader.c:1228
@@ -13,7 +15,8 @@
  *   pth_strip_prefix  replaces pth_loader.c:1238
  *   pth_numel         replaces pth_loader.c:1275
  *   pth_bytes         replaces pth_loader.c:1379
- *   pth_read_f32      replaces pth_loader.c:1330 (F32 / F16 / BF16 -> F32)
+ *   pth_read_f32      replaces pth_loader.c:1330 (F32 / F16 / BF16 -> F32,
+ *                     strided views gathered in C order)
  *   pth_close         replaces pth_loader.c:1392 */
 
 #ifndef I_COREGISTRATION_B200_PTH_LOADER_H
