@@ -9,10 +9,13 @@ Follows i.coregistration.opencl's eloftr.c (folding :103-230, RoPE table
 convolutions, oracle/ops_ref.py's pinned LayerNorm, attention, RoPE and
 resize for the rest. The reference's own model-level compare script runs
 against transformers' EfficientLoFTRForKeypointMatching; this restatement
-is pinned to that model through the coarse stage (backbone, aggregated
-attention with RoPE, coarse matches) by tests/test_eloftr_oracle.py against
-the fixture of tests/golden/make_eloftr_golden.py. The fine stage follows
-eloftr_kernels.cl and is not pinned.
+is pinned to that model by tests/test_eloftr_oracle.py against the fixture
+of tests/golden/make_eloftr_golden.py: the coarse stage (backbone,
+aggregated attention with RoPE, coarse matches), the fine features (the
+model's refinement layer), and the two fine stages, which follow the
+authors' FineMatching as eloftr_kernels.cl does (the fixture restates it in
+torch on the model's own fine windows, since transformers' version
+departs from it).
 """
 
 import math
