@@ -1,5 +1,6 @@
 # SPDX-License-Identifier: Unlicense
-"""DISK keypoints (include/disk.h) and the device descriptor-distance stage
+"""DISK keypoints (include/disk.h), the device descriptor-distance stage,
+AdaLAM (include/adalam.h) and the DISK matcher (include/matcher_disk.h)
 through the C-ABI."""
 
 import ctypes as C
@@ -27,7 +28,30 @@ class DiskModel(C.Structure):
     ]
 
 
+class AdalamConfig(C.Structure):
+    _fields_ = [
+        ("area_ratio", C.c_double),
+        ("search_expansion", C.c_double),
+        ("ransac_iters", I),
+        ("min_inliers", I),
+        ("min_confidence", C.c_double),
+        ("det_thr", C.c_double),
+        ("force_seed_mnn", I),
+    ]
+
+
+class DiskMatcherConfig(C.Structure):
+    _fields_ = [("features", I), ("threshold", F), ("adalam", AdalamConfig)]
+
+
+IP, FP = C.POINTER(C.c_int), C.POINTER(C.c_float)
+
 EXTRA_SIGNATURES.update({
+    "adalam_defaults": (None, [C.POINTER(AdalamConfig)]),
+    "adalam_filter": (I, [P, I, P, I, P, P, P, C.POINTER(AdalamConfig), C.POINTER(IP),
+                          C.POINTER(FP)]),
+    "adalam_match": (I, [C.POINTER(Ops), P, P, I, P, P, I, I, C.POINTER(AdalamConfig),
+                         C.POINTER(IP), C.POINTER(FP)]),
     "disk_load": (None, [C.POINTER(DiskModel), C.POINTER(Ops), C.POINTER(PthFile)]),
     "disk_alloc": (None, [C.POINTER(DiskModel), I, I, I]),
     "disk_detect": (I, [C.POINTER(DiskModel), P, I, I, I, I, I, F, P, P, P, P]),
@@ -105,3 +129,58 @@ def nearest(dev, d1, d2, both=True):
                      score.ctypes.data, None if nn21 is None else nn21.ctypes.data)
     check(lib)
     return nn12, score, nn21
+
+
+_LIBC = C.CDLL(None)
+_LIBC.free.argtypes = [C.c_void_p]
+
+
+def adalam_config(**kw):
+    """adalam_defaults, then the given fields."""
+    cfg = AdalamConfig()
+    load().adalam_defaults(C.byref(cfg))
+    for k, v in kw.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+def take_matches(n, pairs, dist):
+    """(pairs (n, 2) int32, dist (n,) float32) copied out of the library's
+    malloc'd arrays, which are freed."""
+    out = (np.ctypeslib.as_array(pairs, (2 * n,)).reshape(n, 2).copy() if n else
+           np.zeros((0, 2), np.int32),
+           np.ctypeslib.as_array(dist, (n,)).copy() if n else np.zeros(0, np.float32))
+    _LIBC.free(C.cast(pairs, C.c_void_p))
+    _LIBC.free(C.cast(dist, C.c_void_p))
+    return out
+
+
+def adalam_filter(k1, k2, nn12, score, nn21=None, cfg=None):
+    """adalam_filter on host arrays: (pairs, dist)."""
+    lib = load()
+    cfg = cfg or adalam_config()
+    k1 = np.ascontiguousarray(k1, np.float32)
+    k2 = np.ascontiguousarray(k2, np.float32)
+    nn12 = np.ascontiguousarray(nn12, np.int32)
+    score = np.ascontiguousarray(score, np.float32)
+    nn21 = None if nn21 is None else np.ascontiguousarray(nn21, np.int32)
+    pairs, dist = IP(), FP()
+    n = lib.adalam_filter(k1.ctypes.data, len(k1), k2.ctypes.data, len(k2), nn12.ctypes.data,
+                          score.ctypes.data, None if nn21 is None else nn21.ctypes.data,
+                          C.byref(cfg), C.byref(pairs), C.byref(dist))
+    check(lib)
+    return take_matches(n, pairs, dist)
+
+
+def adalam_match(dev, k1, d1, k2, d2, cfg=None):
+    """adalam_match (nearest neighbours on dev, then AdaLAM): (pairs, dist)."""
+    lib = load()
+    cfg = cfg or adalam_config()
+    k1, k2 = (np.ascontiguousarray(k, np.float32) for k in (k1, k2))
+    d1, d2 = (np.ascontiguousarray(d, np.float32) for d in (d1, d2))
+    pairs, dist = IP(), FP()
+    n = lib.adalam_match(dev.ops_p, k1.ctypes.data, d1.ctypes.data, len(d1), k2.ctypes.data,
+                         d2.ctypes.data, len(d2), d1.shape[1], C.byref(cfg), C.byref(pairs),
+                         C.byref(dist))
+    check(lib)
+    return take_matches(n, pairs, dist)

@@ -1,9 +1,9 @@
 /* SPDX-License-Identifier: Unlicense */
 
 /* The few GRASS GIS library calls that the reference's tests/ops_check.c
- * makes, for building that test program against libcoreg_b200.so without
- * GRASS (test infrastructure: oracle/Makefile). Memory calls exit on
- * failure and G_fatal_error exits 1, as in GRASS. */
+ * and adalam.c make, for building them without GRASS (test
+ * infrastructure: oracle/Makefile). Memory calls exit on failure and
+ * G_fatal_error exits 1, as in GRASS. */
 
 #ifndef COREG_SHIM_GRASS_GIS_H
 #define COREG_SHIM_GRASS_GIS_H

@@ -1,11 +1,13 @@
 # SPDX-License-Identifier: Unlicense
 """The matcher.h device stage through the C-ABI (matcher_roma_create,
-matcher_eloftr_create; GPU): the struct matcher's alloc / run / match /
-field / destroy against the same model run directly plus the restated
-glue of the reference (oracle/matcher_ref.py: matcher_roma.c:61-178,
-matcher_eloftr.c:66-96). The model results of both routes come from the
-same kernels, so cell positions, costs and fields must agree exactly (float
-to double conversions aside)."""
+matcher_eloftr_create, matcher_disk_create; GPU): the struct matcher's
+alloc / run / match / field / destroy against the same model run directly
+plus the restated glue of the reference (oracle/matcher_ref.py:
+matcher_roma.c:61-178, matcher_eloftr.c:66-96; the DISK matcher's glue,
+matcher_disk.c:62-92, is the keypoints of each AdaLAM pair at their cells
+with the inverse confidence as cost). The model results of both routes
+come from the same kernels, so cell positions, costs and fields must agree
+exactly (float to double conversions aside)."""
 
 import ctypes as C
 import os
@@ -151,3 +153,52 @@ def test_eloftr_matcher_matches_direct_model():
     for a, b in zip(got, want):
         assert np.allclose(a[:4], b[:4], atol=1e-3)
         assert a[4] == pytest.approx(float(b[4]), abs=1e-5)
+
+
+@pytest.mark.gpu
+def test_disk_matcher_matches_direct_stages():
+    from coreg import disk as D
+    from coreg.roma import Matcher, MatchList, open_pth
+
+    H = W = 128
+    h = w = 120
+    n = 256
+    dev = coreg.Device(0, precision=coreg.OPS_FP32)
+    lib = dev.lib
+    wpath = synth.write_disk_weights(CACHE / "weights", 0)
+    pf = open_pth(lib, wpath)
+    cfg = D.DiskMatcherConfig(features=n, threshold=0.0, adalam=D.adalam_config())
+    m = Matcher()
+    lib.matcher_disk_create(C.byref(m), dev.ops_p, C.byref(pf), C.byref(cfg))
+    coreg.check(lib)
+    lib.pth_close(C.byref(pf))
+    assert m.name == b"disk" and m.multiple == D.DISK_MULTIPLE and not m.field
+    m.alloc(C.byref(m), H, W)
+    coreg.check(lib)
+    rng = np.random.default_rng(9)
+    base = np.stack([synth.band_limited(rng, H, W, 2.0) for _ in range(3)]) / 255.0
+    img1 = np.ascontiguousarray(base, np.float32)
+    img2 = np.ascontiguousarray(np.roll(base, (6, 4), (1, 2)), np.float32)
+    v1, v2m = masks(h, w)
+    t = tile_struct(img1, img2, v1, v2m, h, w)
+    m.run(C.byref(m), C.byref(t))
+    coreg.check(lib)
+    ml = MatchList()
+    got_n = m.match(C.byref(m), C.byref(t), C.byref(ml))
+    coreg.check(lib)
+    got = read_list(ml)
+    m.destroy(C.byref(m))
+
+    net = D.Disk(dev, wpath, H, W, nmax=n)
+    try:
+        xy1, _, d1 = net.detect(img1, h=h, w=w, n=n, thresh=0.0, valid=v1)
+        xy2, _, d2 = net.detect(img2, h=h, w=w, n=n, thresh=0.0, valid=v2m)
+        pairs, dist = D.adalam_match(dev, xy1, d1, xy2, d2, D.adalam_config())
+    finally:
+        net.close()
+        dev.close()
+    assert got_n == len(got) == len(pairs)
+    for g, (a, b), c in zip(got, pairs, dist):
+        assert g[:4] == (xy1[a, 0], xy1[a, 1], xy2[b, 0], xy2[b, 1])
+        assert np.float32(g[4]) == c
+        assert np.isnan(g[5]) and np.isnan(g[6])
