@@ -48,8 +48,8 @@ IP, FP = C.POINTER(C.c_int), C.POINTER(C.c_float)
 
 EXTRA_SIGNATURES.update({
     "adalam_defaults": (None, [C.POINTER(AdalamConfig)]),
-    "adalam_filter": (I, [P, I, P, I, P, P, P, C.POINTER(AdalamConfig), C.POINTER(IP),
-                          C.POINTER(FP)]),
+    "adalam_filter": (I, [C.POINTER(Ops), P, I, P, I, P, P, P, C.POINTER(AdalamConfig),
+                          C.POINTER(IP), C.POINTER(FP)]),
     "adalam_match": (I, [C.POINTER(Ops), P, P, I, P, P, I, I, C.POINTER(AdalamConfig),
                          C.POINTER(IP), C.POINTER(FP)]),
     "disk_load": (None, [C.POINTER(DiskModel), C.POINTER(Ops), C.POINTER(PthFile)]),
@@ -155,8 +155,9 @@ def take_matches(n, pairs, dist):
     return out
 
 
-def adalam_filter(k1, k2, nn12, score, nn21=None, cfg=None):
-    """adalam_filter on host arrays: (pairs, dist)."""
+def adalam_filter(k1, k2, nn12, score, nn21=None, cfg=None, dev=None):
+    """adalam_filter on host arrays, its passes on dev (a coreg.Device) or,
+    with dev None, on host threads: (pairs, dist)."""
     lib = load()
     cfg = cfg or adalam_config()
     k1 = np.ascontiguousarray(k1, np.float32)
@@ -165,7 +166,8 @@ def adalam_filter(k1, k2, nn12, score, nn21=None, cfg=None):
     score = np.ascontiguousarray(score, np.float32)
     nn21 = None if nn21 is None else np.ascontiguousarray(nn21, np.int32)
     pairs, dist = IP(), FP()
-    n = lib.adalam_filter(k1.ctypes.data, len(k1), k2.ctypes.data, len(k2), nn12.ctypes.data,
+    n = lib.adalam_filter(None if dev is None else dev.ops_p, k1.ctypes.data, len(k1),
+                          k2.ctypes.data, len(k2), nn12.ctypes.data,
                           score.ctypes.data, None if nn21 is None else nn21.ctypes.data,
                           C.byref(cfg), C.byref(pairs), C.byref(dist))
     check(lib)

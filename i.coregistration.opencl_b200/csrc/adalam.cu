@@ -9,15 +9,23 @@
 // confidence-based inlier selection (:179-209, :462-476), the refit
 // (:478-541) and the acceptance (:543-560).
 //
-// The nearest neighbours come from the device (desc_nearest). The
-// filtering runs on the host, problem by problem: a neighbourhood's
-// hypotheses need only its own samples, so the problems are spread over
-// host threads, and the one coupling between problems (the duplicate test
-// compares the last sorted residual of a problem with the first of the
-// next, as kornia's unique_consecutive over the concatenated columns does)
-// is carried as each problem's first and last residual per hypothesis.
-// Every floating-point expression keeps the reference's types and order,
-// so that the matches and confidences agree bit for bit.
+// The nearest neighbours come from the device (desc_nearest). Seeds and
+// neighbourhoods are built on the host (O(n^2) comparisons). The two
+// RANSAC passes, which are nearly all of the work (every hypothesis of
+// every neighbourhood: residuals, a sort, then the duplicate test or the
+// inlier selection), run on the device with one CTA per (hypothesis,
+// neighbourhood); the O(N) steps between them (duplicate weights, the
+// best hypothesis, the refit, the final selection) run on the host.
+// adalam_filter without a device runs the same passes on host threads
+// instead, problem by problem.
+//
+// A neighbourhood's hypotheses need only its own samples. The one
+// coupling between neighbourhoods (the duplicate test compares the last
+// sorted residual of one with the first of the next, as kornia's
+// unique_consecutive over the concatenated columns does) is carried as
+// each neighbourhood's first and last residual per hypothesis. Every
+// floating-point expression keeps the reference's types and order, so
+// that the matches and confidences agree bit for bit.
 
 #include <cuda_fp16.h>
 #include <float.h>
@@ -242,6 +250,518 @@ int emit(std::vector<Match> &m, int **pairs, float **dist)
     return k;
 }
 
+// The least-squares affinity of a problem's inliers (the first cnt of
+// order), the identity where its scale change exceeds det_thr.
+Affine refit(const Samples &s, const int *order, long cnt, double det_thr)
+{
+    const double dt2 = det_thr * det_thr;
+    double sxx[4] = {0, 0, 0, 0}, syx[4] = {0, 0, 0, 0}, xi[4];
+    for (long k = 0; k < cnt; k++) {
+        const int t = order[k];
+        const double x0 = s.x0[t], x1 = s.x1[t], y0 = s.y0[t], y1 = s.y1[t];
+        sxx[0] += x0 * x0;
+        sxx[1] += x0 * x1;
+        sxx[2] += x1 * x0;
+        sxx[3] += x1 * x1;
+        syx[0] += y0 * x0;
+        syx[1] += y0 * x1;
+        syx[2] += y1 * x0;
+        syx[3] += y1 * x1;
+    }
+    inverse2(sxx, xi);
+    double a00 = syx[0] * xi[0] + syx[1] * xi[2], a01 = syx[0] * xi[1] + syx[1] * xi[3];
+    double a10 = syx[2] * xi[0] + syx[3] * xi[2], a11 = syx[2] * xi[1] + syx[3] * xi[3];
+    // The eigenvalues of A A^T bound the affinity's scale change.
+    const double ea = a00 * a00 + a01 * a01, eb = a00 * a10 + a01 * a11;
+    const double ed = a10 * a10 + a11 * a11;
+    const double trh = 0.5 * (ea + ed), df = 0.5 * (ea - ed), disc = hypot(df, eb);
+    const double e1 = fmax(trh + disc, 0.0), e2 = fmax(trh - disc, 0.0);
+    if (e2 < 1.0 / dt2 || e1 > dt2) {
+        a00 = a11 = 1;
+        a01 = a10 = 0;
+    }
+    return {(float)a00, (float)a01, (float)a10, (float)a11};
+}
+
+// Boundaries of the duplicate test: a problem's last column equals the
+// next problem's first when their half-precision residuals agree under
+// every hypothesis.
+void join_boundaries(const Samples &s, int iters, const std::vector<float> &first,
+                     const std::vector<float> &last, std::vector<unsigned char> &eq)
+{
+    const int nr = (int)s.off.size();
+    for (int r = 0; r < nr; r++) {
+        unsigned char same = r + 1 < nr;
+        for (int it = 0; it < iters && same; it++)
+            same = last[(size_t)r * iters + it] == first[(size_t)(r + 1) * iters + it];
+        eq[s.off[r] + s.len[r] - 1] = same;
+    }
+}
+
+// The final round, shared by both paths: under the refit affinities, the
+// sorted residuals of every problem (order, sq: N each) give the duplicate
+// weights and one selection per problem.
+void final_round(const Samples &s, const std::vector<float> &sq, double min_conf,
+                 std::vector<Selection> &best)
+{
+    const int N = s.count(), nr = (int)s.off.size();
+    std::vector<unsigned char> eq(N);
+    for (int k = 0; k + 1 < N; k++)
+        eq[k] = via_half(sq[k]) == via_half(sq[k + 1]);
+    eq[N - 1] = 0;
+    std::vector<float> wt;
+    duplicate_weights(eq, wt);
+    for (int r = 0; r < nr; r++)
+        best[r] = select_inliers(sq.data() + s.off[r], wt.data() + s.off[r], s.len[r], min_conf);
+}
+
+// The hypotheses' affinities, problem-major: A[(r * iters + it)].
+std::vector<Affine> all_hypotheses(const Samples &s, const std::vector<int> &ca,
+                                   const std::vector<int> &cb)
+{
+    const int nr = (int)s.off.size(), iters = (int)ca.size();
+    std::vector<Affine> A((size_t)nr * iters);
+    for (int r = 0; r < nr; r++)
+        for (int it = 0; it < iters; it++)
+            A[(size_t)r * iters + it] = hypothesis(s, r, ca[it], cb[it]);
+    return A;
+}
+
+// ------------------------------------------------------------ host path
+
+// Both passes and the final round on host threads: best[r] and the
+// inliers inl (problem-major, the first best[r].cnt of each problem).
+void host_passes(const Samples &s, const std::vector<int> &ca, const std::vector<int> &cb,
+                 const struct adalam_config *cfg, std::vector<Selection> &best,
+                 std::vector<int> &inl)
+{
+    const int nr = (int)s.off.size(), N = s.count(), iters = (int)ca.size();
+    std::vector<unsigned char> eq(N, 1);
+    std::vector<float> first((size_t)nr * iters), last((size_t)nr * iters);
+    for_problems(nr, [&](int r, Scratch &w) {
+        const int o = s.off[r], n = s.len[r];
+        for (int it = 0; it < iters; it++) {
+            sorted_residuals(s, r, hypothesis(s, r, ca[it], cb[it]), w);
+            for (int k = 0; k + 1 < n; k++)
+                if (eq[o + k] && via_half(w.sq[k]) != via_half(w.sq[k + 1]))
+                    eq[o + k] = 0;
+            first[(size_t)r * iters + it] = via_half(w.sq[0]);
+            last[(size_t)r * iters + it] = via_half(w.sq[n - 1]);
+        }
+    });
+    join_boundaries(s, iters, first, last, eq);
+    std::vector<float> wt;
+    duplicate_weights(eq, wt);
+
+    best.assign(nr, Selection());
+    inl.assign(N, 0);
+    for_problems(nr, [&](int r, Scratch &w) {
+        const int o = s.off[r], n = s.len[r];
+        for (int it = 0; it < iters; it++) {
+            sorted_residuals(s, r, hypothesis(s, r, ca[it], cb[it]), w);
+            const Selection sel = select_inliers(w.sq.data(), wt.data() + o, n,
+                                                 cfg->min_confidence);
+            if (sel.cnt > best[r].cnt) {
+                best[r] = sel;
+                std::copy(w.order.begin(), w.order.begin() + sel.cnt, inl.begin() + o);
+            }
+        }
+    });
+
+    long total = 0;
+    for (int r = 0; r < nr; r++)
+        total += best[r].cnt;
+    if (total <= 0)
+        return;
+    std::vector<Affine> fit(nr);
+    for (int r = 0; r < nr; r++)
+        fit[r] = refit(s, inl.data() + s.off[r], best[r].cnt, cfg->det_thr);
+    std::vector<float> sq(N);
+    for_problems(nr, [&](int r, Scratch &w) {
+        sorted_residuals(s, r, fit[r], w);
+        std::copy(w.order.begin(), w.order.end(), inl.begin() + s.off[r]);
+        std::copy(w.sq.begin(), w.sq.end(), sq.begin() + s.off[r]);
+    });
+    final_round(s, sq, cfg->min_confidence, best);
+}
+
+// ---------------------------------------------------------- device path
+//
+// One CTA per (hypothesis, problem): the problem's residuals under the
+// hypothesis, a bitonic sort of (residual, sample) pairs in shared memory,
+// then either the duplicate test of adjacent columns (pass 1) or the
+// inlier selection (pass 2). The affinities come from the host (the same
+// double arithmetic as the host path); on the device every float and
+// double operation is written with its rounding intrinsic, so nothing is
+// contracted, and the residual is the correctly rounded sqrt of the
+// double sum of squares, which is what the host's hypotf returns.
+
+constexpr int DEV_THREADS = 256;
+constexpr int DEV_MAX_SAMPLES = 16384;  // Per problem: 128 KiB of sort keys.
+
+struct DevView {
+    const float *x0, *x1, *y0, *y1;
+    const int *off, *len;
+};
+
+__device__ __forceinline__ float dev_hypot(float x, float y)
+{
+    const double xd = x, yd = y;
+    return __double2float_rn(__dsqrt_rn(__dadd_rn(__dmul_rn(xd, xd), __dmul_rn(yd, yd))));
+}
+
+__device__ __forceinline__ float dev_sq(float v) { return __fmul_rn(v, v); }
+
+__device__ __forceinline__ float dev_half(float v) { return __half2float(__float2half_rn(v)); }
+
+// The smallest power of two >= n (n >= 1).
+__device__ __forceinline__ int pow2_at_least(int n)
+{
+    int p = 1;
+    while (p < n)
+        p <<= 1;
+    return p;
+}
+
+// Problem (o, n)'s residuals under A, sorted ascending by (residual,
+// sample index) into key / idx; entries n..P-1 are padding (+inf).
+__device__ void dev_sorted_residuals(const DevView &v, int o, int n, int P, const float *A,
+                                     float *key, int *idx)
+{
+    for (int k = threadIdx.x; k < P; k += blockDim.x) {
+        if (k < n) {
+            const int t = o + k;
+            const float px = __fadd_rn(__fmul_rn(A[0], v.x0[t]), __fmul_rn(A[1], v.x1[t]));
+            const float py = __fadd_rn(__fmul_rn(A[2], v.x0[t]), __fmul_rn(A[3], v.x1[t]));
+            key[k] = dev_hypot(__fsub_rn(px, v.y0[t]), __fsub_rn(py, v.y1[t]));
+            idx[k] = t;
+        }
+        else {
+            key[k] = __int_as_float(0x7f800000);
+            idx[k] = 0x7fffffff;
+        }
+    }
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j <= i)
+                    continue;
+                const float ki = key[i], kj = key[j];
+                const int ii = idx[i], ij = idx[j];
+                const bool greater = ki > kj || (ki == kj && ii > ij);
+                if (greater == ((i & size) == 0)) {
+                    key[i] = kj;
+                    key[j] = ki;
+                    idx[i] = ij;
+                    idx[j] = ii;
+                }
+            }
+            __syncthreads();
+        }
+}
+
+// Pass 1: clear eq[o + k] where sorted columns k and k + 1 differ in half
+// precision; record the first and last column of the problem.
+__global__ void __launch_bounds__(DEV_THREADS)
+    dup_k(DevView v, const float *A, int iters, unsigned char *eq, float *first, float *last)
+{
+    extern __shared__ float smem[];
+    const int it = blockIdx.x, r = blockIdx.y;
+    const int o = v.off[r], n = v.len[r], P = pow2_at_least(n);
+    float *key = smem;
+    int *idx = (int *)(smem + P);
+    const size_t h = (size_t)r * iters + it;
+    dev_sorted_residuals(v, o, n, P, A + 4 * h, key, idx);
+    for (int k = threadIdx.x; k + 1 < n; k += blockDim.x)
+        if (dev_half(dev_sq(key[k])) != dev_half(dev_sq(key[k + 1])))
+            eq[o + k] = 0;
+    if (threadIdx.x == 0) {
+        first[h] = dev_half(dev_sq(key[0]));
+        last[h] = dev_half(dev_sq(key[n - 1]));
+    }
+}
+
+// Exclusive prefix sum over the block of one double per thread, and the
+// total. Used only where every partial sum is exact, so the result is the
+// sequential one.
+__device__ double block_exclusive_sum(double x, double *total, double *warp_tot)
+{
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    double incl = x;
+    for (int d = 1; d < 32; d <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d)
+            incl = __dadd_rn(incl, y);
+    }
+    if (lane == 31)
+        warp_tot[wid] = incl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double run = 0;
+        for (int w = 0; w < nw; w++) {
+            const double t = warp_tot[w];
+            warp_tot[w] = run;
+            run = __dadd_rn(run, t);
+        }
+        warp_tot[nw] = run;
+    }
+    __syncthreads();
+    const double out = __dadd_rn(warp_tot[wid], __dsub_rn(incl, x));
+    *total = warp_tot[nw];
+    __syncthreads();
+    return out;
+}
+
+// Pass 2: the confidence-based selection of each (hypothesis, problem).
+// With exact = 1 (every column weight at least 2^-16 and at most 2^14
+// columns, so that all partial sums of weights are exact in double) the
+// sums run in parallel; otherwise one thread runs them in order.
+__global__ void __launch_bounds__(DEV_THREADS)
+    select_k(DevView v, const float *A, int iters, const float *wt, double min_conf, int exact,
+             int *cnt, double *bal, float *hi)
+{
+    extern __shared__ float smem[];
+    __shared__ double warp_tot[DEV_THREADS / 32 + 1];
+    const int it = blockIdx.x, r = blockIdx.y;
+    const int o = v.off[r], n = v.len[r], P = pow2_at_least(n);
+    float *key = smem;
+    int *idx = (int *)(smem + P);
+    const size_t h = (size_t)r * iters + it;
+    dev_sorted_residuals(v, o, n, P, A + 4 * h, key, idx);
+    double b = 0, c = 0;
+    if (exact) {
+        const int per = (n + blockDim.x - 1) / blockDim.x;
+        const int k0 = threadIdx.x * per, k1 = min(n, k0 + per);
+        double part = 0;
+        for (int k = k0; k < k1; k++)
+            if (!(dev_sq(key[k]) <= 1e-8f))
+                part = __dadd_rn(part, (double)wt[o + k]);
+        double cum = block_exclusive_sum(part, &b, warp_tot);
+        double mine = 0;
+        for (int k = k0; k < k1; k++) {
+            const float q = dev_sq(key[k]);
+            const bool perfect = q <= 1e-8f;
+            const double w = perfect ? 0.0 : (double)wt[o + k];
+            cum = __dadd_rn(cum, w);
+            if (perfect || __dmul_rn((double)q, min_conf) <= __ddiv_rn(cum, b))
+                mine = __dadd_rn(mine, w);
+        }
+        block_exclusive_sum(mine, &c, warp_tot);
+    }
+    else if (threadIdx.x == 0) {
+        for (int k = 0; k < n; k++)
+            if (!(dev_sq(key[k]) <= 1e-8f))
+                b = __dadd_rn(b, (double)wt[o + k]);
+        double cum = 0;
+        for (int k = 0; k < n; k++) {
+            const float q = dev_sq(key[k]);
+            const bool perfect = q <= 1e-8f;
+            const double w = perfect ? 0.0 : (double)wt[o + k];
+            cum = __dadd_rn(cum, w);
+            if (perfect || __dmul_rn((double)q, min_conf) <= __ddiv_rn(cum, b))
+                c = __dadd_rn(c, w);
+        }
+    }
+    if (threadIdx.x == 0) {
+        const long ct = (long)c;
+        cnt[h] = (int)ct;
+        bal[h] = b;
+        hi[h] = ct > 0 ? dev_sq(key[ct - 1]) : 0.0f;
+    }
+}
+
+// The sorted residuals of problem r under A[r]: sample order and squared
+// residuals, problem-major.
+__global__ void __launch_bounds__(DEV_THREADS)
+    order_k(DevView v, const float *A, int *order, float *sq)
+{
+    extern __shared__ float smem[];
+    const int r = blockIdx.x;
+    const int o = v.off[r], n = v.len[r], P = pow2_at_least(n);
+    float *key = smem;
+    int *idx = (int *)(smem + P);
+    dev_sorted_residuals(v, o, n, P, A + 4 * r, key, idx);
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        order[o + k] = idx[k];
+        sq[o + k] = dev_sq(key[k]);
+    }
+}
+
+// Byte offsets of the arrays in one device allocation.
+struct DevLayout {
+    size_t x0, x1, y0, y1, off, len, A, eq, first, last, wt, cnt, bal, hi, fit, order, sq, bytes;
+    DevLayout(int N, int nr, int iters)
+    {
+        size_t at = 0;
+        auto take = [&at](size_t n) {
+            const size_t p = at;
+            at += (n + 255) / 256 * 256;
+            return p;
+        };
+        const size_t H = (size_t)nr * iters;
+        x0 = take(4 * (size_t)N);
+        x1 = take(4 * (size_t)N);
+        y0 = take(4 * (size_t)N);
+        y1 = take(4 * (size_t)N);
+        off = take(4 * (size_t)nr);
+        len = take(4 * (size_t)nr);
+        A = take(16 * (H > 0 ? H : 1));
+        eq = take((size_t)N);
+        first = take(4 * H + 4);
+        last = take(4 * H + 4);
+        wt = take(4 * (size_t)N);
+        cnt = take(4 * H + 4);
+        bal = take(8 * H + 8);
+        hi = take(4 * H + 4);
+        fit = take(16 * (size_t)nr);
+        order = take(4 * (size_t)N);
+        sq = take(4 * (size_t)N);
+        bytes = at;
+    }
+};
+
+// Both passes on the device of o, the refit and final round on the host
+// (as in host_passes); false with a recorded error on failure.
+bool device_passes(struct ops *o, const Samples &s, const std::vector<int> &ca,
+                   const std::vector<int> &cb, const struct adalam_config *cfg,
+                   std::vector<Selection> &best, std::vector<int> &inl)
+{
+    using coreg::cuda_ok;
+    using coreg::launch_ok;
+    const int nr = (int)s.off.size(), N = s.count(), iters = (int)ca.size();
+    int maxlen = 0;
+    for (int r = 0; r < nr; r++)
+        maxlen = std::max(maxlen, s.len[r]);
+    if (nr > 65535) {
+        fail("adalam: %d neighbourhoods exceed the device grid", nr);
+        return false;
+    }
+    if (maxlen > DEV_MAX_SAMPLES) {
+        fail("adalam: a neighbourhood of %d matches exceeds the device limit of %d", maxlen,
+             DEV_MAX_SAMPLES);
+        return false;
+    }
+    int P = 1;
+    while (P < maxlen)
+        P <<= 1;
+    const size_t smem = (size_t)P * 8;
+    struct ocl_backend *ocl = o->ocl;
+    cudaSetDevice(ocl->device);
+    cudaStream_t st = coreg::stream_of(ocl);
+    if (!cuda_ok(cudaFuncSetAttribute(dup_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem),
+                 "adalam dup_k smem") ||
+        !cuda_ok(cudaFuncSetAttribute(select_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem),
+                 "adalam select_k smem") ||
+        !cuda_ok(cudaFuncSetAttribute(order_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem),
+                 "adalam order_k smem"))
+        return false;
+
+    const DevLayout L(N, nr, iters);
+    cl_mem buf = ocl_alloc(ocl, L.bytes, "adalam");
+    if (pending())
+        return false;
+    char *base = (char *)buf->ptr;
+    DevView v = {(const float *)(base + L.x0), (const float *)(base + L.x1),
+                 (const float *)(base + L.y0), (const float *)(base + L.y1),
+                 (const int *)(base + L.off), (const int *)(base + L.len)};
+    const std::vector<Affine> hyp = iters ? all_hypotheses(s, ca, cb) : std::vector<Affine>();
+    ocl_write(ocl, buf, L.x0, s.x0.data(), 4 * (size_t)N);
+    ocl_write(ocl, buf, L.x1, s.x1.data(), 4 * (size_t)N);
+    ocl_write(ocl, buf, L.y0, s.y0.data(), 4 * (size_t)N);
+    ocl_write(ocl, buf, L.y1, s.y1.data(), 4 * (size_t)N);
+    ocl_write(ocl, buf, L.off, s.off.data(), 4 * (size_t)nr);
+    ocl_write(ocl, buf, L.len, s.len.data(), 4 * (size_t)nr);
+    if (iters)
+        ocl_write(ocl, buf, L.A, hyp.data(), hyp.size() * sizeof(Affine));
+    cuda_ok(cudaMemsetAsync(base + L.eq, 1, (size_t)N, st), "adalam eq");
+
+    best.assign(nr, Selection());
+    inl.assign(N, 0);
+    std::vector<unsigned char> eq(N, 1);
+    std::vector<float> first((size_t)nr * iters), last((size_t)nr * iters), wt;
+    if (iters && !pending()) {
+        const dim3 grid(iters, nr);
+        dup_k<<<grid, DEV_THREADS, smem, st>>>(v, (const float *)(base + L.A), iters,
+                                               (unsigned char *)(base + L.eq),
+                                               (float *)(base + L.first),
+                                               (float *)(base + L.last));
+        if (launch_ok("adalam dup_k")) {
+            ocl_read(ocl, buf, L.eq, eq.data(), (size_t)N);
+            ocl_read(ocl, buf, L.first, first.data(), 4 * first.size());
+            ocl_read(ocl, buf, L.last, last.data(), 4 * last.size());
+        }
+    }
+    join_boundaries(s, iters, first, last, eq);
+    duplicate_weights(eq, wt);
+
+    if (iters && !pending()) {
+        // Exact parallel sums need every weight >= 2^-16 and <= 2^14 columns.
+        const float wmin = *std::min_element(wt.begin(), wt.end());
+        const int exact = wmin >= 1.0f / 65536.0f && maxlen <= 16384;
+        ocl_write(ocl, buf, L.wt, wt.data(), 4 * (size_t)N);
+        const dim3 grid(iters, nr);
+        select_k<<<grid, DEV_THREADS, smem, st>>>(
+            v, (const float *)(base + L.A), iters, (const float *)(base + L.wt),
+            cfg->min_confidence, exact, (int *)(base + L.cnt), (double *)(base + L.bal),
+            (float *)(base + L.hi));
+        std::vector<int> cnt((size_t)nr * iters);
+        std::vector<double> bal((size_t)nr * iters);
+        std::vector<float> hi((size_t)nr * iters);
+        if (launch_ok("adalam select_k")) {
+            ocl_read(ocl, buf, L.cnt, cnt.data(), 4 * cnt.size());
+            ocl_read(ocl, buf, L.bal, bal.data(), 8 * bal.size());
+            ocl_read(ocl, buf, L.hi, hi.data(), 4 * hi.size());
+        }
+        // Each problem's best hypothesis: the first with the highest count.
+        std::vector<int> best_it(nr, -1);
+        for (int r = 0; r < nr; r++)
+            for (int it = 0; it < iters; it++) {
+                const size_t h = (size_t)r * iters + it;
+                if (cnt[h] > best[r].cnt) {
+                    best[r].cnt = cnt[h];
+                    best[r].bal = bal[h];
+                    best[r].hi = hi[h];
+                    best_it[r] = it;
+                }
+            }
+        long total = 0;
+        for (int r = 0; r < nr; r++)
+            total += best[r].cnt;
+        if (total > 0 && !pending()) {
+            // The inliers of each best hypothesis, for the host's refit.
+            std::vector<Affine> A(nr);
+            for (int r = 0; r < nr; r++)
+                A[r] = hyp[(size_t)r * iters + best_it[r]];
+            ocl_write(ocl, buf, L.fit, A.data(), A.size() * sizeof(Affine));
+            order_k<<<nr, DEV_THREADS, smem, st>>>(v, (const float *)(base + L.fit),
+                                                   (int *)(base + L.order),
+                                                   (float *)(base + L.sq));
+            if (launch_ok("adalam order_k"))
+                ocl_read(ocl, buf, L.order, inl.data(), 4 * (size_t)N);
+            for (int r = 0; r < nr; r++)
+                A[r] = refit(s, inl.data() + s.off[r], best[r].cnt, cfg->det_thr);
+            ocl_write(ocl, buf, L.fit, A.data(), A.size() * sizeof(Affine));
+            order_k<<<nr, DEV_THREADS, smem, st>>>(v, (const float *)(base + L.fit),
+                                                   (int *)(base + L.order),
+                                                   (float *)(base + L.sq));
+            std::vector<float> sq(N);
+            if (launch_ok("adalam order_k")) {
+                ocl_read(ocl, buf, L.order, inl.data(), 4 * (size_t)N);
+                ocl_read(ocl, buf, L.sq, sq.data(), 4 * (size_t)N);
+            }
+            if (!pending())
+                final_round(s, sq, cfg->min_confidence, best);
+        }
+    }
+    ocl_release(&buf);
+    return !pending();
+}
+
 }  // namespace
 
 extern "C" void adalam_defaults(struct adalam_config *c)
@@ -255,8 +775,8 @@ extern "C" void adalam_defaults(struct adalam_config *c)
     c->force_seed_mnn = 0;
 }
 
-extern "C" int adalam_filter(const float *k1, int n1, const float *k2, int n2, const int *nn12,
-                             const float *score, const int *nn21,
+extern "C" int adalam_filter(struct ops *o, const float *k1, int n1, const float *k2, int n2,
+                             const int *nn12, const float *score, const int *nn21,
                              const struct adalam_config *cfg, int **pairs, float **dist)
 {
     *pairs = nullptr;
@@ -302,7 +822,6 @@ extern "C" int adalam_filter(const float *k1, int n1, const float *k2, int n2, c
     // in both images, in ascending order of score (ties by index); seeds
     // with fewer than min_inliers of them are dropped.
     Samples s;
-    std::vector<int> kept;
     std::vector<std::pair<float, int>> nb;
     for (int si : seeds) {
         const float *t1 = k1 + 2 * si, *t2 = k2 + 2 * nn12[si];
@@ -313,7 +832,6 @@ extern "C" int adalam_filter(const float *k1, int n1, const float *k2, int n2, c
         if ((int)nb.size() < cfg->min_inliers || nb.empty())
             continue;
         std::sort(nb.begin(), nb.end());
-        kept.push_back(si);
         s.off.push_back(s.count());
         s.len.push_back((int)nb.size());
         for (const auto &e : nb) {
@@ -326,7 +844,7 @@ extern "C" int adalam_filter(const float *k1, int n1, const float *k2, int n2, c
             s.kp2.push_back(q);
         }
     }
-    const int nr = (int)kept.size(), N = s.count();
+    const int nr = (int)s.off.size();
 
     std::vector<Match> out;
     if (nr == 0) {
@@ -339,102 +857,14 @@ extern "C" int adalam_filter(const float *k1, int n1, const float *k2, int n2, c
 
     std::vector<int> ca, cb;
     first_couples(cfg->ransac_iters, ca, cb);
-    const int iters = (int)ca.size();
-
-    // Pass 1, the duplicate columns: a column equals the next when their
-    // sorted squared residuals agree in half precision under every
-    // hypothesis. Inside a problem that is tracked per column; across a
-    // problem boundary through the first and last residual of each.
-    std::vector<unsigned char> eq(N, 1);
-    std::vector<float> first((size_t)nr * iters), last((size_t)nr * iters);
-    for_problems(nr, [&](int r, Scratch &w) {
-        const int o = s.off[r], n = s.len[r];
-        for (int it = 0; it < iters; it++) {
-            sorted_residuals(s, r, hypothesis(s, r, ca[it], cb[it]), w);
-            for (int k = 0; k + 1 < n; k++)
-                if (eq[o + k] && via_half(w.sq[k]) != via_half(w.sq[k + 1]))
-                    eq[o + k] = 0;
-            first[(size_t)r * iters + it] = via_half(w.sq[0]);
-            last[(size_t)r * iters + it] = via_half(w.sq[n - 1]);
-        }
-    });
-    for (int r = 0; r < nr; r++) {
-        unsigned char same = r + 1 < nr;
-        for (int it = 0; it < iters && same; it++)
-            same = last[(size_t)r * iters + it] == first[(size_t)(r + 1) * iters + it];
-        eq[s.off[r] + s.len[r] - 1] = same;
+    std::vector<Selection> best;
+    std::vector<int> inl;
+    if (o) {
+        if (!device_passes(o, s, ca, cb, cfg, best, inl))
+            return 0;
     }
-    std::vector<float> wt;
-    duplicate_weights(eq, wt);
-
-    // Pass 2: each problem's best hypothesis (the first with the highest
-    // inlier count) and its inliers.
-    std::vector<Selection> best(nr);
-    std::vector<int> inl(N);
-    for_problems(nr, [&](int r, Scratch &w) {
-        const int o = s.off[r], n = s.len[r];
-        for (int it = 0; it < iters; it++) {
-            sorted_residuals(s, r, hypothesis(s, r, ca[it], cb[it]), w);
-            const Selection sel = select_inliers(w.sq.data(), wt.data() + o, n,
-                                                 cfg->min_confidence);
-            if (sel.cnt > best[r].cnt) {
-                best[r] = sel;
-                std::copy(w.order.begin(), w.order.begin() + sel.cnt, inl.begin() + o);
-            }
-        }
-    });
-
-    long total = 0;
-    for (int r = 0; r < nr; r++)
-        total += best[r].cnt;
-    if (total > 0) {
-        // Refit: the least-squares affinity of each problem's inliers, the
-        // identity where its scale change exceeds det_thr; then one
-        // selection round under it.
-        const double dt2 = cfg->det_thr * cfg->det_thr;
-        std::vector<Affine> fit(nr);
-        for (int r = 0; r < nr; r++) {
-            double sxx[4] = {0, 0, 0, 0}, syx[4] = {0, 0, 0, 0}, xi[4];
-            for (long k = 0; k < best[r].cnt; k++) {
-                const int t = inl[s.off[r] + k];
-                const double x0 = s.x0[t], x1 = s.x1[t], y0 = s.y0[t], y1 = s.y1[t];
-                sxx[0] += x0 * x0;
-                sxx[1] += x0 * x1;
-                sxx[2] += x1 * x0;
-                sxx[3] += x1 * x1;
-                syx[0] += y0 * x0;
-                syx[1] += y0 * x1;
-                syx[2] += y1 * x0;
-                syx[3] += y1 * x1;
-            }
-            inverse2(sxx, xi);
-            double a00 = syx[0] * xi[0] + syx[1] * xi[2], a01 = syx[0] * xi[1] + syx[1] * xi[3];
-            double a10 = syx[2] * xi[0] + syx[3] * xi[2], a11 = syx[2] * xi[1] + syx[3] * xi[3];
-            // The eigenvalues of A A^T bound the affinity's scale change.
-            const double ea = a00 * a00 + a01 * a01, eb = a00 * a10 + a01 * a11;
-            const double ed = a10 * a10 + a11 * a11;
-            const double trh = 0.5 * (ea + ed), df = 0.5 * (ea - ed), disc = hypot(df, eb);
-            const double e1 = fmax(trh + disc, 0.0), e2 = fmax(trh - disc, 0.0);
-            if (e2 < 1.0 / dt2 || e1 > dt2) {
-                a00 = a11 = 1;
-                a01 = a10 = 0;
-            }
-            fit[r] = {(float)a00, (float)a01, (float)a10, (float)a11};
-        }
-        std::vector<float> sq(N);
-        for_problems(nr, [&](int r, Scratch &w) {
-            sorted_residuals(s, r, fit[r], w);
-            std::copy(w.order.begin(), w.order.end(), inl.begin() + s.off[r]);
-            std::copy(w.sq.begin(), w.sq.end(), sq.begin() + s.off[r]);
-        });
-        for (int k = 0; k + 1 < N; k++)
-            eq[k] = via_half(sq[k]) == via_half(sq[k + 1]);
-        eq[N - 1] = 0;
-        duplicate_weights(eq, wt);
-        for (int r = 0; r < nr; r++)
-            best[r] = select_inliers(sq.data() + s.off[r], wt.data() + s.off[r], s.len[r],
-                                     cfg->min_confidence);
-    }
+    else
+        host_passes(s, ca, cb, cfg, best, inl);
 
     // Accept the inliers of the confident problems that keep enough.
     for (int r = 0; r < nr; r++) {
@@ -459,12 +889,16 @@ extern "C" int adalam_match(struct ops *o, const float *k1, const float *d1, int
     *dist = nullptr;
     if (pending() || n1 <= 1 || n2 <= 1)
         return 0;
+    if (!o) {
+        fail("adalam_match: no device (ops) given");
+        return 0;
+    }
     std::vector<int> nn12(n1), nn21(cfg->force_seed_mnn ? n2 : 0);
     std::vector<float> score(n1);
     desc_nearest(o, d1, n1, d2, n2, dim, nn12.data(), score.data(),
                  cfg->force_seed_mnn ? nn21.data() : nullptr);
     if (pending())
         return 0;
-    return adalam_filter(k1, n1, k2, n2, nn12.data(), score.data(),
+    return adalam_filter(o, k1, n1, k2, n2, nn12.data(), score.data(),
                          cfg->force_seed_mnn ? nn21.data() : nullptr, cfg, pairs, dist);
 }

@@ -8,12 +8,12 @@
  *   struct adalam_config  the reference's adalam.h:11-19
  *   adalam_defaults       replaces adalam.c:23
  *   adalam_match          replaces adalam.c:300, with the ops handle of the
- *                         device that computes the nearest neighbours first
- *                         (the reference computes them on the host,
- *                         adalam.c:38-98); the filtering runs on the host,
- *                         as in the reference
+ *                         device first: the nearest neighbours (which the
+ *                         reference computes on the host, adalam.c:38-98)
+ *                         and the RANSAC passes of the filter run there
  *   adalam_filter         the filtering alone (adalam.c:320-600), given the
- *                         nearest neighbours; no counterpart in the
+ *                         nearest neighbours, on the device of o, or on
+ *                         host threads when o is NULL; no counterpart in the
  *                         reference's header
  *
  * Results are those of the reference: the same matches in the same order
@@ -48,18 +48,21 @@ void adalam_defaults(struct adalam_config *c);
  * squared distance on the device of o, with Lowe's ratio of the two
  * nearest as score, then AdaLAM. Writes the accepted matches as index
  * pairs (i1, i2) sorted by i1 then i2 into *pairs and their inverse
- * confidence into *dist (both malloc'd, NULL when there is none; free()
- * them); returns their number. */
+ * confidence into *dist (both malloc'd, free() them; NULL when n1 or n2
+ * is below 2); returns their number. */
 int adalam_match(struct ops *o, const float *k1, const float *d1, int n1, const float *k2,
                  const float *d2, int n2, int dim, const struct adalam_config *cfg, int **pairs,
                  float **dist);
 
 /* AdaLAM on given nearest neighbours: nn12 (the nearest k2 of each k1),
  * score (its ratio) and, when cfg->force_seed_mnn is set, nn21 (the
- * nearest k1 of each k2; may be NULL otherwise). Output as adalam_match. */
-int adalam_filter(const float *k1, int n1, const float *k2, int n2, const int *nn12,
-                  const float *score, const int *nn21, const struct adalam_config *cfg,
-                  int **pairs, float **dist);
+ * nearest k1 of each k2; may be NULL otherwise). The RANSAC passes run on
+ * the device of o, or on host threads when o is NULL; the results are the
+ * same. A neighbourhood may hold at most 16384 matches on the device.
+ * Output as adalam_match. */
+int adalam_filter(struct ops *o, const float *k1, int n1, const float *k2, int n2,
+                  const int *nn12, const float *score, const int *nn21,
+                  const struct adalam_config *cfg, int **pairs, float **dist);
 
 #ifdef __cplusplus
 }

@@ -1,9 +1,10 @@
 # SPDX-License-Identifier: Unlicense
 """AdaLAM (include/adalam.h) against the reference's own adalam.c,
 compiled where it lies into oracle/_ref/libadalam_ref.so by oracle/Makefile
-(test infrastructure; the tests skip when it has not been built). CPU,
-except the last test, which runs adalam_match with its nearest neighbours
-on the device.
+(test infrastructure; the tests skip when it has not been built). The
+CPU tests run adalam_filter's host path; the GPU tests run its device
+passes on the same scenes, and adalam_match with its nearest neighbours on
+the device too.
 
 The reference's adalam_match computes its nearest neighbours on the host;
 this build's adalam_filter takes them as input. The scenes use descriptors
@@ -163,6 +164,44 @@ def test_single_keypoint_gives_nothing(ref):
     nn12, score, _ = nearest_exact(d1[:1], d2)
     got_p, got_d = D.adalam_filter(k1[:1], k2, nn12, score)
     assert len(want_p) == len(got_p) == 0 and len(got_d) == 0
+
+
+@pytest.fixture(scope="module")
+def device():
+    import coreg
+
+    dev = coreg.Device(0)
+    yield dev
+    dev.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["one", "two", "repeats", "mnn", "settings", "fallback"])
+def test_device_passes_match_reference(ref, device, case):
+    """adalam_filter with its RANSAC passes on the device, given the same
+    nearest neighbours as the host path: the reference's result."""
+    cfg = D.adalam_config()
+    if case == "one":
+        sc = scene(0)
+    elif case == "two":
+        sc = scene(3, n=500, outliers=0.2, motions=2)
+    elif case == "repeats":
+        sc = scene(5, n=300, repeats=60)
+    elif case == "mnn":
+        sc, cfg = scene(6), D.adalam_config(force_seed_mnn=1)
+    elif case == "settings":
+        sc = scene(7, n=350, outliers=0.4)
+        cfg = D.adalam_config(search_expansion=4.0, ransac_iters=64, min_inliers=4,
+                              det_thr=2.0, min_confidence=50.0, area_ratio=60.0)
+    else:
+        sc = scene(9, n=5, outliers=0.0)
+    k1, d1, k2, d2 = sc
+    want_p, want_d = ref_match(ref, k1, d1, k2, d2, cfg)
+    nn12, score, nn21 = nearest_exact(d1, d2)
+    got_p, got_d = D.adalam_filter(k1, k2, nn12, score, nn21 if cfg.force_seed_mnn else None,
+                                   cfg, dev=device)
+    assert np.array_equal(got_p, want_p)
+    assert np.array_equal(got_d.view(np.uint32), want_d.view(np.uint32))
 
 
 @pytest.mark.gpu
