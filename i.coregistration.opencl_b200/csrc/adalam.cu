@@ -225,6 +225,26 @@ void for_problems(int nr, F body)
         th.join();
 }
 
+// Run fn(i) for every i < n on up to 32 host threads.
+template <class F>
+void parallel_for(int n, F fn)
+{
+    const int nt = std::max(1, std::min({n, 32, (int)std::thread::hardware_concurrency()}));
+    if (nt == 1) {
+        for (int i = 0; i < n; i++)
+            fn(i);
+        return;
+    }
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nt; t++)
+        pool.emplace_back([&, t] {
+            for (int i = t; i < n; i += nt)
+                fn(i);
+        });
+    for (auto &th : pool)
+        th.join();
+}
+
 struct Match {
     int i1, i2;
     float dist;
@@ -820,31 +840,58 @@ extern "C" int adalam_filter(struct ops *o, const float *k1, int n1, const float
 
     // Neighbourhoods: the matches within the expanded radius of the seed
     // in both images, in ascending order of score (ties by index); seeds
-    // with fewer than min_inliers of them are dropped.
-    Samples s;
-    std::vector<std::pair<float, int>> nb;
-    for (int si : seeds) {
-        const float *t1 = k1 + 2 * si, *t2 = k2 + 2 * nn12[si];
-        nb.clear();
+    // with fewer than min_inliers of them are dropped. Walking the matches
+    // in that order once sorted, each neighbourhood comes out sorted; the
+    // seeds are counted, then filled, on host threads.
+    std::vector<std::pair<float, int>> by_score(n1);
+    for (int j = 0; j < n1; j++)
+        by_score[j] = {score[j], j};
+    std::sort(by_score.begin(), by_score.end());
+    const int ns = (int)seeds.size();
+    const auto member = [&](int si, int j) {
+        return sqdist(k1 + 2 * si, k1 + 2 * j) < se1sq &&
+               sqdist(k2 + 2 * nn12[si], k2 + 2 * nn12[j]) < se2sq;
+    };
+    std::vector<int> count(ns);
+    parallel_for(ns, [&](int q) {
+        int c = 0;
         for (int j = 0; j < n1; j++)
-            if (sqdist(t1, k1 + 2 * j) < se1sq && sqdist(t2, k2 + 2 * nn12[j]) < se2sq)
-                nb.push_back({score[j], j});
-        if ((int)nb.size() < cfg->min_inliers || nb.empty())
-            continue;
-        std::sort(nb.begin(), nb.end());
-        s.off.push_back(s.count());
-        s.len.push_back((int)nb.size());
-        for (const auto &e : nb) {
-            const int j = e.second, q = nn12[j];
-            s.x0.push_back((float)((k1[2 * j] - t1[0]) / se1));
-            s.x1.push_back((float)((k1[2 * j + 1] - t1[1]) / se1));
-            s.y0.push_back((float)((k2[2 * q] - t2[0]) / se2));
-            s.y1.push_back((float)((k2[2 * q + 1] - t2[1]) / se2));
-            s.kp1.push_back(j);
-            s.kp2.push_back(q);
+            c += member(seeds[q], j);
+        count[q] = c;
+    });
+    Samples s;
+    std::vector<int> kept, at;
+    int N = 0;
+    for (int q = 0; q < ns; q++)
+        if (count[q] >= cfg->min_inliers && count[q] > 0) {
+            kept.push_back(seeds[q]);
+            s.off.push_back(N);
+            s.len.push_back(count[q]);
+            N += count[q];
         }
-    }
-    const int nr = (int)s.off.size();
+    const int nr = (int)kept.size();
+    for (auto *v : {&s.x0, &s.x1, &s.y0, &s.y1})
+        v->resize(N);
+    s.kp1.resize(N);
+    s.kp2.resize(N);
+    parallel_for(nr, [&](int r) {
+        const int si = kept[r];
+        const float *t1 = k1 + 2 * si, *t2 = k2 + 2 * nn12[si];
+        int t = s.off[r];
+        for (const auto &e : by_score) {
+            const int j = e.second;
+            if (!member(si, j))
+                continue;
+            const int q = nn12[j];
+            s.x0[t] = (float)((k1[2 * j] - t1[0]) / se1);
+            s.x1[t] = (float)((k1[2 * j + 1] - t1[1]) / se1);
+            s.y0[t] = (float)((k2[2 * q] - t2[0]) / se2);
+            s.y1[t] = (float)((k2[2 * q + 1] - t2[1]) / se2);
+            s.kp1[t] = j;
+            s.kp2[t] = q;
+            t++;
+        }
+    });
 
     std::vector<Match> out;
     if (nr == 0) {
