@@ -903,7 +903,7 @@ extern "C" int adalam_filter(struct ops *o, const float *k1, int n1, const float
     }
 
     std::vector<int> ca, cb;
-    first_couples(cfg->ransac_iters, ca, cb);
+    first_couples(std::max(0, cfg->ransac_iters), ca, cb);
     std::vector<Selection> best;
     std::vector<int> inl;
     if (o) {
