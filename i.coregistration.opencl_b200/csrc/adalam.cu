@@ -47,9 +47,32 @@ using coreg::pending;
 
 namespace {
 
-// A value rounded to IEEE binary16 and back (kornia compares the sorted
-// residuals of the hypotheses in half precision).
-inline float via_half(float v) { return __half2float(__float2half_rn(v)); }
+// A value rounded to IEEE binary16 (to nearest, ties to even) and back:
+// kornia compares the sorted residuals of the hypotheses in half
+// precision. Bit arithmetic on the float: normal halves keep 10 mantissa
+// bits, subnormal ones are multiples of 2^-24, 65520 and above overflow.
+// Equal to the compiler's float -> _Float16 -> float conversion for all
+// 2^32 inputs (checked exhaustively when this was written).
+inline float via_half(float f)
+{
+    uint32_t u, r;
+    memcpy(&u, &f, 4);
+    const uint32_t sign = u & 0x80000000u, a = u & 0x7fffffffu;
+    if (a >= 0x7f800000u)
+        r = a;
+    else if (a >= 0x477ff000u)
+        r = 0x7f800000u;
+    else if (a >= 0x38800000u)
+        r = (a + 0xfffu + ((a >> 13) & 1u)) & 0xffffe000u;
+    else {
+        const float back = nearbyintf(fabsf(f) * 16777216.0f) / 16777216.0f;
+        memcpy(&r, &back, 4);
+    }
+    r |= sign;
+    float out;
+    memcpy(&out, &r, 4);
+    return out;
+}
 
 inline float sqdist(const float *a, const float *b)
 {
@@ -325,14 +348,21 @@ void final_round(const Samples &s, const std::vector<float> &sq, double min_conf
                  std::vector<Selection> &best)
 {
     const int N = s.count(), nr = (int)s.off.size();
+    constexpr int CHUNK = 1 << 16;
+    std::vector<float> h(N);
+    parallel_for((N + CHUNK - 1) / CHUNK, [&](int c) {
+        for (int k = c * CHUNK; k < std::min(N, (c + 1) * CHUNK); k++)
+            h[k] = via_half(sq[k]);
+    });
     std::vector<unsigned char> eq(N);
     for (int k = 0; k + 1 < N; k++)
-        eq[k] = via_half(sq[k]) == via_half(sq[k + 1]);
+        eq[k] = h[k] == h[k + 1];
     eq[N - 1] = 0;
     std::vector<float> wt;
     duplicate_weights(eq, wt);
-    for (int r = 0; r < nr; r++)
+    parallel_for(nr, [&](int r) {
         best[r] = select_inliers(sq.data() + s.off[r], wt.data() + s.off[r], s.len[r], min_conf);
+    });
 }
 
 // The hypotheses' affinities, problem-major: A[(r * iters + it)].
@@ -362,11 +392,15 @@ void host_passes(const Samples &s, const std::vector<int> &ca, const std::vector
         const int o = s.off[r], n = s.len[r];
         for (int it = 0; it < iters; it++) {
             sorted_residuals(s, r, hypothesis(s, r, ca[it], cb[it]), w);
-            for (int k = 0; k + 1 < n; k++)
-                if (eq[o + k] && via_half(w.sq[k]) != via_half(w.sq[k + 1]))
+            float prev = via_half(w.sq[0]);
+            first[(size_t)r * iters + it] = prev;
+            for (int k = 0; k + 1 < n; k++) {
+                const float next = via_half(w.sq[k + 1]);
+                if (eq[o + k] && prev != next)
                     eq[o + k] = 0;
-            first[(size_t)r * iters + it] = via_half(w.sq[0]);
-            last[(size_t)r * iters + it] = via_half(w.sq[n - 1]);
+                prev = next;
+            }
+            last[(size_t)r * iters + it] = prev;
         }
     });
     join_boundaries(s, iters, first, last, eq);
