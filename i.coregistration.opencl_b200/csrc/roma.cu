@@ -616,9 +616,13 @@ bool pil_axis(roma_impl *I, int n_in, int n_out, PilDev *d)
     d->weight = (double *)dmalloc(I, wt.size() * sizeof(double), "pil");
     if (pending())
         return false;
-    cudaMemcpy(d->start, start.data(), n_out * sizeof(int), cudaMemcpyHostToDevice);
-    cudaMemcpy(d->weight, wt.data(), wt.size() * sizeof(double),
-               cudaMemcpyHostToDevice);
+    if (!cuda_ok(cudaMemcpy(d->start, start.data(), n_out * sizeof(int),
+                            cudaMemcpyHostToDevice),
+                 "RoMa resampling taps") ||
+        !cuda_ok(cudaMemcpy(d->weight, wt.data(), wt.size() * sizeof(double),
+                            cudaMemcpyHostToDevice),
+                 "RoMa resampling weights"))
+        return false;
     d->ax.n_out = n_out;
     d->ax.taps = taps;
     d->ax.start = d->start;
