@@ -18,10 +18,12 @@ available. The two encoders are pinned to the libraries RoMa builds them
 from, on the same seeded weights (tests/test_roma_oracle_pins.py): the
 DINOv2 encoder with its position interpolation to transformers' Dinov2Model
 and DINOv2's original interpolation call, the VGG19-BN pyramid to
-torchvision's vgg19_bn. The input resampling is pinned bit-exact to
-Pillow's own resize of float bands, and the refiners' local correlation to
-its sampling form through torch's grid_sample. The decoder,
-Gaussian-process embedding and the rest of the refiners are checked
+torchvision's vgg19_bn. The decoder's transformer blocks are pinned to
+transformers' Dinov2Layer configured as RoMa's decoder block, the input
+resampling bit-exact to Pillow's own resize of float bands, and the
+refiners' local correlation to its sampling form through torch's
+grid_sample. The Gaussian-process embedding, cls_to_flow and the rest of
+the refiners are checked
 through the generic ops they share with oracle/ops_ref.py (pinned to the
 reference's ops_compare.py) and by reading the cited lines.
 """

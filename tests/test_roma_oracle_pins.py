@@ -14,6 +14,11 @@ synthetic weights (CPU only, float64):
   folding, vgg roma.c:742-768) against torchvision's vgg19_bn features:
   tests/golden/vgg_golden.npz from tests/golden/make_vgg_golden.py (a
   32 x 32 input, the four block outputs). Relative L2 <= 1e-5 each.
+* the coordinate decoder's five transformer blocks (block roma.c:679-713
+  with the decoder's settings roma.c:44-46: 8 heads of 128, no qkv bias,
+  LayerNorm eps 1e-5, no LayerScale) against transformers' Dinov2Layer
+  configured alike: tests/golden/decoder_golden.npz from
+  tests/golden/make_decoder_golden.py (32 tokens). Relative L2 <= 1e-5.
 * the input resampling (prepare / resize_axis / pil_cubic,
   roma.c:1106-1186, Pillow's antialiased bicubic restated in double)
   against Pillow's own resize of float ("F" mode) bands: bit-exact, at the
@@ -74,6 +79,17 @@ def test_vgg_pyramid_matches_torchvision(model):
         want = g[name].astype(np.float64)
         assert got[name].shape == want.shape
         assert np.linalg.norm(got[name] - want) / np.linalg.norm(want) <= 1e-5, name
+
+
+def test_decoder_blocks_match_transformers(model):
+    g = np.load(GOLDEN / "decoder_golden.npz")
+    run = roma_ref.Runner(model, coarse=112, dtype=torch.float64)
+    x = torch.from_numpy(g["x"]).double()
+    for b in model.dec:
+        x = run.block(x, b, roma_ref.DEC_HEADS, roma_ref.EPS_LN_DEC)
+    want = g["out"].astype(np.float64)
+    got = x.numpy()
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-5
 
 
 @pytest.mark.parametrize("H,W,h,w", [(1024, 1024, 560, 560), (1024, 1024, 864, 864),
