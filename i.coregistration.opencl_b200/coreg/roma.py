@@ -110,6 +110,8 @@ EXTRA_SIGNATURES.update({
     "matcher_roma_create": (None, [C.POINTER(Matcher), C.POINTER(Ops), C.POINTER(PthFile),
                                    C.POINTER(PthFile), C.POINTER(PthFile), C.c_char_p, I, I, F]),
     "match_add": (None, [C.POINTER(MatchList), C.POINTER(Match)]),
+    "roma_sample_matches": (I, [P, P, P, P, I, I, I, I, I, F, P, P, C.POINTER(MatchList)]),
+    "roma_dense_field": (None, [P, P, P, I, I, I, I, P, P, P, P, P, P]),
 })
 
 

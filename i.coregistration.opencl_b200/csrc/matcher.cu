@@ -2,7 +2,8 @@
 //
 // The matcher interface (matcher.h) and the RoMa matcher
 // (matcher_roma.h): the device stage through roma_match, the host stage
-// with the reference's sampling rules (matcher_roma.c:41-232).
+// (roma_sample_matches, roma_dense_field) with the reference's sampling
+// rules (matcher_roma.c:41-232).
 
 #include <math.h>
 #include <stdio.h>
@@ -35,6 +36,131 @@ extern "C" void matcher_dump_file(const char *dir, int tile, const char *what,
         fail("Unable to write debug dump <%s>", path);
     if (fp)
         fclose(fp);
+}
+
+// ---------------------------------------------- RoMa's host stage
+//
+// The warp (2, H, W) is normalized to [-1, 1] over the padded tile with
+// align_corners false, so a warp value f lands at ((f + 1) n - 1) / 2
+// cells along an axis of n cells.
+
+namespace {
+
+inline double landing(float f, int n) { return (f + 1.0) * 0.5 * n - 0.5; }
+
+// Whether (x, y), rounded half away from zero, is a cell of the h x w tile
+// that valid (NULL: all) marks.
+bool lands_valid(const unsigned char *valid, int h, int w, double x, double y)
+{
+    const long ix = lround(x), iy = lround(y);
+    if (ix < 0 || iy < 0 || ix >= w || iy >= h)
+        return false;
+    return !valid || valid[(size_t)iy * w + ix];
+}
+
+// Distance in cells from (x, y) to where the reverse warp bflow sends
+// (xr, yr): (xr, yr) clamped into the h x w tile, the reverse landing
+// interpolated bilinearly over the 2 x 2 cells at or left / above it (the
+// last pair when it lies on the last row or column) (matcher_roma.c:61-90).
+float cycle_distance(const float *bflow, int H, int W, int h, int w, int x, int y,
+                     double xr, double yr)
+{
+    if (w == 1 || h == 1)
+        return NAN;
+    xr = xr < 0 ? 0 : xr > w - 1 ? w - 1 : xr;
+    yr = yr < 0 ? 0 : yr > h - 1 ? h - 1 : yr;
+    const int cx = (int)xr < w - 2 ? (int)xr : w - 2;
+    const int cy = (int)yr < h - 2 ? (int)yr : h - 2;
+    const double fx = xr - cx, fy = yr - cy;
+    const size_t plane = (size_t)H * W;
+    double sx = 0, sy = 0;
+    for (int j = 0; j < 2; j++)
+        for (int i = 0; i < 2; i++) {
+            const size_t k = (size_t)(cy + j) * W + cx + i;
+            const double wgt = (i ? fx : 1 - fx) * (j ? fy : 1 - fy);
+            sx += wgt * landing(bflow[k], W);
+            sy += wgt * landing(bflow[plane + k], H);
+        }
+    return (float)hypot(sx - x, sy - y);
+}
+
+}  // namespace
+
+extern "C" int roma_sample_matches(const float *flow, const float *cert, const float *sd,
+                                   const float *bflow, int H, int W, int h, int w,
+                                   int spacing, float min_cert,
+                                   const unsigned char *valid1,
+                                   const unsigned char *valid2, struct match_list *out)
+{
+    if (pending())
+        return 0;
+    if (spacing < 1 || h > H || w > W) {
+        fail("roma_sample_matches: spacing %d, tile %d x %d of %d x %d", spacing, h, w, H, W);
+        return 0;
+    }
+    const size_t plane = (size_t)H * W;
+    int n = 0;
+    for (int by = 0; by < h; by += spacing)
+        for (int bx = 0; bx < w; bx += spacing) {
+            // The block's first valid cell of highest certainty.
+            const int ye = by + spacing < h ? by + spacing : h;
+            const int xe = bx + spacing < w ? bx + spacing : w;
+            long best = -1;
+            for (int y = by; y < ye; y++)
+                for (int x = bx; x < xe; x++)
+                    if (!valid1 || valid1[(size_t)y * w + x]) {
+                        const long i = (long)y * W + x;
+                        if (best < 0 || cert[i] > cert[best])
+                            best = i;
+                    }
+            if (best < 0 || !(cert[best] >= min_cert))
+                continue;
+            const int x = (int)(best % W), y = (int)(best / W);
+            struct match mt;
+            mt.x1 = x;
+            mt.y1 = y;
+            mt.x2 = landing(flow[best], W);
+            mt.y2 = landing(flow[plane + best], H);
+            if (!lands_valid(valid2, h, w, mt.x2, mt.y2))
+                continue;
+            mt.cost = 1.0f - cert[best];
+            mt.sd = sd ? sd[best] : NAN;
+            mt.cycle = bflow ? cycle_distance(bflow, H, W, h, w, x, y, mt.x2, mt.y2) : NAN;
+            match_add(out, &mt);
+            n++;
+        }
+    return n;
+}
+
+extern "C" void roma_dense_field(const float *flow, const float *cert, const float *sd,
+                                 int H, int W, int h, int w, const unsigned char *valid1,
+                                 const unsigned char *valid2, float *dx, float *dy,
+                                 float *certo, float *sdo)
+{
+    if (pending())
+        return;
+    if (h > H || w > W) {
+        fail("roma_dense_field: tile %d x %d of %d x %d", h, w, H, W);
+        return;
+    }
+    const size_t plane = (size_t)H * W;
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) {
+            const size_t i = (size_t)y * W + x, o = (size_t)y * w + x;
+            const double xr = landing(flow[i], W), yr = landing(flow[plane + i], H);
+            if ((valid1 && !valid1[o]) || !lands_valid(valid2, h, w, xr, yr)) {
+                dx[o] = dy[o] = NAN;
+                certo[o] = 0.0f;
+                if (sdo)
+                    sdo[o] = NAN;
+                continue;
+            }
+            dx[o] = (float)(xr - x);
+            dy[o] = (float)(yr - y);
+            certo[o] = cert[i];
+            if (sdo)
+                sdo[o] = sd ? sd[i] : NAN;
+        }
 }
 
 namespace {
@@ -72,111 +198,26 @@ void roma_m_run(struct matcher *m, const struct matcher_tile *t)
     roma_match(&s->net, t->img1, t->img2, m->dump_dir, t->index);
 }
 
-// Cycle error (matcher_roma.c:61-90): distance from (x, y) to the reverse
-// warp at (xr, yr), bilinear between the tile's cells.
-float cycle_error(const roma_state *s, const struct matcher_tile *t, int x,
-                  int y, double xr, double yr)
-{
-    const size_t hw = (size_t)t->H * t->W;
-    double bx = 0, by = 0;
-    xr = xr < 0 ? 0 : xr > t->w - 1 ? t->w - 1 : xr;
-    yr = yr < 0 ? 0 : yr > t->h - 1 ? t->h - 1 : yr;
-    int x0 = (int)xr < t->w - 1 ? (int)xr : t->w - 1;
-    int y0 = (int)yr < t->h - 1 ? (int)yr : t->h - 1;
-    if (t->w == 1 || t->h == 1)
-        return NAN;
-    if (x0 == t->w - 1)
-        x0--;
-    if (y0 == t->h - 1)
-        y0--;
-    const double fx = xr - x0, fy = yr - y0;
-    for (int j = 0; j < 2; j++)
-        for (int i = 0; i < 2; i++) {
-            const size_t k = (size_t)(y0 + j) * t->W + x0 + i;
-            const double wgt = (i ? fx : 1 - fx) * (j ? fy : 1 - fy);
-            bx += wgt * ((s->bflow[k] + 1.0) * 0.5 * t->W - 0.5);
-            by += wgt * ((s->bflow[hw + k] + 1.0) * 0.5 * t->H - 0.5);
-        }
-    return (float)hypot(bx - x, by - y);
-}
-
-int valid_at(const unsigned char *v, int h, int w, double x, double y)
-{
-    const long ix = lround(x), iy = lround(y);
-    return ix >= 0 && iy >= 0 && ix < w && iy < h &&
-           (!v || v[(size_t)iy * w + ix]);
-}
-
-// matcher_roma.c:103-145.
 int roma_m_match(struct matcher *m, const struct matcher_tile *t,
                  struct match_list *out)
 {
     roma_state *s = (roma_state *)m->state;
-    const float *cert = s->net.cert, *flow = s->net.flow, *sd = s->net.sd;
-    const size_t hw = (size_t)t->H * t->W;
-    const int S = s->spacing;
-    int n = 0;
     if (pending())
         return 0;
-    for (int by = 0; by < t->h; by += S)
-        for (int bx = 0; bx < t->w; bx += S) {
-            const int bxe = bx + S < t->w ? bx + S : t->w;
-            const int bye = by + S < t->h ? by + S : t->h;
-            long best = -1;
-            for (int y = by; y < bye; y++)
-                for (int x = bx; x < bxe; x++) {
-                    const size_t i = (size_t)y * t->W + x;
-                    if (t->valid1 && !t->valid1[(size_t)y * t->w + x])
-                        continue;
-                    if (best < 0 || cert[i] > cert[best])
-                        best = (long)i;
-                }
-            if (best < 0 || !(cert[best] >= s->min_cert))
-                continue;
-            struct match mt;
-            mt.x1 = best % t->W;
-            mt.y1 = best / t->W;
-            mt.x2 = (flow[best] + 1.0) * 0.5 * t->W - 0.5;
-            mt.y2 = (flow[hw + best] + 1.0) * 0.5 * t->H - 0.5;
-            mt.cost = 1.0f - cert[best];
-            mt.sd = sd ? sd[best] : NAN;
-            if (!valid_at(t->valid2, t->h, t->w, mt.x2, mt.y2))
-                continue;
-            mt.cycle = m->cycle ? cycle_error(s, t, (int)mt.x1, (int)mt.y1, mt.x2,
-                                              mt.y2)
-                                : NAN;
-            match_add(out, &mt);
-            n++;
-        }
-    return n;
+    return roma_sample_matches(s->net.flow, s->net.cert, s->net.sd,
+                               m->cycle ? s->bflow : nullptr, t->H, t->W, t->h,
+                               t->w, s->spacing, s->min_cert, t->valid1,
+                               t->valid2, out);
 }
 
-// matcher_roma.c:150-178.
 void roma_m_field(struct matcher *m, const struct matcher_tile *t, float *dx,
                   float *dy, float *cert, float *sdo)
 {
     roma_state *s = (roma_state *)m->state;
-    const float *c = s->net.cert, *flow = s->net.flow;
-    const size_t hw = (size_t)t->H * t->W;
-    for (int y = 0; y < t->h; y++)
-        for (int x = 0; x < t->w; x++) {
-            const size_t i = (size_t)y * t->W + x, o = (size_t)y * t->w + x;
-            const double xr = (flow[i] + 1.0) * 0.5 * t->W - 0.5;
-            const double yr = (flow[hw + i] + 1.0) * 0.5 * t->H - 0.5;
-            if ((t->valid1 && !t->valid1[o]) ||
-                !valid_at(t->valid2, t->h, t->w, xr, yr)) {
-                dx[o] = dy[o] = NAN;
-                cert[o] = 0.0f;
-                if (sdo)
-                    sdo[o] = NAN;
-                continue;
-            }
-            dx[o] = (float)(xr - x);
-            dy[o] = (float)(yr - y);
-            cert[o] = c[i];
-            if (sdo)
-                sdo[o] = s->net.sd ? s->net.sd[i] : NAN;
-        }
+    if (pending())
+        return;
+    roma_dense_field(s->net.flow, s->net.cert, s->net.sd, t->H, t->W, t->h,
+                     t->w, t->valid1, t->valid2, dx, dy, cert, sdo);
 }
 
 void roma_m_dump(struct matcher *m, const struct matcher_tile *t,
