@@ -81,9 +81,10 @@ def rank_tile_seeds(rank, ntiles):
 
 def make_tiles(seeds):
     """Synthetic 1024 x 1024 tile pairs of the configuration's scene
-    generator, resampled to the 864 x 864 processing size (float32 in
-    0..1, (3, H, W))."""
-    from scipy.ndimage import zoom
+    generator, resampled to the 864 x 864 processing size with Pillow's
+    antialiased bicubic on float bands (the resampler the reference's
+    prepare restates): float32 in 0..1, (3, H, W)."""
+    from PIL import Image
 
     from coreg import synth
 
@@ -93,7 +94,8 @@ def make_tiles(seeds):
         pair = []
         for img in (a, b):
             f = img.astype(np.float32) / 255.0
-            f = zoom(f, (1, H / TILE_SRC, W / TILE_SRC), order=1, grid_mode=True, mode="nearest")
+            f = np.stack([np.asarray(Image.fromarray(band, mode="F").resize((W, H), Image.BICUBIC))
+                          for band in f])
             pair.append(np.ascontiguousarray(np.clip(f, 0, 1), np.float32))
         out.append(pair)
     return out
