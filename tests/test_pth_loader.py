@@ -128,6 +128,19 @@ def test_torch_save_formats_match_torch_load(lib, tmp_path, how):
     assert_same(got, want)
 
 
+def test_archive_folder_name_from_a_stream(lib, tmp_path):
+    """torch.save to a stream names the archive's folder "archive/"; the
+    reader finds data.pkl and the storages under any folder name."""
+    buf = io.BytesIO()
+    sd = state_dict()
+    torch.save(sd, buf)
+    p = tmp_path / "stream.pth"
+    p.write_bytes(buf.getvalue())
+    with zipfile.ZipFile(p) as z:
+        assert any(n.startswith("archive/") for n in z.namelist())
+    assert_same(read_all(lib, p), expected(torch.load(p, weights_only=False)))
+
+
 def test_views_keep_their_strides(lib, tmp_path):
     sd = state_dict()
     p = tmp_path / "w.pth"
