@@ -112,6 +112,7 @@ EXTRA_SIGNATURES.update({
     "match_add": (None, [C.POINTER(MatchList), C.POINTER(Match)]),
     "roma_sample_matches": (I, [P, P, P, P, I, I, I, I, I, F, P, P, C.POINTER(MatchList)]),
     "roma_dense_field": (None, [P, P, P, I, I, I, I, P, P, P, P, P, P]),
+    "eloftr_sample_matches": (I, [P, P, I, I, I, P, P, C.POINTER(MatchList)]),
 })
 
 

@@ -57,33 +57,13 @@ void el_run(struct matcher *m, const struct matcher_tile *t)
     eloftr_match(&s->net, s->grey0.data(), s->grey1.data(), m->dump_dir, t->index);
 }
 
-bool valid_at(const unsigned char *v, int h, int w, double x, double y)
-{
-    const long ix = lround(x), iy = lround(y);
-    return ix >= 0 && iy >= 0 && ix < w && iy < h && (!v || v[(size_t)iy * w + ix]);
-}
-
 int el_match(struct matcher *m, const struct matcher_tile *t, struct match_list *out)
 {
     eloftr_state *s = (eloftr_state *)m->state;
-    int n = 0;
-    for (int i = 0; i < s->net.nm; i++) {
-        const float *k = s->net.kp + 4 * (size_t)i;
-        struct match mt;
-        mt.x1 = k[0] + KP_OFFSET;
-        mt.y1 = k[1] + KP_OFFSET;
-        mt.x2 = k[2] + KP_OFFSET;
-        mt.y2 = k[3] + KP_OFFSET;
-        mt.cost = 1.0f - s->net.mconf[i];
-        mt.sd = NAN;
-        mt.cycle = NAN;
-        if (!valid_at(t->valid1, t->h, t->w, mt.x1, mt.y1) ||
-            !valid_at(t->valid2, t->h, t->w, mt.x2, mt.y2))
-            continue;
-        match_add(out, &mt);
-        n++;
-    }
-    return n;
+    if (coreg::pending())
+        return 0;
+    return eloftr_sample_matches(s->net.kp, s->net.mconf, s->net.nm, t->h, t->w, t->valid1,
+                                 t->valid2, out);
 }
 
 void el_dump(struct matcher *m, const struct matcher_tile *t, const char *dir)
@@ -120,6 +100,38 @@ void el_destroy(struct matcher *m)
 }
 
 }  // namespace
+
+// The matches of the keypoint pairs kp (x0, y0, x1, y1 in the network's
+// convention, KP_OFFSET from the cells') whose both ends round to valid
+// cells (matcher_eloftr.c:66-96).
+extern "C" int eloftr_sample_matches(const float *kp, const float *mconf, int nm, int h, int w,
+                                     const unsigned char *valid1,
+                                     const unsigned char *valid2, struct match_list *out)
+{
+    if (coreg::pending())
+        return 0;
+    const auto on_valid = [h, w](const unsigned char *v, double x, double y) {
+        const long ix = lround(x), iy = lround(y);
+        return ix >= 0 && iy >= 0 && ix < w && iy < h && (!v || v[(size_t)iy * w + ix]);
+    };
+    int n = 0;
+    for (int i = 0; i < nm; i++) {
+        const float *k = kp + 4 * (size_t)i;
+        struct match mt;
+        mt.x1 = k[0] + KP_OFFSET;
+        mt.y1 = k[1] + KP_OFFSET;
+        mt.x2 = k[2] + KP_OFFSET;
+        mt.y2 = k[3] + KP_OFFSET;
+        if (!on_valid(valid1, mt.x1, mt.y1) || !on_valid(valid2, mt.x2, mt.y2))
+            continue;
+        mt.cost = 1.0f - mconf[i];
+        mt.sd = NAN;
+        mt.cycle = NAN;
+        match_add(out, &mt);
+        n++;
+    }
+    return n;
+}
 
 extern "C" void matcher_eloftr_create(struct matcher *m, struct ops *ops, struct pth_file *pf,
                                       const char *name, int npe)

@@ -1,8 +1,10 @@
 # SPDX-License-Identifier: Unlicense
-"""The RoMa matcher's host stage (roma_sample_matches, roma_dense_field of
-include/matcher_roma.h; matcher_roma.c:61-178) against the restated glue
-of oracle/matcher_ref.py on seeded warps, certainties and masks (CPU; the
-library's host code only). The rules are exact: the same matches in the
+"""The matchers' host stages against the restated glue of
+oracle/matcher_ref.py (CPU; the library's host code only): RoMa's
+(roma_sample_matches, roma_dense_field of include/matcher_roma.h;
+matcher_roma.c:61-178) on seeded warps, certainties and masks, and
+ELoFTR's (eloftr_sample_matches of include/matcher_eloftr.h;
+matcher_eloftr.c:66-96) on seeded keypoint pairs. The rules are exact: the same matches in the
 same order, the same positions, costs, sd and cycle distances (float to
 double conversions aside), and the same dense field bit for bit.
 
@@ -113,3 +115,30 @@ def test_bad_spacing_is_an_error(lib):
     assert n == 0
     with pytest.raises(coreg.CoregError):
         coreg.check(lib)
+
+
+@pytest.mark.parametrize("seed,h,w,masks", [(0, 120, 120, True), (1, 64, 80, False),
+                                            (2, 50, 61, True)])
+def test_eloftr_sampling_matches_oracle(lib, seed, h, w, masks):
+    rng = np.random.default_rng(seed)
+    nm = 300
+    # Keypoints around and past the tile, half-cell positions included.
+    kp = (rng.uniform(-6, max(h, w) + 2, (nm, 4)) - 3.5).astype(np.float32)
+    kp[:20] = np.round(kp[:20]) + np.float32(0.5) - np.float32(3.5)
+    mconf = rng.uniform(0, 1, nm).astype(np.float32)
+    v1 = v2 = None
+    if masks:
+        v1 = (rng.random((h, w)) > 0.2).astype(np.uint8)
+        v2 = (rng.random((h, w)) > 0.2).astype(np.uint8)
+    ml = MatchList()
+    n = lib.eloftr_sample_matches(ptr(kp), ptr(mconf), nm, h, w, ptr(v1), ptr(v2), C.byref(ml))
+    coreg.check(lib)
+    got = [(m.x1, m.y1, m.x2, m.y2, m.cost, m.sd, m.cycle) for m in ml.v[:ml.n]]
+    if ml.v:
+        LIBC.free(C.cast(ml.v, C.c_void_p))
+    want = matcher_ref.eloftr_matches(kp, mconf, h, w, v1, v2)
+    assert n == len(got) == len(want) > 0
+    for g, r in zip(got, want):
+        assert g[:4] == tuple(float(v) for v in r[:4])
+        assert np.float32(g[4]) == np.float32(r[4])
+        assert np.isnan(g[5]) and np.isnan(g[6])
