@@ -2,7 +2,9 @@
 """CPU restatement of the reference's matcher glue (TEST INFRASTRUCTURE):
 the RoMa sampling of the dense warp into matches (matcher_roma.c:103-145),
 its dense field (:150-178) and cycle error (:61-90), and the Efficient
-LoFTR keypoint offsets and validity filter (matcher_eloftr.c:66-96)."""
+LoFTR keypoint offsets and validity filter (matcher_eloftr.c:66-96).
+Pinned to the reference's own glue, compiled into oracle/_ref/libglue_ref.so
+by oracle/Makefile (tests/test_matcher_host_stage.py)."""
 
 import math
 

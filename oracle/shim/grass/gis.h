@@ -1,8 +1,9 @@
 /* SPDX-License-Identifier: Unlicense */
 
-/* The few GRASS GIS library calls that the reference's tests/ops_check.c
- * and adalam.c make, for building them without GRASS (test
- * infrastructure: oracle/Makefile). Memory calls exit on failure and
+/* The few GRASS GIS library calls that the reference's tests/ops_check.c,
+ * adalam.c and matcher glue (matcher.c, matcher_roma.c, matcher_eloftr.c)
+ * make, for building them without GRASS (test infrastructure:
+ * oracle/Makefile). Memory calls exit on failure and
  * G_fatal_error exits 1, as in GRASS. */
 
 #ifndef COREG_SHIM_GRASS_GIS_H
@@ -40,6 +41,12 @@ static inline void G_fatal_error(const char *fmt, ...)
     fprintf(stderr, "\n");
     va_end(ap);
     exit(1);
+}
+
+static inline void G_debug(int level, const char *fmt, ...)
+{
+    (void)level;
+    (void)fmt;
 }
 
 static inline void G_message(const char *fmt, ...)
