@@ -18,12 +18,14 @@ available. The two encoders are pinned to the libraries RoMa builds them
 from, on the same seeded weights (tests/test_roma_oracle_pins.py): the
 DINOv2 encoder with its position interpolation to transformers' Dinov2Model
 and DINOv2's original interpolation call, the VGG19-BN pyramid to
-torchvision's vgg19_bn. The decoder's transformer blocks are pinned to
+torchvision's vgg19_bn. The Gaussian-process solve (gp_solve), prepare and
+interp_pos are pinned to the reference's own host functions, compiled from
+its roma.c by oracle/Makefile. The decoder's transformer blocks are pinned to
 transformers' Dinov2Layer configured as RoMa's decoder block, the input
 resampling bit-exact to Pillow's own resize of float bands, and the
 refiners' local correlation to its sampling form through torch's
-grid_sample. The Gaussian-process embedding, cls_to_flow and the rest of
-the refiners are checked
+grid_sample. The Gaussian-process kernel matrices, cls_to_flow and the
+rest of the refiners are checked
 through the generic ops they share with oracle/ops_ref.py (pinned to the
 reference's ops_compare.py) and by reading the cited lines.
 """
@@ -224,6 +226,15 @@ class Model:
 
 # ------------------------------------------------------------- the tile
 
+def gp_solve(K, F):
+    """gp_solve (roma.c:772-836): (K + 0.1 I)^-1 F in float64 through the
+    Cholesky factor, K (n, n) and F (n, d) as given (float32 in the
+    reference), the result in float64."""
+    n = K.shape[0]
+    A = K.double() + GP_NOISE * torch.eye(n, dtype=torch.float64)
+    return torch.cholesky_solve(F.double(), torch.linalg.cholesky(A))
+
+
 def pil_cubic(x):
     a = -0.5
     x = abs(x)
@@ -348,9 +359,7 @@ class Runner:
 
         kyy = cosk(yb, nb, yb, nb)
         kxy = cosk(ya, na, yb, nb)
-        K = kyy.double() + GP_NOISE * torch.eye(self.n16, dtype=torch.float64)
-        L = torch.linalg.cholesky(K)
-        X = torch.cholesky_solve(torch.from_numpy(self.basis).double(), L).to(self.dt)
+        X = gp_solve(kyy, torch.from_numpy(self.basis)).to(self.dt)
         mu = kxy @ X
         self.dumps["gp"] = mu
         return torch.cat([mu, ya], 1)

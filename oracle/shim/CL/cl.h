@@ -1,10 +1,11 @@
 /* SPDX-License-Identifier: Unlicense */
 
 /* The OpenCL 1.2 scalar and handle types that the reference's headers name
- * (ocl_backend.h, ops.h, roma.h, eloftr.h), as opaque types, so that its
- * host-only sources (matcher.c, matcher_roma.c, matcher_eloftr.c) compile
- * as checkers without OpenCL (test infrastructure: oracle/Makefile). No
- * OpenCL function is declared or called. */
+ * (ocl_backend.h, ops.h, roma.h, eloftr.h), as opaque types, and the
+ * prototypes (from the OpenCL 1.2 specification) of the few OpenCL calls
+ * that roma.c makes, so that its sources compile as checkers of their
+ * host-only functions without OpenCL (test infrastructure:
+ * oracle/Makefile). No OpenCL function is defined or called. */
 
 #ifndef COREG_SHIM_CL_H
 #define COREG_SHIM_CL_H
@@ -15,6 +16,7 @@ typedef int32_t cl_int;
 typedef uint32_t cl_uint;
 typedef int64_t cl_long;
 typedef uint64_t cl_ulong;
+typedef float cl_float;
 typedef struct shim_cl_platform *cl_platform_id;
 typedef struct shim_cl_device *cl_device_id;
 typedef struct shim_cl_context *cl_context;
@@ -22,5 +24,23 @@ typedef struct shim_cl_queue *cl_command_queue;
 typedef struct shim_cl_program *cl_program;
 typedef struct shim_cl_kernel *cl_kernel;
 typedef struct shim_cl_mem *cl_mem;
+typedef struct shim_cl_event *cl_event;
+
+#include <stddef.h>
+
+cl_int clSetKernelArg(cl_kernel kernel, cl_uint index, size_t size, const void *value);
+cl_int clReleaseKernel(cl_kernel kernel);
+cl_int clEnqueueCopyBuffer(cl_command_queue queue, cl_mem src, cl_mem dst, size_t src_offset,
+                           size_t dst_offset, size_t size, cl_uint n_wait,
+                           const cl_event *wait, cl_event *event);
+cl_int clEnqueueCopyBufferRect(cl_command_queue queue, cl_mem src, cl_mem dst,
+                               const size_t *src_origin, const size_t *dst_origin,
+                               const size_t *region, size_t src_row_pitch,
+                               size_t src_slice_pitch, size_t dst_row_pitch,
+                               size_t dst_slice_pitch, cl_uint n_wait, const cl_event *wait,
+                               cl_event *event);
+cl_int clEnqueueFillBuffer(cl_command_queue queue, cl_mem buffer, const void *pattern,
+                           size_t pattern_size, size_t offset, size_t size, cl_uint n_wait,
+                           const cl_event *wait, cl_event *event);
 
 #endif /* COREG_SHIM_CL_H */
