@@ -1,9 +1,9 @@
 /* SPDX-License-Identifier: Unlicense */
 
 /* The few GRASS GIS library calls that the reference's tests/ops_check.c,
- * adalam.c and matcher glue (matcher.c, matcher_roma.c, matcher_eloftr.c)
- * make, for building them without GRASS (test infrastructure:
- * oracle/Makefile). Memory calls exit on failure and
+ * adalam.c, pth_loader.c, roma.c and matcher glue (matcher.c,
+ * matcher_roma.c, matcher_eloftr.c) make, for building them without GRASS
+ * (test infrastructure: oracle/Makefile). Memory calls exit on failure and
  * G_fatal_error exits 1, as in GRASS. */
 
 #ifndef COREG_SHIM_GRASS_GIS_H
@@ -12,6 +12,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #define GPATH_MAX 4096
 
@@ -42,6 +43,17 @@ static inline void G_fatal_error(const char *fmt, ...)
     va_end(ap);
     exit(1);
 }
+
+static inline char *G_store(const char *s)
+{
+    size_t n = strlen(s) + 1;
+    char *p = (char *)G__shim_check(malloc(n));
+
+    memcpy(p, s, n);
+    return p;
+}
+
+static inline void G_verbose_message(const char *fmt, ...) { (void)fmt; }
 
 static inline void G_debug(int level, const char *fmt, ...)
 {

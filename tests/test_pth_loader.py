@@ -9,7 +9,12 @@ sliced, sharing a storage), parameters and tensors with Python
 attributes, and for the wrappers around a state_dict the reference
 accepts ("model", "state_dict", a single dict of tensors). Integer
 tensors are left out. Malformed files give the reference's errors.
-CPU only: no device call."""
+
+The well-formed files are also read by the reference's own pth_loader.c,
+compiled into oracle/_ref/libpth_ref.so by oracle/Makefile (that test
+skips when it has not been built): the same index (names, shapes, strides,
+storage offsets, dtypes, file offsets, storage sizes), the same pth_bytes
+and bit-identical pth_read_f32 arrays. CPU only: no device call."""
 
 import ctypes as C
 import io
@@ -17,6 +22,7 @@ import json
 import struct
 import zipfile
 from collections import OrderedDict
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -323,3 +329,71 @@ def test_missing_tensor_and_wrong_shape(lib, tmp_path):
         assert t and lib.pth_numel(t) == 6
     finally:
         lib.pth_close(C.byref(pf))
+
+
+PTH_REF = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libpth_ref.so"
+
+
+@pytest.fixture(scope="module")
+def ref_reader():
+    if not PTH_REF.exists():
+        pytest.skip("oracle/_ref/libpth_ref.so not built (make -C oracle)")
+    r = C.CDLL(str(PTH_REF))
+    r.pth_open.restype = None
+    r.pth_open.argtypes = [C.POINTER(R.PthFile), C.c_char_p]
+    r.pth_read_f32.restype = C.POINTER(C.c_float)
+    r.pth_read_f32.argtypes = [C.POINTER(R.PthFile), C.POINTER(R.PthTensor)]
+    r.pth_bytes.restype = C.c_double
+    r.pth_bytes.argtypes = [C.POINTER(R.PthFile), C.c_char_p]
+    r.pth_close.restype = None
+    r.pth_close.argtypes = [C.POINTER(R.PthFile)]
+    return r
+
+
+def index_and_data(lib, path, prefix=b""):
+    """(index rows, arrays, pth_bytes(prefix)) of a reader: this build's
+    library or the reference's."""
+    pf = R.PthFile()
+    lib.pth_open(C.byref(pf), str(path).encode())
+    rows, arrays = [], []
+    for i in range(pf.ntensors):
+        t = pf.tensors[i]
+        rows.append((t.name.decode(), t.ndim, tuple(t.shape[:t.ndim]), tuple(t.stride[:t.ndim]),
+                     t.storage_offset, t.dtype, t.data_offset, t.storage_bytes))
+        p = lib.pth_read_f32(C.byref(pf), C.byref(t))
+        n = int(np.prod(t.shape[:t.ndim]))
+        arrays.append(np.ctypeslib.as_array(p, (max(n, 1),))[:n].copy())
+        LIBC.free(C.cast(p, C.c_void_p))
+    nbytes = lib.pth_bytes(C.byref(pf), prefix)
+    lib.pth_close(C.byref(pf))
+    return rows, arrays, nbytes
+
+
+def well_formed_files(tmp_path):
+    sd = state_dict()
+    files = {}
+    for name, kw in (("zip", {}), ("p4", {"pickle_protocol": 4}),
+                     ("legacy", {"_use_new_zipfile_serialization": False})):
+        files[name] = tmp_path / f"{name}.pth"
+        torch.save(sd, files[name], **kw)
+    files["zip64"] = tmp_path / "z64.pth"
+    zip64_copy(files["zip"], files["zip64"])
+    files["wrapped"] = tmp_path / "wrapped.pth"
+    torch.save({"epoch": 1, "model": sd}, files["wrapped"])
+    buf = io.BytesIO()
+    torch.save(sd, buf)
+    files["stream"] = tmp_path / "stream.pth"
+    files["stream"].write_bytes(buf.getvalue())
+    files["safetensors"] = tmp_path / "w.safetensors"
+    write_safetensors_mixed(files["safetensors"])
+    return files
+
+
+def test_index_and_values_match_reference_reader(lib, ref_reader, tmp_path):
+    for name, path in well_formed_files(tmp_path).items():
+        mine = index_and_data(lib, path, b"view.")
+        ref = index_and_data(ref_reader, path, b"view.")
+        assert mine[0] == ref[0], name
+        assert mine[2] == ref[2], name
+        for a, b in zip(mine[1], ref[1]):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), name
