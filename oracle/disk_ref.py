@@ -10,7 +10,9 @@ convolutions). Pinned only through the generic ops it shares with
 oracle/ops_ref.py (conv2d with normalized and gated input, instance-norm
 statistics, average pooling, bilinear resize; pinned to the reference's
 ops_compare.py); the upstream kornia DISK is not available here, so the
-network as a whole is parity unpinned beyond the restated semantics.
+network as a whole is parity unpinned beyond the restated semantics. The
+keypoint selection (select) is pinned to the reference's own disk_detect
+host code, compiled by oracle/Makefile (tests/test_disk_select_ref.py).
 """
 
 import numpy as np
