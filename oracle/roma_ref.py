@@ -24,8 +24,11 @@ its roma.c by oracle/Makefile. The decoder's transformer blocks are pinned to
 transformers' Dinov2Layer configured as RoMa's decoder block, the input
 resampling bit-exact to Pillow's own resize of float bands, and the
 refiners' local correlation to its sampling form through torch's
-grid_sample. The Gaussian-process kernel matrices, cls_to_flow and the
-rest of the refiners are checked
+grid_sample. Its kernel-level steps (the Gaussian-process kernel
+matrices, cls_to_flow, warp sampling, local correlation, displacement,
+updates, depthwise convolution) are pinned to the reference's own
+roma_kernels.cl, compiled as C and run on the CPU through oracle/cl_emul.h.
+The rest is checked
 through the generic ops they share with oracle/ops_ref.py (pinned to the
 reference's ops_compare.py) and by reading the cited lines.
 """
@@ -226,6 +229,35 @@ class Model:
 
 # ------------------------------------------------------------- the tile
 
+def cos_exp(S, nx, ny):
+    """roma_cos_exp (roma_kernels.cl:27-38) on the dot products S (N, M)
+    with the row norms nx (N) and ny (M)."""
+    return torch.exp((S / (nx[:, None] * ny[None, :] + COS_EPS) - 1.0) / GP_T)
+
+
+def disp(flow, gx, gy, fx, fy):
+    """roma_disp (roma_kernels.cl:196-208): (fx, fy) (warp - cell centre)."""
+    return torch.stack([fx * (flow[0] - gx), fy * (flow[1] - gy)])
+
+
+def update(flow, cert, d, scale, Wf, Hf):
+    """roma_update (roma_kernels.cl:213-224)."""
+    flow = flow + torch.stack([scale * (d[0] / (4.0 * Wf)), scale * (d[1] / (4.0 * Hf))])
+    return flow, cert + d[2]
+
+
+def update2(flow, conf, d, W, H):
+    """roma2_update (roma_kernels.cl:230-250): warp += d / (4 W, 4 H),
+    confidence += overlap logit and the precision terms of the softplus
+    Cholesky factor (threshold 20, + 1e-6)."""
+    flow = flow + torch.stack([d[0] / (4.0 * W), d[1] / (4.0 * H)])
+    sp = lambda x: torch.where(x > 20, x, torch.log1p(torch.exp(x)))
+    l00 = sp(d[3]) + 1e-6
+    l10 = d[4]
+    l11 = sp(d[5]) + 1e-6
+    return flow, conf + torch.stack([d[2], l00 * l00, l00 * l10, l10 * l10 + l11 * l11])
+
+
 def gp_solve(K, F):
     """gp_solve (roma.c:772-836): (K + 0.1 I)^-1 F in float64 through the
     Cholesky factor, K (n, n) and F (n, d) as given (float32 in the
@@ -353,9 +385,7 @@ class Runner:
         na, nb = ya.norm(dim=1), yb.norm(dim=1)
 
         def cosk(a, an, b, bn):
-            s = a @ b.T
-            c = s / (an[:, None] * bn[None, :] + COS_EPS)
-            return torch.exp((c - 1.0) / GP_T)
+            return cos_exp(a @ b.T, an, bn)
 
         kyy = cosk(yb, nb, yb, nb)
         kxy = cosk(ya, na, yb, nb)
@@ -401,10 +431,13 @@ class Runner:
         return gx, gy
 
     def sample(self, f, H, W, flow):
-        """roma_warp_sample (roma_kernels.cl:130-141): (C, n)."""
-        g = flow.T.reshape(1, 1, H * W, 2)
-        return F.grid_sample(f.reshape(1, -1, H, W), g, mode="bilinear", padding_mode="zeros",
-                             align_corners=False)[0, :, 0]
+        """roma_warp_sample (roma_kernels.cl:130-141): (C, n); zero where
+        the warp is not finite (bilinear0, roma_kernels.cl:106-128)."""
+        ok = torch.isfinite(flow).all(0)
+        g = torch.where(ok[None], flow, 0).T.reshape(1, 1, H * W, 2)
+        out = F.grid_sample(f.reshape(1, -1, H, W), g, mode="bilinear", padding_mode="zeros",
+                            align_corners=False)[0, :, 0]
+        return torch.where(ok[None], out, 0)
 
     def local_corr(self, f1, f2, H, W, r, flow):
         """roma_local_corr (roma_kernels.cl:153-192): whole-cell dot
@@ -445,8 +478,7 @@ class Runner:
         9 blocks of depthwise 5 x 5 (+ ReLU) and 1 x 1."""
         n = H * W
         gx, gy = self.grid(H, W, self.dt)
-        disp = torch.stack([dfx * (flow[0] - gx), dfy * (flow[1] - gy)])
-        emb = self.t(r["emb_w"]) @ disp + self.t(r["emb_b"])[:, None]
+        emb = self.t(r["emb_w"]) @ disp(flow, gx, gy, dfx, dfy) + self.t(r["emb_b"])[:, None]
         parts = [fa, self.sample(fb, H, W, flow), emb]
         if r["radius"]:
             parts.append(self.local_corr(fa, fb, H, W, r["radius"], flow))
@@ -462,20 +494,13 @@ class Runner:
         r = self.m.ref[s]
         fac = 40.0 / 32.0 * sf
         d = self.refine_body(r, P[s][0], P[s][1], H, W, fac, fac, flow)
-        flow = flow + torch.stack([r["scale"] * (d[0] / (4.0 * Wf)), r["scale"] * (d[1] / (4.0 * Hf))])
-        return flow, cert + d[2]
+        return update(flow, cert, d, r["scale"], Wf, Hf)
 
     def refine2(self, j, P2, H, W, Hp, Wp, flow, conf):
         """refine2 + roma2_update (roma.c:1033-1104, roma_kernels.cl:230-250)."""
         r = self.m.ref2[j]
         d = self.refine_body(r, P2[j][0], P2[j][1], H, W, Wp / 512.0, Hp / 512.0, flow)
-        flow = flow + torch.stack([d[0] / (4.0 * W), d[1] / (4.0 * H)])
-        sp = lambda x: torch.where(x > 20, x, torch.log1p(torch.exp(x)))
-        l00 = sp(d[3]) + 1e-6
-        l10 = d[4]
-        l11 = sp(d[5]) + 1e-6
-        conf = conf + torch.stack([d[2], l00 * l00, l00 * l10, l10 * l10 + l11 * l11])
-        return flow, conf
+        return update2(flow, conf, d, W, H)
 
     @staticmethod
     def resize(x, C, h, w, H, W):
