@@ -7,7 +7,8 @@
  * a work-group of L work-items runs as L host threads with a barrier, and
  * the float built-ins the kernels use map to the C library's float
  * functions (OpenCL permits a few units in the last place for them; the
- * C library is one realization). */
+ * C library is one realization; mad is an unfused multiply-add, one of the
+ * two forms OpenCL allows). */
 
 #ifndef COREG_CL_EMUL_H
 #define COREG_CL_EMUL_H
@@ -37,6 +38,26 @@ void emul_barrier(void);
 static inline float emul_rsqrt(float x) { return 1.0f / sqrtf(x); }
 static inline int emul_clampi(int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; }
 
+typedef unsigned char uchar;
+typedef unsigned long ulong;
+typedef struct {
+    int x, y, z, w;
+} int4;
+typedef struct {
+    float x, y, z, w;
+} float4;
+
+/* OpenCL's vector literal (float4)(a, b, c, d) has no C form: the build
+ * recipe rewrites it to emul_float4(a, b, c, d) in its copy of the source
+ * (oracle/Makefile). */
+static inline float4 emul_float4(float x, float y, float z, float w)
+{
+    float4 v = {x, y, z, w};
+    return v;
+}
+
+#define mad(a, b, c) ((a) * (b) + (c))
+#define log(x) _Generic((x), float: logf, default: log)(x)
 #define rsqrt(x) emul_rsqrt(x)
 #define clamp(v, lo, hi) emul_clampi((v), (lo), (hi))
 #define exp(x) _Generic((x), float: expf, default: exp)(x)

@@ -12,7 +12,9 @@ statistics, average pooling, bilinear resize; pinned to the reference's
 ops_compare.py); the upstream kornia DISK is not available here, so the
 network as a whole is parity unpinned beyond the restated semantics. The
 keypoint selection (select) is pinned to the reference's own disk_detect
-host code, compiled by oracle/Makefile (tests/test_disk_select_ref.py).
+host code, compiled by oracle/Makefile (tests/test_disk_select_ref.py), and
+nms_mask and gather to its disk_kernels.cl, compiled as C and run on the
+CPU (tests/test_eloftr_disk_kernels_ref.py).
 """
 
 import numpy as np

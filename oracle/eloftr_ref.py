@@ -15,7 +15,9 @@ aggregated attention with RoPE, coarse matches), the fine features (the
 model's refinement layer), and the two fine stages, which follow the
 authors' FineMatching as eloftr_kernels.cl does (the fixture restates it in
 torch on the model's own fine windows, since transformers' version
-departs from it).
+departs from it). The dual softmax and the fine matching are also pinned
+to the reference's own eloftr_kernels.cl, compiled as C and run on the CPU
+(tests/test_eloftr_disk_kernels_ref.py).
 """
 
 import math
@@ -169,6 +171,20 @@ class Model:
         return mi, mj, mconf, kp, dumps
 
 
+def dual_softmax_maxima(S):
+    """The dual-softmax confidence softmax_row(S) * softmax_col(S) of the
+    scores S (n0, n1) (eloftr_kernels.cl:12-144): each row's maximum and
+    first argmax, each column's maximum and first argmax."""
+    sr = S - S.max(1, keepdims=True)
+    pr = np.exp(sr) / np.exp(sr).sum(1, keepdims=True)
+    sc = S - S.max(0, keepdims=True)
+    pc = np.exp(sc) / np.exp(sc).sum(0, keepdims=True)
+    conf = pr * pc
+    rarg = conf.argmax(1)
+    carg = conf.argmax(0)
+    return (conf[np.arange(len(S)), rarg], rarg, conf[carg, np.arange(S.shape[1])], carg)
+
+
 def coarse_match(x0, x1):
     """Dual softmax of S = f0 f1^T / (256 0.1), mutual first argmaxes above
     0.2, away from the 2-cell border (eloftr.c:473-571); also the margins
@@ -176,14 +192,7 @@ def coarse_match(x0, x1):
     h, w = x0.shape[1:]
     n = h * w
     S = x0.reshape(D, n).T @ x1.reshape(D, n) / (D * COARSE_T)
-    sr = S - S.max(1, keepdims=True)
-    pr = np.exp(sr) / np.exp(sr).sum(1, keepdims=True)
-    sc = S - S.max(0, keepdims=True)
-    pc = np.exp(sc) / np.exp(sc).sum(0, keepdims=True)
-    conf = pr * pc
-    rarg = conf.argmax(1)
-    rmax = conf[np.arange(n), rarg]
-    carg = conf.argmax(0)
+    rmax, rarg, _, carg = dual_softmax_maxima(S)
     mi, mj, mc = [], [], []
     for i in range(n):
         j = rarg[i]
