@@ -15,8 +15,13 @@
 __thread struct emul_item emul_wi;
 
 static pthread_barrier_t group_barrier;
+static int group_of_one;
 
-void emul_barrier(void) { pthread_barrier_wait(&group_barrier); }
+void emul_barrier(void)
+{
+    if (!group_of_one)
+        pthread_barrier_wait(&group_barrier);
+}
 
 struct emul_launch {
     void (*body)(void *);
@@ -36,6 +41,8 @@ static void emul_set(const struct emul_launch *L, const size_t grp[3], const siz
         emul_wi.grp[d] = grp[d];
         emul_wi.lid[d] = lid[d];
         emul_wi.gid[d] = grp[d] * L->l[d] + lid[d];
+        emul_wi.lsz[d] = L->l[d];
+        emul_wi.gsz[d] = L->g[d];
     }
 }
 
@@ -68,6 +75,7 @@ void emul_launch(void (*body)(void *), void *args, const size_t g[3], const size
         L.ng[d] = g[d] / l[d];
         items *= l[d];
     }
+    group_of_one = items == 1;
     if (items == 1) {
         size_t grp[3], lid[3] = {0, 0, 0};
 

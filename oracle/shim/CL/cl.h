@@ -2,10 +2,11 @@
 
 /* The OpenCL 1.2 scalar and handle types that the reference's headers name
  * (ocl_backend.h, ops.h, roma.h, eloftr.h), as opaque types, and the
- * prototypes (from the OpenCL 1.2 specification) of the few OpenCL calls
- * that roma.c makes, so that its sources compile as checkers of their
- * host-only functions without OpenCL (test infrastructure:
- * oracle/Makefile). No OpenCL function is defined or called. */
+ * prototypes (from the OpenCL 1.2 specification) of the OpenCL calls
+ * that its host sources make, so that they compile without OpenCL (test
+ * infrastructure: oracle/Makefile). oracle/cl_backend_emul.c defines
+ * these calls over host memory, for the builds that run the reference's
+ * kernels on the CPU. */
 
 #ifndef COREG_SHIM_CL_H
 #define COREG_SHIM_CL_H
@@ -28,7 +29,20 @@ typedef struct shim_cl_event *cl_event;
 
 #include <stddef.h>
 
+typedef cl_uint cl_profiling_info;
+#define CL_SUCCESS 0
+#define CL_PROFILING_COMMAND_START 0x1282
+#define CL_PROFILING_COMMAND_END 0x1283
+
 cl_int clSetKernelArg(cl_kernel kernel, cl_uint index, size_t size, const void *value);
+cl_int clEnqueueNDRangeKernel(cl_command_queue queue, cl_kernel kernel, cl_uint dims,
+                              const size_t *offset, const size_t *global, const size_t *local,
+                              cl_uint n_wait, const cl_event *wait, cl_event *event);
+cl_int clWaitForEvents(cl_uint n, const cl_event *events);
+cl_int clGetEventProfilingInfo(cl_event event, cl_profiling_info name, size_t size,
+                               void *value, size_t *size_ret);
+cl_int clReleaseEvent(cl_event event);
+cl_int clFinish(cl_command_queue queue);
 cl_int clReleaseKernel(cl_kernel kernel);
 cl_int clEnqueueCopyBuffer(cl_command_queue queue, cl_mem src, cl_mem dst, size_t src_offset,
                            size_t dst_offset, size_t size, cl_uint n_wait,
