@@ -14,7 +14,9 @@ network as a whole is parity unpinned beyond the restated semantics. The
 keypoint selection (select) is pinned to the reference's own disk_detect
 host code, compiled by oracle/Makefile (tests/test_disk_select_ref.py), and
 nms_mask and gather to its disk_kernels.cl, compiled as C and run on the
-CPU (tests/test_eloftr_disk_kernels_ref.py).
+CPU (tests/test_eloftr_disk_kernels_ref.py). The whole detect is pinned to
+the reference's own DISK stage (disk.c, ops.c and the kernels, unchanged)
+run on the CPU over the OpenCL emulation (tests/test_disk_ref_cpu.py).
 """
 
 import numpy as np
