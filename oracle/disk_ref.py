@@ -6,17 +6,15 @@ path, never the product).
 Follows i.coregistration.opencl's disk.c (U-Net :23-31 and :163-214,
 candidate selection :236-266), disk_kernels.cl (nms5x5 :10-35, gather_desc
 :39-60) and adalam.c (nearest :38-98), in float64 (torch for the
-convolutions). Pinned only through the generic ops it shares with
-oracle/ops_ref.py (conv2d with normalized and gated input, instance-norm
-statistics, average pooling, bilinear resize; pinned to the reference's
-ops_compare.py); the upstream kornia DISK is not available here, so the
-network as a whole is parity unpinned beyond the restated semantics. The
-keypoint selection (select) is pinned to the reference's own disk_detect
+convolutions). The upstream kornia DISK is not available here; the
+reference's own DISK stage is the checker instead. The whole detect
+(network, NMS, selection, descriptors) is pinned to the reference's disk.c,
+ops.c and kernels, unchanged, run on the CPU over the OpenCL emulation of
+oracle/cl_backend_emul.c (tests/test_disk_ref_cpu.py). Its pieces are
+pinned as well: the keypoint selection (select) is pinned to the reference's own disk_detect
 host code, compiled by oracle/Makefile (tests/test_disk_select_ref.py), and
 nms_mask and gather to its disk_kernels.cl, compiled as C and run on the
-CPU (tests/test_eloftr_disk_kernels_ref.py). The whole detect is pinned to
-the reference's own DISK stage (disk.c, ops.c and the kernels, unchanged)
-run on the CPU over the OpenCL emulation (tests/test_disk_ref_cpu.py).
+CPU (tests/test_eloftr_disk_kernels_ref.py).
 """
 
 import numpy as np

@@ -7,7 +7,7 @@ against the DISK oracle (oracle/disk_ref.py), on the seeded synthetic
 weights and a band-limited 48 x 48 image (44 x 44 valid). This pins the
 oracle's U-Net, NMS, selection and descriptors to the reference itself:
 network output relative L2 <= 1e-5, the same keypoints in the same
-order, scores and descriptors within 1e-5. CPU only (about 15 s: the
+order, scores and descriptors within 1e-5. CPU only (about 25 s: the
 emulation runs every work-item as C on the host)."""
 
 import ctypes as C
