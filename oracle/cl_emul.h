@@ -4,7 +4,8 @@
  * CPU, so that the reference's own .cl sources serve as checkers here,
  * where no OpenCL platform exists (oracle/Makefile). The address-space
  * qualifiers vanish, local arrays become statics shared by one work-group,
- * a work-group of L work-items runs as L host threads with a barrier, and
+ * a work-group of L work-items runs as L coroutines that take turns at
+ * each barrier, and
  * the float built-ins the kernels use map to the C library's float
  * functions (OpenCL permits a few units in the last place for them; the
  * C library is one realization; mad is an unfused multiply-add, one of the

@@ -17,7 +17,10 @@ authors' FineMatching as eloftr_kernels.cl does (the fixture restates it in
 torch on the model's own fine windows, since transformers' version
 departs from it). The dual softmax and the fine matching are also pinned
 to the reference's own eloftr_kernels.cl, compiled as C and run on the CPU
-(tests/test_eloftr_disk_kernels_ref.py).
+(tests/test_eloftr_disk_kernels_ref.py), and the whole stage to the
+reference's own eloftr.c, ops.c and kernels run on the CPU: its debug dumps
+of the backbone, transformer and fusion features, and its matches
+(tests/test_eloftr_ref_cpu.py).
 """
 
 import math
