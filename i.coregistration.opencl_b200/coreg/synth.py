@@ -167,6 +167,20 @@ def roma_weights(seed=0):
         main[f"{pre}.out_conv.bias"] = g.normal((3,), 0.05)
         main[f"{pre}.disp_emb.weight"] = g.normal((e, 2, 1, 1), 0.7)
         main[f"{pre}.disp_emb.bias"] = g.normal((e,), 0.05)
+    _roma_v2(g, v2)
+    return main, dino, v2
+
+
+def roma_v2_weights(seed=0):
+    """RoMa v2's refiners alone (their own seeded stream, not the one
+    roma_weights draws them from)."""
+    v2 = {}
+    _roma_v2(Gen(seed), v2)
+    return v2
+
+
+def _roma_v2(g, v2):
+    """RoMa v2's refiner features and refiners (roma.c:460-545)."""
     _vgg(g, v2, "refiner_features.layers", 3)
     for j in range(3):
         f, e, r, fin = REF2_FEAT[j], REF2_EMB[j], REF2_RADIUS[j], REF2_IN[j]
@@ -181,7 +195,6 @@ def roma_weights(seed=0):
         v2[f"{pre}.warp_head.bias"] = g.normal((2,), 0.05)
         v2[f"{pre}.confidence_head.weight"] = g.normal((4, cin, 1, 1), math.sqrt(1.0 / cin))
         v2[f"{pre}.confidence_head.bias"] = g.normal((4,), 0.05)
-    return main, dino, v2
 
 
 def write_roma_weights(folder, seed=0):

@@ -11,10 +11,13 @@ function cites the lines it restates. The coarse-pass side is a parameter
 (roma.c fixes it at ROMA_COARSE = 560) so that the parity tests can run
 small.
 
-Parity pinned for the encoders, unpinned after them: the reference's own
-RoMa path needs an OpenCL platform to run and its model-level compare
-scripts need the upstream romatch / RoMaV2 packages, none of which is
-available. The two encoders are pinned to the libraries RoMa builds them
+Parity pinned for the encoders and for RoMa v2's refiners, unpinned for
+the wiring of the coarse pass: the reference's whole roma_match is too
+slow to run on the CPU at its fixed 560 coarse side, and its model-level
+compare scripts need the upstream romatch / RoMaV2 packages, which are
+absent. RoMa v2's second pass (vgg2 and refiners2, roma.c:1000-1306) is
+pinned to the reference's own code run on the CPU over an OpenCL
+emulation (tests/test_roma_v2_ref_cpu.py). The two encoders are pinned to the libraries RoMa builds them
 from, on the same seeded weights (tests/test_roma_oracle_pins.py): the
 DINOv2 encoder with its position interpolation to transformers' Dinov2Model
 and DINOv2's original interpolation call, the VGG19-BN pyramid to
@@ -502,6 +505,23 @@ class Runner:
         d = self.refine_body(r, P2[j][0], P2[j][1], H, W, Wp / 512.0, Hp / 512.0, flow)
         return update2(flow, conf, d, W, H)
 
+    def refiners2(self, p, Hp, Wp, h, w, flow, conf, zero_prec, Pp):
+        """refiners2 (roma.c:1272-1306): RoMa v2's refiners of pass p (size
+        Hp x Wp) from the warp and confidence on an h x w grid; with
+        zero_prec the precision is cleared first."""
+        for j in range(3):
+            hs, ws = Hp // REF2_SCALE[j], Wp // REF2_SCALE[j]
+            if zero_prec and j == 0:
+                conf = conf.clone()
+                conf[1:] = 0
+            flow = self.resize(flow, 2, h, w, hs, ws)
+            conf = self.resize(conf, 4, h, w, hs, ws)
+            flow, conf = self.refine2(j, Pp, hs, ws, Hp, Wp, flow, conf)
+            self.dumps[f"p{p}_v2s{REF2_SCALE[j]}_flow"] = flow
+            self.dumps[f"p{p}_v2s{REF2_SCALE[j]}_conf"] = conf
+            h, w = hs, ws
+        return flow, conf, h, w
+
     @staticmethod
     def resize(x, C, h, w, H, W):
         """ops_resize with size semantics (ops.cl:723-754)."""
@@ -562,27 +582,13 @@ class Runner:
             conf = torch.zeros(4, h * w, dtype=self.dt)
             conf[0] = cert
 
-            def refiners2(p, Hp, Wp, h, w, flow, conf, zero_prec, Pp):
-                for j in range(3):
-                    hs, ws = Hp // REF2_SCALE[j], Wp // REF2_SCALE[j]
-                    if zero_prec and j == 0:
-                        conf = conf.clone()
-                        conf[1:] = 0
-                    flow = self.resize(flow, 2, h, w, hs, ws)
-                    conf = self.resize(conf, 4, h, w, hs, ws)
-                    flow, conf = self.refine2(j, Pp, hs, ws, Hp, Wp, flow, conf)
-                    self.dumps[f"p{p}_v2s{REF2_SCALE[j]}_flow"] = flow
-                    self.dumps[f"p{p}_v2s{REF2_SCALE[j]}_conf"] = conf
-                    h, w = hs, ws
-                return flow, conf, h, w
-
-            flow, conf, h, w = refiners2(0, Cs, Cs, h, w, flow, conf, False, P2)
+            flow, conf, h, w = self.refiners2(0, Cs, Cs, h, w, flow, conf, False, P2)
             proj2 = [(r["proj_w"], r["proj_b"]) for r in m.ref2]
             for k in range(2):
                 img = self.t(prepare(ins[k], H, W, m.imagenet))
                 self.dumps[f"in_f_{k}"] = img
                 self.vgg(img, k, P2, [keep(P2, 2 - blk, proj2) for blk in range(3)], m.vgg2)
-            flow, conf, h, w = refiners2(1, H, W, h, w, flow, conf, True, P2)
+            flow, conf, h, w = self.refiners2(1, H, W, h, w, flow, conf, True, P2)
             flow = flow.double().numpy()
             c = conf[0].double().numpy()
             prec = conf[1:].float().double().numpy()
