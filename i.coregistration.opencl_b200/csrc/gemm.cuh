@@ -43,8 +43,10 @@ struct GemmArgs {
     // image (row m = pixel, column k = (ky, kx, c)); 2 implicit im2col of
     // a patchify convolution (cP x cP, stride cP) over a channels-last
     // (cH, cW, cC) image (row m = patch, column k = (c, ky, kx)).
+    // amode 1: cK is the kernel size, 3 (also when 0: padding 1) or 5
+    // (padding 2, column k = (ky, kx, c) likewise).
     int amode;
-    int cH, cW, cC, cP;
+    int cH, cW, cC, cP, cK;
 };
 
 inline GemmArgs gemm_args(int M, int N, int K)
@@ -58,6 +60,22 @@ inline GemmArgs gemm_args(int M, int N, int K)
     g.alpha = 1.0f;
     return g;
 }
+
+// The rule by which ops_gemm (and ops_gemm_noalloc, which must give the
+// same results) rounds float32 operands to bfloat16 for the tensor-core
+// tiles: an OPS_BF16 context, a K-major B (transb) and a K the tiles take.
+inline bool gemm_packs_bf16(int precision, int M, int N, int K, int transb)
+{
+    return precision == OPS_BF16 && transb && M >= 64 && N >= 1 && K >= 16 &&
+           K % 8 == 0;
+}
+
+// Float32 rows x cols of each of nb batch products (batch b at
+// (b / nb1) s0 + (b % nb1) s1, rows ld apart) into packed bfloat16 rows of
+// `cols`, batch after batch; rows are walked by a grid-stride loop, so any
+// row count launches.
+void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
+                    int nb1, int rows, int cols, __nv_bfloat16 *dst);
 
 // Float32 FMA tiles (the accurate path): any strides, any type mix.
 void gemm_simt(cudaStream_t st, const GemmArgs &g);

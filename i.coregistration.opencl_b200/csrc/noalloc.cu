@@ -73,20 +73,6 @@ void *scratch_of(int dev)
     return p;
 }
 
-// Float32 rows x cols of every batch product (batch offsets as ops_gemm)
-// into packed bfloat16 rows of `cols`.
-__global__ void noalloc_pack_k(const float *src, long ld, long s0, long s1, int nb1,
-                               int rows, int cols, __nv_bfloat16 *dst)
-{
-    const long b = blockIdx.z, b0 = b / nb1, b1 = b % nb1;
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    const int r = blockIdx.y;
-
-    if (c < cols)
-        dst[(b * rows + r) * (long)cols + c] =
-            __float2bfloat16_rn(src[b0 * s0 + b1 * s1 + (long)r * ld + c]);
-}
-
 }  // namespace
 
 extern "C" size_t ops_gemm_noalloc_max_bytes(void)
@@ -135,8 +121,7 @@ extern "C" void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd
     g.c = DT_F32;
     cudaStream_t st = stream_of(o->ocl);
 
-    if (!(o->precision == OPS_BF16 && transb && M >= 64 && N >= 64 && K >= 16 &&
-          K % 8 == 0)) {
+    if (!gemm_packs_bf16(o->precision, M, N, K, transb)) {
         // The float32 tiles stage nothing.
         gemm_simt(st, g);
         launch_ok("ops_gemm_noalloc");
@@ -156,10 +141,8 @@ extern "C" void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd
         return;
     __nv_bfloat16 *a16 = (__nv_bfloat16 *)base;
     __nv_bfloat16 *b16 = (__nv_bfloat16 *)(base + a_bytes);
-    noalloc_pack_k<<<dim3(cdiv(K, 256), M, nb), 256, 0, st>>>(
-        (const float *)g.A, g.lda, g.sa0, g.sa1, nb1, M, K, a16);
-    noalloc_pack_k<<<dim3(cdiv(K, 256), N, nb), 256, 0, st>>>(
-        (const float *)g.B, g.ldb, g.sb0, g.sb1, nb1, N, K, b16);
+    pack_bf16_rows(st, (const float *)g.A, g.lda, g.sa0, g.sa1, nb, nb1, M, K, a16);
+    pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
     if (!launch_ok("ops_gemm_noalloc pack"))
         return;
     GemmArgs h = g;

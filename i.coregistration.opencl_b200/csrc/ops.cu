@@ -55,21 +55,38 @@ static const int T256 = 256;
 
 // ------------------------------------------------------------------- GEMM
 
-// Float32 copy of an operand into bfloat16 (OPS_BF16 on ops_gemm): rows
-// x cols of src (leading dimension ld) per batch product, packed.
+// Float32 copy of an operand into bfloat16 (OPS_BF16 on ops_gemm and
+// ops_gemm_noalloc): rows x cols of src (leading dimension ld) per batch
+// product, packed; blockIdx.y walks the nb x rows rows with a stride of
+// gridDim.y (at most 65535).
 __global__ void to_bf16_kernel(const float *src, long ld, long s0, long s1,
-                               int nb1, int rows, int cols,
+                               int nb1, long nrows, int rows, int cols,
                                __nv_bfloat16 *dst)
 {
-    const long b = blockIdx.z, b0 = b / nb1, b1 = b % nb1;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    const int r = blockIdx.y;
-
     if (c >= cols)
         return;
-    dst[(b * rows + r) * (long)cols + c] =
-        __float2bfloat16_rn(src[b0 * s0 + b1 * s1 + (long)r * ld + c]);
+    for (long br = blockIdx.y; br < nrows; br += gridDim.y) {
+        const long b = br / rows, r = br % rows, b0 = b / nb1, b1 = b % nb1;
+        dst[br * (long)cols + c] =
+            __float2bfloat16_rn(src[b0 * s0 + b1 * s1 + r * ld + c]);
+    }
 }
+
+namespace coreg {
+
+void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
+                    int nb1, int rows, int cols, __nv_bfloat16 *dst)
+{
+    const long nrows = (long)nb * rows;
+    if (nrows <= 0 || cols <= 0)
+        return;
+    const unsigned gy = (unsigned)(nrows < 65535 ? nrows : 65535);
+    to_bf16_kernel<<<dim3(cdiv(cols, 256), gy), 256, 0, st>>>(src, ld, s0, s1, nb1, nrows,
+                                                               rows, cols, dst);
+}
+
+}  // namespace coreg
 
 extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
                          struct opnd B, int transb, struct opnd C, int nb,
@@ -108,8 +125,7 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
     g.slope = slope;
     g.ab = DT_F32;
     g.c = DT_F32;
-    if (o->precision == OPS_BF16 && transb && M >= 64 && N >= 1 && K >= 16 &&
-        K % 8 == 0) {
+    if (gemm_packs_bf16(o->precision, M, N, K, transb)) {
         // Pack both operands to bfloat16 (row-major, K contiguous), then
         // the tensor-core tiles.
         size_t ea = (size_t)nb * M * K, eb = (size_t)nb * N * K;
@@ -127,10 +143,8 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
         cudaStream_t st = stream_of(o->ocl);
         {
             Prof p(o->ocl, "gemm_pack_bf16");
-            to_bf16_kernel<<<dim3(cdiv(K, 256), M, nb), 256, 0, st>>>(
-                (const float *)g.A, g.lda, g.sa0, g.sa1, nb1, M, K, a16);
-            to_bf16_kernel<<<dim3(cdiv(K, 256), N, nb), 256, 0, st>>>(
-                (const float *)g.B, g.ldb, g.sb0, g.sb1, nb1, N, K, b16);
+            pack_bf16_rows(st, (const float *)g.A, g.lda, g.sa0, g.sa1, nb, nb1, M, K, a16);
+            pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
             if (!launch_ok("gemm_pack_bf16"))
                 return;
         }
@@ -288,6 +302,158 @@ static void conv_im2col(struct ops *o, cl_mem in, int C, int H, int W, cl_mem w,
     }
 }
 
+// ------------------------------------- bfloat16 convolutions, tensor cores
+//
+// OPS_BF16 contexts run the stride-1 3 x 3 (padding 1) and 5 x 5 (padding
+// 2) convolutions of ops_conv2d, normalized input included, on the tcgen05
+// GEMM's implicit-convolution mode, keeping ops_conv2d's channel-major
+// float32 layout on both sides:
+//   1. the weights (K, C, k, k) float32 -> (K, k, k, Cp) bfloat16, C padded
+//      to Cp, a multiple of 64, with zeros;
+//   2. the input (C, H, W) float32 -> (H W, Cp) bfloat16, normalized and
+//      PReLU-gated on the way when mean is given (the same arithmetic as
+//      the float32 kernel: the gate before the zero padding, ops.cl:328-387);
+//   3. the GEMM over k k Cp columns (one 3-D TMA box per tap and 64-channel
+//      chunk, zeros outside the map) with bias and activation, into a
+//      channels-last float32 map of 16-byte rows;
+//   4. a transpose into out (K, H, W).
+// Steps 1, 2 and 4 move the operands once; the product is the tensor
+// cores'. All four buffers come from o->scratch16.
+
+namespace {
+
+int conv_cpad(int C) { return (C + 63) / 64 * 64; }
+int conv_opitch(int K) { return (K + 3) / 4 * 4; }
+
+// (K, C, kk) float32 -> (K, kk, Cp) bfloat16, zero for c >= C.
+__global__ void conv_w16_k(const float *w, int K, int C, int kk, int Cp, __nv_bfloat16 *out)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)K * kk * Cp)
+        return;
+    const int c = (int)(e % Cp), tap = (int)(e / Cp % kk), k = (int)(e / ((long)Cp * kk));
+    out[e] = __float2bfloat16_rn(c < C ? w[((long)k * C + c) * kk + tap] : 0.0f);
+}
+
+// Input (C, n) float32 into n x Cp bfloat16 rows, gated as described
+// above; channels C..Cp-1 zero. One block of 256 threads per `cells` cells
+// (64, 32 or 16, so that the Cp x (cells + 1) tile fits 48 KB of shared
+// memory): coalesced reads along the cells of a channel, coalesced writes
+// along the channels of a cell.
+__host__ __device__ inline int gate_cells(int Cp) { return Cp <= 128 ? 64 : Cp <= 256 ? 32 : 16; }
+__global__ void __launch_bounds__(256)
+conv_gate_cl_k(const float *in, int C, long n, const float *mean, const float *rstd,
+               const float *alpha, int Cp, __nv_bfloat16 *out)
+{
+    extern __shared__ float tile[];  // Cp x (cells + 1)
+    const int cells = gate_cells(Cp);
+    const long p0 = (long)blockIdx.x * cells;
+    const int tx = threadIdx.x % cells, ty = threadIdx.x / cells;
+    for (int c = ty; c < Cp; c += blockDim.x / cells) {
+        float v = 0.0f;
+        if (c < C && p0 + tx < n) {
+            v = in[(long)c * n + p0 + tx];
+            if (mean) {
+                v = (v - mean[c]) * rstd[c];
+                const float a = alpha ? alpha[c] : 1.0f;
+                v = v >= 0.0f ? v : a * v;
+            }
+        }
+        tile[c * (cells + 1) + tx] = v;
+    }
+    __syncthreads();
+    const int pairs = Cp / 2;
+    for (int e = threadIdx.x; e < cells * pairs; e += blockDim.x) {
+        const int px = e / pairs, c = 2 * (e % pairs);
+        if (p0 + px < n)
+            *(__nv_bfloat162 *)(out + (p0 + px) * Cp + c) = __floats2bfloat162_rn(
+                tile[c * (cells + 1) + px], tile[(c + 1) * (cells + 1) + px]);
+    }
+}
+
+// Channels-last (n x ld) float32 -> channel-major (K, n), 32 x 32 tiles.
+__global__ void conv_to_cm_k(const float *in, long n, int ld, int K, float *out)
+{
+    __shared__ float t[32][33];
+    const long p0 = (long)blockIdx.x * 32;
+    const int k0 = blockIdx.y * 32, x = threadIdx.x % 32, y = threadIdx.x / 32;
+    for (int r = y; r < 32; r += blockDim.x / 32)
+        if (p0 + r < n && k0 + x < K)
+            t[r][x] = in[(p0 + r) * ld + k0 + x];
+    __syncthreads();
+    for (int r = y; r < 32; r += blockDim.x / 32)
+        if (k0 + r < K && p0 + x < n)
+            out[(long)(k0 + r) * n + p0 + x] = t[x][r];
+}
+
+// Whether ops_conv2d takes the tensor-core path: a bfloat16 context, a
+// stride-1 3 x 3 / padding 1 or 5 x 5 / padding 2 convolution without
+// groups or dilation, at most 512 input channels (the gate tile's shared
+// memory) and at least 64 output positions (one tensor-core row block).
+bool conv_tc_geometry(const struct ops *o, int C, int H, int W, const struct conv_geom *g)
+{
+    return o->precision == OPS_BF16 && g->groups == 1 && g->dy == 1 && g->dx == 1 &&
+           g->sy == 1 && g->sx == 1 && g->kh == g->kw && (g->kh == 3 || g->kh == 5) &&
+           g->py == g->kh / 2 && g->px == g->kw / 2 && (long)H * W >= 64 &&
+           conv_cpad(C) <= 512;
+}
+
+// The tensor-core convolution; false (after recording an error, or with
+// nothing launched when the GEMM does not take the shape) otherwise.
+bool conv2d_tc(struct ops *o, cl_mem in, int C, int H, int W, cl_mem w, cl_mem b, int K,
+               int ks, cl_mem mean, cl_mem rstd, cl_mem alpha, int act, float slope,
+               cl_mem out)
+{
+    const long n = (long)H * W;
+    const int Cp = conv_cpad(C), kk = ks * ks, ld = conv_opitch(K);
+    const size_t wb = ((size_t)K * kk * Cp * 2 + 255) / 256 * 256;
+    const size_t ib = ((size_t)n * Cp * 2 + 255) / 256 * 256;
+    const size_t bytes = wb + ib + (size_t)n * ld * 4;
+    if (n >= (1L << 31) / ld)
+        return false;
+    GemmArgs gg = gemm_args((int)n, K, kk * Cp);
+    gg.amode = 1;
+    gg.cK = ks;
+    gg.cH = H;
+    gg.cW = W;
+    gg.cC = Cp;
+    gg.ldb = kk * Cp;
+    gg.transb = 1;
+    gg.ldc = ld;
+    gg.bias = fptr(b);
+    gg.act = act;
+    gg.slope = slope;
+    gg.ab = DT_BF16;
+    gg.c = DT_F32;
+    if (bytes > o->scratch16_bytes) {
+        ocl_release(&o->scratch16);
+        o->scratch16 = ocl_alloc(o->ocl, bytes, "convolution operands");
+        o->scratch16_bytes = bytes;
+        if (pending())
+            return false;
+    }
+    char *base = (char *)o->scratch16->ptr;
+    __nv_bfloat16 *w16 = (__nv_bfloat16 *)base, *a16 = (__nv_bfloat16 *)(base + wb);
+    float *cl = (float *)(base + wb + ib);
+    gg.A = a16;
+    gg.B = w16;
+    gg.C = cl;
+    cudaStream_t st = stream_of(o->ocl);
+    Prof p(o->ocl, ks == 5 ? "conv5x5_tc" : "conv3x3_tc");
+    const int cells = gate_cells(Cp);
+    conv_w16_k<<<cdiv((long)K * kk * Cp, 256), 256, 0, st>>>(fptr(w), K, C, kk, Cp, w16);
+    conv_gate_cl_k<<<cdiv(n, cells), 256, Cp * (cells + 1) * 4, st>>>(
+        fptr(in), C, n, fptr(mean), fptr(rstd), fptr(alpha), Cp, a16);
+    if (!launch_ok("convolution operands"))
+        return false;
+    if (!gemm_tc(st, gg, o->ocl->sm_count))
+        return false;
+    conv_to_cm_k<<<dim3(cdiv(n, 32), cdiv(K, 32)), 256, 0, st>>>(cl, n, ld, K, fptr(out));
+    return launch_ok(ks == 5 ? "conv5x5_tc" : "conv3x3_tc");
+}
+
+}  // namespace
+
 extern "C" void ops_conv2d(struct ops *o, cl_mem in, int C, int H, int W,
                            cl_mem w, cl_mem b, int K, const struct conv_geom *g,
                            cl_mem mean, cl_mem rstd, cl_mem alpha, int act,
@@ -311,6 +477,11 @@ extern "C" void ops_conv2d(struct ops *o, cl_mem in, int C, int H, int W,
         !count_ok((long)K * Ho * Wo, "convolution output"))
         return;
     if (Ho <= 0 || Wo <= 0)
+        return;
+    if (conv_tc_geometry(o, C, H, W, g) &&
+        conv2d_tc(o, in, C, H, W, w, b, K, g->kh, mean, rstd, alpha, act, slope, out))
+        return;
+    if (pending())
         return;
     if (g->groups == 1 && !mean && !alpha && g->dy == 1 && g->dx == 1 &&
         (long)C * g->kh * g->kw * Ho * Wo >= 4096) {

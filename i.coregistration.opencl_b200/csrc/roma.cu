@@ -1291,6 +1291,10 @@ void decoder(Ctx &c)
     }
     gemm_nt(c, "to_out", n, NCLS + 1, D, x, D, I->at, I->to_out_w, I->to_out_b,
             I->t_out, NCLS + 1, DT_F32, ACTF_NONE, false);
+    // The anchor logits and the certainty logit, token-major (n x 4097):
+    // an extra dump point, so that a check can tell the tokens whose
+    // first-index argmax is a near-tie from kernel error.
+    dump_dev(c, "cls_logits", I->t_out, DT_F32, (size_t)n * (NCLS + 1));
     Prof p(c.m->ocl, "roma_cls_to_flow");
     roma_cls_to_flow_l(c.st, I->t_out, NCLS + 1, NCLS, ROMA_CLS_RES, n, I->fl[0],
                        I->ce[0]);

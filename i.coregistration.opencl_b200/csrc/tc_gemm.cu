@@ -5,9 +5,9 @@
 // contiguous), float32 accumulation in tensor memory, float32 or
 // bfloat16 C: the GemmArgs contract of gemm.cuh (one product, column
 // bias). In convolution mode (GemmArgs::amode 1) A is the implicit im2col
-// of a 3 x 3 / stride 1 / padding 1 convolution over a channels-last map,
-// each k-block a 3-D TMA box of the map shifted by the tap, zeros read at
-// the borders: no im2col buffer.
+// of a 3 x 3 / padding 1 or 5 x 5 / padding 2 convolution (stride 1) over a
+// channels-last map, each k-block a 3-D TMA box of the map shifted by the
+// tap, zeros read at the borders: no im2col buffer.
 //
 // Persistent: one CTA per SM walks the 128 x BN output tiles t = blockIdx.x,
 // blockIdx.x + gridDim.x, ... (row blocks fastest, so that the CTAs running
@@ -60,10 +60,11 @@ struct TcParams {
     int act;
     float slope;
     int c_bf16;
-    // Convolution mode (3 x 3, stride 1, padding 1, channels-last input of
-    // cH x cW x cC, cC a multiple of 64): the tile is TW x TH output pixels
-    // (TW TH = 128), k-block kb = (tap, 64-channel chunk).
-    int conv, cH, cW, cC, TW, TH, tiles_x, tiles_y;
+    // Convolution mode (ksz x ksz, ksz 3 or 5, stride 1, padding ksz / 2,
+    // channels-last input of cH x cW x cC, cC a multiple of 64): the tile
+    // is TW x TH output pixels (TW TH = 128), k-block kb = (tap, 64-channel
+    // chunk), tap = ky ksz + kx.
+    int conv, cH, cW, cC, TW, TH, tiles_x, tiles_y, ksz;
     // Epilogue through TMA stores (output tensor map tma_c); else one
     // coalesced store per row.
     int tma_out;
@@ -83,10 +84,11 @@ struct Smem {
 constexpr int EPI_WARPS = NTHREADS / 32 - 2;
 static_assert(EPI_WARPS == 8, "one staging block per epilogue warp");
 
-// TMEM columns per accumulator: BN, at least the 32 that one tcgen05.ld of
-// the epilogue reads (the allocation granule).
+// TMEM columns per accumulator: BN rounded up to a power of two (the
+// allocation must be one), at least the 32 that one tcgen05.ld of the
+// epilogue reads (the allocation granule).
 template <int BN>
-constexpr int acc_cols() { return BN < 32 ? 32 : BN; }
+constexpr int acc_cols() { return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256; }
 
 // Tiles of at most 64 columns end after a few k-blocks, so that one
 // epilogue per tile cannot keep up: the two epilogue warp groups (warps
@@ -248,9 +250,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     mbar_expect_tx(&s.full[st], bytes);
                     if (p.conv) {
                         const int chunks = p.cC / BK, tap = kb / chunks;
-                        const int c0 = (kb % chunks) * BK;
-                        tma_load_3d(s.a[st], &tma_a, &s.full[st], c0, tl.cx0 + tap % 3 - 1,
-                                    tl.cy0 + tap / 3 - 1);
+                        const int c0 = (kb % chunks) * BK, pad = p.ksz / 2;
+                        tma_load_3d(s.a[st], &tma_a, &s.full[st], c0,
+                                    tl.cx0 + tap % p.ksz - pad, tl.cy0 + tap / p.ksz - pad);
                     }
                     else
                         tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, tl.m0);
@@ -437,6 +439,7 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     long tiles_m = cdiv(g.M, BM);
     if (g.amode == 1) {
         p.conv = 1;
+        p.ksz = g.cK ? g.cK : 3;
         p.cH = g.cH;
         p.cW = g.cW;
         p.cC = g.cC;
@@ -638,7 +641,9 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         sm_count = 148;
     if (g.ab != DT_BF16 || !g.transb || g.nb != 1)
         return false;
-    if (g.amode == 2 || (g.amode == 1 && (g.cC % tc::BK || g.K != 9 * g.cC)))
+    const int ksz = g.cK ? g.cK : 3;
+    if (g.amode == 2 ||
+        (g.amode == 1 && ((ksz != 3 && ksz != 5) || g.cC % tc::BK || g.K != ksz * ksz * g.cC)))
         return false;
     if (g.biasrow && g.bias)
         return false;
@@ -665,6 +670,10 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         return tc::launch_tc<32, 8>(st, g, sm_count);
     if (g.N <= 64)
         return tc::launch_tc<64, 8>(st, g, sm_count);
+    // 129 to 144 columns (DISK's last layer: 128 descriptor channels and
+    // the heatmap) in one 144-wide tile rather than two of 128.
+    if (g.N > 128 && g.N <= 144)
+        return tc::launch_tc<144, 5>(st, g, sm_count);
     return tc::launch_tc<128, 6>(st, g, sm_count);
 }
 

@@ -326,6 +326,7 @@ class Runner:
         self.pos = self.t(interp_pos(model.pos_raw, self.c16))
         self.basis = gp_basis(model.gp_w, model.gp_b, self.c16)
         self.dumps = {}
+        self.force_mode = None
 
     def t(self, a):
         return torch.as_tensor(np.asarray(a)).to(self.dt)
@@ -399,13 +400,21 @@ class Runner:
 
     def cls_to_flow(self, L):
         """roma_cls_to_flow (roma_kernels.cl:46-102): first-index argmax,
-        clamped neighbours (a clamped one counts twice)."""
+        clamped neighbours (a clamped one counts twice).
+
+        With `force_mode` set (one anchor index per token), those anchors
+        replace the argmax and the expectation is taken around them: a
+        check uses it to start the refiners of this restatement from the
+        anchors another run chose at its near-ties."""
         n = L.shape[0]
         logits = L[:, :NCLS]
         m, _ = logits.max(1)
         # First index of the maximum.
         idx = torch.arange(NCLS)[None, :].expand(n, NCLS)
         mode = torch.where(logits == m[:, None], idx, NCLS).min(1).values
+        if getattr(self, "force_mode", None) is not None:
+            mode = torch.as_tensor(np.asarray(self.force_mode), dtype=torch.long)
+            m = torch.gather(logits, 1, mode[:, None])[:, 0]
         s = torch.exp(logits - m[:, None]).sum(1)
         nb = torch.stack([mode - 1, mode, mode + 1, mode - CLS_RES, mode + CLS_RES], 1).clamp(0, NCLS - 1)
         pr = torch.exp(torch.gather(logits, 1, nb) - m[:, None]) / s[:, None]
@@ -420,6 +429,7 @@ class Runner:
         for b in self.m.dec:
             x = self.block(x, b, DEC_HEADS, EPS_LN_DEC)
         L = x @ self.t(self.m.to_out_w).T + self.t(self.m.to_out_b)
+        self.dumps["cls_logits"] = L
         return self.cls_to_flow(L)
 
     # -- refiners -----------------------------------------------------

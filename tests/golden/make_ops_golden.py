@@ -5,8 +5,8 @@ Writes the inputs of every case of oracle/ops_cases.py (the reference's
 tests/ops_check.c cases and generator) in the folder format that
 ops_check.c produces, then runs the reference's tests/ops_compare.py
 reference functions (torch float64) on them and stores their outputs as
-float32. Needs the reference checkout ($COREG_REFERENCE, else the build
-container's copy) and torch; run from the repository root:
+float32. Needs the reference checkout ($COREG_REFERENCE, else `reference` beside
+this repository's folder) and torch; run from the repository root:
 
     python tests/golden/make_ops_golden.py
 """
@@ -26,7 +26,7 @@ from oracle.ops_cases import build_cases, rope_table  # noqa: E402
 
 
 def main():
-    ref = Path(os.environ.get("COREG_REFERENCE", "/root/reference"))
+    ref = Path(os.environ.get("COREG_REFERENCE", ROOT.parent / "reference"))
     spec = importlib.util.spec_from_file_location("ops_compare", ref / "tests" / "ops_compare.py")
     oc = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(oc)

@@ -9,7 +9,8 @@ of 1e-5 per operation (checked per stage with the bound the stage's depth
 allows, below), dense warp within 0.05 px mean and 0.25 px p99, certainty
 within 1e-2 absolute. bfloat16 mode: per-stage relative L2 within 2e-2.
 Sizes: coarse pass 224 (16 x 16 DINOv2 tokens) and 128 x 128 tiles, so that
-the oracle finishes in seconds; the full 560 / 864 size is the last test.
+the oracle finishes in seconds; the benchmarked 560 / 864 size is checked
+in tests/test_roma_headline_gpu.py.
 """
 
 import numpy as np
