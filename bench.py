@@ -1,12 +1,23 @@
 # SPDX-License-Identifier: Unlicense
 """Benchmark of the dense-matching path: RoMa-v2ref tile pairs per second.
 
-One step = one roma_match of a tile pair at 864 x 864 with the coarse pass
-at 560 (the default matcher roma_v2ref), random
-init weights (seed 0) in the reference's layout, synthetic imagery of the
-configuration's generator. Tiles are independent, so N GPUs each process
-their own tiles (one process per GPU, no collective on the data path;
-"scaling": "weak"): value = all tiles / max-over-ranks device time.
+The unit of work is one roma_match of a tile pair at 864 x 864 with the
+coarse pass at 560 (the default matcher
+roma_v2ref), random init weights (seed 0) in the reference's layout,
+synthetic imagery of the configuration's generator. One step is one batch
+of --batch tile pairs (a slice of the configuration's 8192 x 8192 scene),
+spread over the GPU's concurrent tile pipelines. Tiles are independent, so
+N GPUs each process their own tiles (one process per GPU, no collective on
+the data path; "scaling": "weak"): value = all tiles / max-over-ranks
+device time.
+
+Beside the headline (bfloat16, the tensor-core path) the line carries:
+  fp32_mode    the same workload in float32 mode, the reference's
+               arithmetic (the validation mode);
+  secondary    Efficient LoFTR on 640 x 640 grey pairs and
+               DISK + descriptor matching on 1024 x 1024 RGB pairs with
+               2048 keypoints, through their public entry
+               points, with their path-level tensor fractions.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--precision bf16|fp32]
   python bench.py --impl reference ...   (the CPU baseline arm)
@@ -34,8 +45,14 @@ COARSE = 560
 TILE_SRC = 1024
 METRIC = "RoMa-v2ref tile pairs/s"
 UNIT = "tile_pairs/s"
-# Seconds of timed CPU work in the reference arm (whole tile pairs).
-REF_BUDGET_S = 120.0
+# Longest timed CPU work of the reference arm (whole tile pairs), seconds.
+REF_BUDGET_S = 420.0
+# Algorithmic FLOPs per pair of the secondary workloads (2 M N K per
+# product, per image where there are two): Efficient LoFTR at 640 x 640
+# (backbone 287, transformer 87, coarse matching 42, fusion 190 GFLOP) and
+# DISK on two 1024 x 1024 images plus the 2048 x 2048 x 128 distance GEMM.
+ELOFTR_FLOP = 605e9
+DISK_FLOP = 2 * 675e9 + 2 * 2048 * 2048 * 128
 CACHE = Path(os.environ.get("COREG_CACHE", "/tmp/coreg_cache"))
 
 
@@ -287,29 +304,43 @@ def cpu_sample(tiles, threads, reps=1, warmup=0, budget_s=None):
     return times
 
 
+def bench_config(args, world):
+    """The workload keys both arms print."""
+    return {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 (BASELINE configs[3])",
+            "tile_px": H, "coarse_px": COARSE, "tiles_per_rank": args.tiles,
+            "tiles_per_step": args.batch, "pipelines_per_gpu": max(1, args.streams),
+            "parallelism": f"tiles sharded over {world} GPU(s), {max(1, args.streams)} "
+                           "concurrent tile pipelines (streams) per GPU",
+            "l2": "no flush: every step streams the weights and activations "
+                  "(> 1 GB per tile pair) through the 126 MB L2"}
+
+
 def reference_arm(args, rank, world):
     """The reference's CPU implementation of the path: the oracle port on
     all host cores (the reference's OpenCL path has no OpenCL platform to
-    run on). One step is one full tile pair; at most one warm-up pair and
-    REF_BUDGET_S seconds of timed pairs, so that the run ends in minutes."""
+    run on). Its step is a bounded sample of the GPU arm's step, one full
+    tile pair; it runs the same warm-up and timed step counts, stopping
+    early (and saying so in "steps") only past REF_BUDGET_S seconds of
+    timed pairs."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     tiles = make_tiles(range(2))
-    warm = min(args.warmup, 1)
-    t = cpu_sample(tiles, threads, reps=max(1, args.steps), warmup=warm, budget_s=REF_BUDGET_S)
+    t = cpu_sample(tiles, threads, reps=max(1, args.steps), warmup=args.warmup,
+                   budget_s=REF_BUDGET_S)
     v = len(t) / sum(t)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": len(t), "warmup": warm, "ms_per_step": 1000 * sum(t) / len(t),
+        "steps": len(t), "warmup": args.warmup, "ms_per_step": 1000 * sum(t) / len(t),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded scene generator, random-init weights seed 0)",
-        "config": {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 "
-                               "(BASELINE configs[3])", "tile_px": H, "coarse_px": COARSE},
+        "data": "synthetic (seeded scene generator per 1024^2 tile, resampled to 864^2; "
+                "random-init weights seed 0)",
+        "config": bench_config(args, world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{len(t)} full tile pair(s) through the oracle "
-                                   "(torch float32 restatement of roma.c; the reference's "
-                                   "OpenCL path cannot run: no OpenCL platform on the box)"},
+                         "sample": f"{len(t)} full tile pair(s), one per step, through the "
+                                   "oracle (torch float32 restatement of roma.c on all host "
+                                   "cores; the reference's OpenCL path cannot run: no OpenCL "
+                                   "platform on the box)"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -317,65 +348,174 @@ def reference_arm(args, rank, world):
 
 # -------------------------------------------------------------- GPU arm
 
+class Pipelines:
+    """S tile pipelines on one GPU, each its own backend (stream), model and
+    tile graph: tiles are independent, and a second pipeline fills the SMs
+    that one tile's latency-bound stages (the Gaussian-process chain,
+    launch gaps, last waves) leave idle. Device-resident tiles are copied
+    into a pipeline's fixed graph inputs before each launch."""
+
+    def __init__(self, local, prec, S, tiles, weights):
+        import coreg
+        from coreg.roma import Roma
+
+        main, dino, v2 = weights
+        self.S = S
+        self.devs = [coreg.Device(local, precision=prec) for _ in range(S)]
+        self.dev = self.devs[0]
+        self.lib = self.dev.lib
+        self.nets = [Roma(d, main, dino, v2, H=H, W=W, coarse=COARSE) for d in self.devs]
+        self.hw3 = 3 * H * W
+        self.dtiles = [(self.dev.upload(a), self.dev.upload(b)) for a, b in tiles]
+        self.ins = [(d.alloc(self.hw3 * 4), d.alloc(self.hw3 * 4)) for d in self.devs]
+        self.kernels = [self.nets[s].graph_build(self.ins[s][0].ptr, self.ins[s][1].ptr)
+                        for s in range(S)]
+
+    def launch(self, i):
+        """Tile pair i on pipeline i % S; returns the kernels launched."""
+        s = i % self.S
+        a, b = self.dtiles[i % len(self.dtiles)]
+        for src, dst in ((a, self.ins[s][0]), (b, self.ins[s][1])):
+            self.lib.ocl_copy(self.devs[s].ocl_p, src.handle, 0, dst.handle, 0, self.hw3 * 4)
+        self.nets[s].graph_launch()
+        return self.kernels[s]
+
+    def sync(self):
+        for d, n_ in zip(self.devs, self.nets):
+            d.finish()
+            n_.sync()
+
+    def timed(self, count):
+        """Device milliseconds of `count` tile pairs, round robin over the
+        pipelines, between events on the first stream (the others joined
+        to it at both ends), and the kernels launched."""
+        import coreg
+
+        lib, dev = self.lib, self.dev
+        lib.ocl_timer_start(dev.ocl_p)
+        for s in range(1, self.S):
+            lib.ocl_join(self.devs[s].ocl_p, dev.ocl_p)
+        kernels = sum(self.launch(i) for i in range(count))
+        for s in range(1, self.S):
+            lib.ocl_join(dev.ocl_p, self.devs[s].ocl_p)
+        ms = lib.ocl_timer_stop(dev.ocl_p)
+        coreg.check(lib)
+        self.sync()
+        return ms, kernels
+
+    def close(self):
+        for n_, d in zip(self.nets, self.devs):
+            n_.close()
+            d.close()
+
+
+def fp32_mode(local, tiles, weights, count=8, S=2):
+    """Tile pairs/s of the same workload in float32 mode (float32 products,
+    the reference's arithmetic), device-resident tiles, after one warm-up
+    tile per pipeline."""
+    import coreg
+
+    p = Pipelines(local, coreg.OPS_FP32, S, tiles, weights)
+    try:
+        for i in range(S):
+            p.launch(i)
+        p.sync()
+        ms, _ = p.timed(count)
+    finally:
+        p.close()
+    return {"value": count / (ms / 1000.0), "unit": UNIT, "dtype": "f32", "tile_pairs": count,
+            "pipelines_per_gpu": S}
+
+
+def secondary(local, peak_tflops, pairs_eloftr=16, pairs_disk=4):
+    """Configs 2 and 5 through their public entry points (synchronous host
+    calls, host images in, host results out), wall clock per pair after one
+    warm-up pair, bfloat16 contexts."""
+    import coreg
+    from coreg import synth
+    from coreg.disk import Disk, nearest
+    from coreg.eloftr import Eloftr
+
+    out = {}
+    rng = np.random.default_rng(2)
+    side = 640
+    g0 = (synth.band_limited(rng, side, side, 3.0) / 255.0).astype(np.float32)
+    g1 = np.clip(np.roll(g0, (12, -9), (0, 1)) + 0.01 * rng.standard_normal(g0.shape), 0,
+                 1).astype(np.float32)
+    dev = coreg.Device(local, precision=coreg.OPS_BF16)
+    net = Eloftr(dev, synth.write_eloftr_weights(CACHE / "weights", 0), side, side)
+    try:
+        net.match(g0, g1)
+        t = time.perf_counter()
+        for _ in range(pairs_eloftr):
+            net.match(g0, g1)
+        sec = (time.perf_counter() - t) / pairs_eloftr
+    finally:
+        net.close()
+        dev.close()
+    out["eloftr"] = {"value": 1.0 / sec, "unit": "pairs/s",
+                     "workload": "Efficient LoFTR, 640x640 grey pair (BASELINE configs[1])",
+                     "tflops": ELOFTR_FLOP / sec / 1e12,
+                     "tensor_frac": ELOFTR_FLOP / sec / 1e12 / peak_tflops}
+    side, n = 1024, 2048
+    pairs = []
+    for k in range(2):
+        a, b, _ = synth.scene_pair(40 + k, side, side)
+        pairs.append((synth.tile_input(a, side, side), synth.tile_input(b, side, side)))
+    dev = coreg.Device(local, precision=coreg.OPS_BF16)
+    d = Disk(dev, synth.write_disk_weights(CACHE / "weights", 0), side, side, nmax=n)
+
+    def one(pair):
+        _, _, da = d.detect(pair[0], n=n)
+        _, _, db = d.detect(pair[1], n=n)
+        nearest(dev, da, db)
+
+    try:
+        one(pairs[0])
+        t = time.perf_counter()
+        for i in range(pairs_disk):
+            one(pairs[i % 2])
+        sec = (time.perf_counter() - t) / pairs_disk
+    finally:
+        d.close()
+        dev.close()
+    out["disk"] = {"value": 1.0 / sec, "unit": "pairs/s",
+                   "workload": "DISK + descriptor matching, 1024x1024 RGB pair, 2048 keypoints "
+                               "(BASELINE configs[4])",
+                   "tflops": DISK_FLOP / sec / 1e12,
+                   "tensor_frac": DISK_FLOP / sec / 1e12 / peak_tflops}
+    return out
+
+
 def gpu_arm(args, rank, world, local):
     import coreg
     from coreg import synth
-    from coreg.roma import Roma
 
     prec = coreg.OPS_BF16 if args.precision == "bf16" else coreg.OPS_FP32
     if rank == 0:
         synth.write_roma_weights(CACHE / "weights", 0)
     barrier(world)
-    main, dino, v2 = synth.write_roma_weights(CACHE / "weights", 0)
-    # S tile pipelines per GPU, each its own backend (stream), model and
-    # tile graph: tiles are independent, and a second pipeline fills the
-    # SMs that one tile's latency-bound stages (the Gaussian-process chain,
-    # launch gaps, last waves) leave idle.
+    weights = synth.write_roma_weights(CACHE / "weights", 0)
     S = max(1, args.streams)
-    devs = [coreg.Device(local, precision=prec) for _ in range(S)]
-    dev = devs[0]
-    lib = dev.lib
-    nets = [Roma(d, main, dino, v2, H=H, W=W, coarse=COARSE) for d in devs]
-    net = nets[0]
+    B = max(1, args.batch)
     ntiles = args.tiles
     tiles = make_tiles(rank_tile_seeds(rank, ntiles))
-    hw3 = 3 * H * W
-    # Device-resident tiles, and each graph's fixed input buffers.
-    dtiles = [(dev.upload(a), dev.upload(b)) for a, b in tiles]
-    ins = [(d.alloc(hw3 * 4), d.alloc(hw3 * 4)) for d in devs]
-
-    def load_tile(s, i):
-        a, b = dtiles[i % ntiles]
-        lib.ocl_copy(devs[s].ocl_p, a.handle, 0, ins[s][0].handle, 0, hw3 * 4)
-        lib.ocl_copy(devs[s].ocl_p, b.handle, 0, ins[s][1].handle, 0, hw3 * 4)
-
-    kernels = [nets[s].graph_build(ins[s][0].ptr, ins[s][1].ptr) for s in range(S)]
-    for i in range(max(args.warmup, S)):
-        load_tile(i % S, i)
-        nets[i % S].graph_launch()
-    for d, n_ in zip(devs, nets):
-        d.finish()
-        n_.sync()
+    pipes = Pipelines(local, prec, S, tiles, weights)
+    lib, dev, nets = pipes.lib, pipes.dev, pipes.nets
+    hw3 = pipes.hw3
+    for i in range(max(args.warmup * B, S)):
+        pipes.launch(i)
+    pipes.sync()
     barrier(world)
     with Clocks(local) as clk:
-        lib.ocl_timer_start(dev.ocl_p)
-        for s in range(1, S):
-            lib.ocl_join(devs[s].ocl_p, dev.ocl_p)
-        for i in range(args.steps):
-            load_tile(i % S, i)
-            nets[i % S].graph_launch()
-        for s in range(1, S):
-            lib.ocl_join(dev.ocl_p, devs[s].ocl_p)
-        ms = lib.ocl_timer_stop(dev.ocl_p)
-    coreg.check(lib)
-    for n_ in nets:
-        n_.sync()
+        ms, launches = pipes.timed(args.steps * B)
     ms_max = allmax(world, ms)
-    value = world * args.steps / (ms_max / 1000.0)
+    value = world * args.steps * B / (ms_max / 1000.0)
 
     # End to end through the public API: host (pinned) images in, host
-    # results out, per step; one host thread per pipeline (roma_match is
-    # synchronous), wall clock.
+    # results out, per tile pair; one host thread per pipeline (roma_match
+    # is synchronous), wall clock over the same number of tile pairs as the
+    # timed region.
     import ctypes
     import threading
 
@@ -408,7 +548,7 @@ def gpu_arm(args, rank, world, local):
 
     e2e_run(1)
     barrier(world)
-    e2e_per = max(1, args.steps // (2 * S))
+    e2e_per = max(1, args.steps * B // S)
     t0 = time.perf_counter()
     e2e_run(e2e_per)
     e2e_ms = (time.perf_counter() - t0) * 1000.0
@@ -419,7 +559,8 @@ def gpu_arm(args, rank, world, local):
         lib.coreg_host_free(pb)
 
     # Roofline of the dominant kernel, from one profiled tile.
-    prof = profile_step(lib, dev, net, ins[0][0].ptr, ins[0][1].ptr)
+    prof = profile_step(lib, dev, nets[0], pipes.ins[0][0].ptr, pipes.ins[0][1].ptr)
+    pipes.close()
     fl, by = work_model(es=2 if prec else 4)
     hbm, bf16, peak_kind = peaks()
     # The dominant profiled operation that has a work model and a DRAM
@@ -435,19 +576,24 @@ def gpu_arm(args, rank, world, local):
         ach = fl[dom] / (ms_d / 1000.0) / 1e12
         roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
                 "frac": ach / bf16, "peak_kind": peak_kind,
-                "traffic": traffic_from_profiles(dom), "launches_per_step": calls,
+                "traffic": traffic_from_profiles(dom), "launches_per_step": calls * B,
                 "algorithmic_per_launch": fl[dom] / calls}
     elif dom in by:
         ms_d, calls = prof[dom]
         ach = by[dom] / (ms_d / 1000.0) / 1e9
         roof = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": hbm, "unit": "GB/s",
                 "frac": ach / hbm, "peak_kind": peak_kind,
-                "traffic": traffic_from_profiles(dom), "launches_per_step": calls,
+                "traffic": traffic_from_profiles(dom), "launches_per_step": calls * B,
                 "algorithmic_per_launch": by[dom] / calls}
     tot_ms = sum(v[0] for v in prof.values())
     shares = sorted(((k, v[0] / tot_ms) for k, v in prof.items()), key=lambda x: -x[1])[:14]
     flops_pair = sum(fl.values())
 
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_extra:
+        if prec == coreg.OPS_BF16:
+            extra["fp32_mode"] = fp32_mode(local, tiles, weights)
+        extra["secondary"] = secondary(local, bf16)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -464,39 +610,33 @@ def gpu_arm(args, rank, world, local):
             "vs_baseline": None, "dtype": "bf16" if prec else "f32",
             "data": "synthetic (seeded scene generator per 1024^2 tile, resampled to 864^2; "
                     "random-init weights seed 0)",
-            "config": {"workload": "roma_v2ref tile pair: coarse 560, fine 864x864 "
-                                   "(BASELINE configs[3])",
-                       "tile_px": H, "coarse_px": COARSE, "tiles_per_rank": ntiles,
-                       "pipelines_per_gpu": S,
-                       "parallelism": f"tiles sharded over {world} GPU(s), {S} concurrent "
-                                      "tile pipelines (streams) per GPU",
-                       "l2": "no flush: every step streams the weights and activations "
-                             "(> 1 GB) through the 126 MB L2"},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * hw3 * 4,
-                    "d2h_bytes_per_step": 4 * H * W * 4,
+            "config": bench_config(args, world),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * 2 * hw3 * 4,
+                    "d2h_bytes_per_step": B * 4 * H * W * 4,
                     "api": "roma_match (host images in pinned memory, host results)"},
-            "gpu_launches": sum(kernels[i % S] for i in range(args.steps)),
+            "gpu_launches": launches,
             "roofline": roof,
-            "path_tflops": flops_pair / (ms_max / args.steps / 1000.0) / 1e12,
+            "path_tflops": flops_pair / (ms_max / (args.steps * B) / 1000.0) / 1e12,
             "time_shares": {k: round(v, 4) for k, v in shares},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
-    for n_, d in zip(nets, devs):
-        n_.close()
-        d.close()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--tiles", type=int, default=4, help="distinct tile pairs per GPU")
+    ap.add_argument("--batch", type=int, default=8, help="tile pairs per step")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the float32-mode and secondary workloads")
     ap.add_argument("--streams", type=int, default=4,
                     help="concurrent tile pipelines (streams, models) per GPU")
     args = ap.parse_args()
