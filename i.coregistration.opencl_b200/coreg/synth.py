@@ -363,6 +363,25 @@ def scene_pair(seed, H, W, bands=3, sigma=3.0, drift=12.0, patches=64):
             np.stack([mx, my]))
 
 
+def grey_affine_pair(seed, H, W):
+    """Config-2 pair (Efficient LoFTR): A = band-limited noise (N(128, 40),
+    Gaussian sigma 3 px, clipped) from seed; B = A under a seeded affine
+    (rotation within 5 degrees, scale 0.95..1.05, shift within 20 px, from
+    seed + 1) plus N(0, 3) noise. uint8 (H, W) each."""
+    rng = np.random.default_rng(seed)
+    a = band_limited(rng, H, W, 3.0)
+    r = np.random.default_rng(seed + 1)
+    ang = np.deg2rad(r.uniform(-5, 5))
+    sc = r.uniform(0.95, 1.05)
+    tx, ty = r.uniform(-20, 20, 2)
+    yy, xx = np.mgrid[0:H, 0:W].astype(np.float64)
+    cx, cy = W / 2, H / 2
+    mx = cx + sc * (np.cos(ang) * (xx - cx) - np.sin(ang) * (yy - cy)) + tx
+    my = cy + sc * (np.sin(ang) * (xx - cx) + np.cos(ang) * (yy - cy)) + ty
+    b = warp_bilinear(a[None], mx, my)[0] + r.normal(0, 3, (H, W))
+    return np.clip(a, 0, 255).astype(np.uint8), np.clip(b, 0, 255).astype(np.uint8)
+
+
 def tile_input(img_u8, H, W):
     """uint8 (3, h, w) tile to the matcher input: (3, H, W) float32 in
     0..1, zero padded (the reference's tile_input, main.c)."""

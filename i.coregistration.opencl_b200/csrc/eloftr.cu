@@ -582,10 +582,10 @@ void coarse_match(struct eloftr_model *m)
     fill_f_k<<<cdiv(n, 256), 256, 0, st>>>((float *)I->col_s->ptr, n, 0.0f);
     fill_f_k<<<cdiv(n, 256), 256, 0, st>>>((float *)I->col_max->ptr, n, -1.0f);
     fill_i_k<<<cdiv(n, 256), 256, 0, st>>>((int *)I->col_arg->ptr, n, -1);
-    // The scores in float32, whatever the ops precision: the match indices
-    // are compared exactly.
-    const int prec = o->precision;
-    o->precision = OPS_FP32;
+    // The scores in the context's precision: float32 contexts give the
+    // reference's match indices exactly; bfloat16 contexts take the score
+    // product on the tensor cores (bfloat16 features, float32 sums), which
+    // can only move matches whose confidence or mutual test is a near-tie.
     for (int pass = 0; pass < 2; pass++)
         for (int r0 = 0; r0 < n; r0 += R) {
             const int rows = n - r0 < R ? n - r0 : R;
@@ -606,7 +606,6 @@ void coarse_match(struct eloftr_model *m)
                                                          (int *)I->col_arg->ptr);
             }
         }
-    o->precision = prec;
     if (!launch_ok("eloftr coarse matching"))
         return;
     std::vector<float> rmax(n);
