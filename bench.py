@@ -512,55 +512,37 @@ def gpu_arm(args, rank, world, local):
     ms_max = allmax(world, ms)
     value = world * args.steps * B / (ms_max / 1000.0)
 
-    # End to end through the public API: host (pinned) images in, host
-    # results out, per tile pair; one host thread per pipeline (roma_match
-    # is synchronous), wall clock over the same number of tile pairs as the
-    # timed region.
-    import ctypes
-    import threading
-
-    pin = []
-    for a, b in tiles:
-        pa = lib.coreg_host_alloc(hw3 * 4)
-        pb = lib.coreg_host_alloc(hw3 * 4)
-        ctypes.memmove(pa, a.ctypes.data, hw3 * 4)
-        ctypes.memmove(pb, b.ctypes.data, hw3 * 4)
-        pin.append((pa, pb))
-    errors = []
-
-    def e2e_worker(s, count):
-        try:
-            for j in range(count):
-                pa, pb = pin[(s + S * j) % ntiles]
-                lib.roma_match(nets[s].mp, pa, pb, None, 1)
-            coreg.check(lib)
-        except Exception as e:  # reported on the main thread
-            errors.append(e)
-
-    def e2e_run(count_per):
-        th = [threading.Thread(target=e2e_worker, args=(s, count_per)) for s in range(S)]
-        for t_ in th:
-            t_.start()
-        for t_ in th:
-            t_.join()
-        if errors:
-            raise errors[0]
-
-    e2e_run(1)
-    barrier(world)
-    e2e_per = max(1, args.steps * B // S)
-    t0 = time.perf_counter()
-    e2e_run(e2e_per)
-    e2e_ms = (time.perf_counter() - t0) * 1000.0
-    e2e_max = allmax(world, e2e_ms)
-    e2e_value = world * S * e2e_per / (e2e_max / 1000.0)
-    for pa, pb in pin:
-        lib.coreg_host_free(pa)
-        lib.coreg_host_free(pb)
-
     # Roofline of the dominant kernel, from one profiled tile.
     prof = profile_step(lib, dev, nets[0], pipes.ins[0][0].ptr, pipes.ins[0][1].ptr)
     pipes.close()
+
+    # End to end through the library's tile queue (roma_tiles.h), the call
+    # a user with a scene makes: S pipelines on this GPU, each tile's host
+    # images copied into a pipeline's pinned inputs, roma_match (copies in,
+    # the tile, copies out), the host results handed back in tile order;
+    # wall clock over as many tile pairs as the timed region.
+    from coreg.roma import RomaTiles
+
+    q = RomaTiles([local], S, prec, *weights, H=H, W=W, coarse=COARSE)
+
+    def get(i, a, b):
+        a[...] = tiles[i % ntiles][0]
+        b[...] = tiles[i % ntiles][1]
+
+    def put(i, flow, cert, sd):
+        pass
+
+    try:
+        q.run(S, get, put)
+        barrier(world)
+        t0 = time.perf_counter()
+        e2e_tiles = q.run(args.steps * B, get, put)
+        e2e_ms = (time.perf_counter() - t0) * 1000.0
+    finally:
+        q.close()
+    e2e_max = allmax(world, e2e_ms)
+    e2e_value = world * e2e_tiles / (e2e_max / 1000.0)
+
     fl, by = work_model(es=2 if prec else 4)
     hbm, bf16, peak_kind = peaks()
     # The dominant profiled operation that has a work model and a DRAM
@@ -613,7 +595,8 @@ def gpu_arm(args, rank, world, local):
             "config": bench_config(args, world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * 2 * hw3 * 4,
                     "d2h_bytes_per_step": B * 4 * H * W * 4,
-                    "api": "roma_match (host images in pinned memory, host results)"},
+                    "api": "roma_tiles_run (host images into pinned inputs, roma_match per "
+                           "tile, host results in tile order)"},
             "gpu_launches": launches,
             "roofline": roof,
             "path_tflops": flops_pair / (ms_max / (args.steps * B) / 1000.0) / 1e12,

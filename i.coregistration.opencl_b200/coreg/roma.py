@@ -113,7 +113,15 @@ EXTRA_SIGNATURES.update({
     "roma_sample_matches": (I, [P, P, P, P, I, I, I, I, I, F, P, P, C.POINTER(MatchList)]),
     "roma_dense_field": (None, [P, P, P, I, I, I, I, P, P, P, P, P, P]),
     "eloftr_sample_matches": (I, [P, P, I, I, I, P, P, C.POINTER(MatchList)]),
+    "roma_tiles_create": (P, [C.POINTER(C.c_int), I, I, I, C.c_char_p, C.c_char_p, C.c_char_p,
+                              I, I, I, I]),
+    "roma_tiles_run": (I, [P, I, P, P, P]),
+    "roma_tiles_pipelines": (I, [P]),
+    "roma_tiles_free": (None, [P]),
 })
+
+TILE_GET = C.CFUNCTYPE(None, P, I, C.POINTER(F), C.POINTER(F))
+TILE_PUT = C.CFUNCTYPE(None, P, I, C.POINTER(F), C.POINTER(F), C.POINTER(F))
 
 
 def open_pth(lib, path):
@@ -192,3 +200,58 @@ class Roma:
         if self.mp is not None:
             self.lib.roma_free(self.mp)
             self.mp = None
+
+
+class RomaTiles:
+    """roma_tiles.h: pipelines of RoMa models on several devices (or
+    several per device), tiles dealt to free pipelines, results in tile
+    order."""
+
+    def __init__(self, devices, per_device, precision, main, dino, v2=None, H=864, W=864,
+                 coarse=560, imagenet=True):
+        self.lib = lib = load()
+        devs = (C.c_int * len(devices))(*devices)
+        self.h = lib.roma_tiles_create(devs, len(devices), per_device, precision,
+                                       str(main).encode(), str(dino).encode(),
+                                       str(v2).encode() if v2 else None, H, W, coarse,
+                                       int(imagenet))
+        check(lib)
+        self.H, self.W = H, W
+
+    @property
+    def pipelines(self):
+        return self.lib.roma_tiles_pipelines(self.h)
+
+    def run(self, ntiles, get, put):
+        """get(index, imgA, imgB) fills two (3, H, W) float32 numpy views of
+        the pipeline's pinned inputs; put(index, flow, cert, sd) receives
+        numpy views (valid during the call; sd None without v2), in
+        index order. Returns the number of tiles delivered."""
+        H, W = self.H, self.W
+        errors = []
+
+        def c_get(_ctx, idx, a, b):
+            try:
+                get(idx, np.ctypeslib.as_array(a, (3, H, W)), np.ctypeslib.as_array(b, (3, H, W)))
+            except Exception as e:  # re-raised on the calling thread
+                errors.append(e)
+
+        def c_put(_ctx, idx, flow, cert, sd):
+            try:
+                put(idx, np.ctypeslib.as_array(flow, (2, H, W)),
+                    np.ctypeslib.as_array(cert, (H, W)),
+                    np.ctypeslib.as_array(sd, (H, W)) if sd else None)
+            except Exception as e:
+                errors.append(e)
+
+        g, p = TILE_GET(c_get), TILE_PUT(c_put)
+        n = self.lib.roma_tiles_run(self.h, ntiles, C.cast(g, P), C.cast(p, P), None)
+        check(self.lib)
+        if errors:
+            raise errors[0]
+        return n
+
+    def close(self):
+        if self.h:
+            self.lib.roma_tiles_free(self.h)
+            self.h = None

@@ -135,6 +135,11 @@ struct roma_impl {
     bool alloc_done = false;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+    // roma_match's own graph of the tile over in_dev, built on its first
+    // call without dumps or profiling.
+    cudaGraph_t match_graph = nullptr;
+    cudaGraphExec_t match_exec = nullptr;
+    int match_imagenet = -1;  // m->imagenet when match_graph was captured
 };
 
 // ------------------------------------------------------------- utilities
@@ -772,6 +777,10 @@ extern "C" void roma_free(struct roma_model *m)
             cudaGraphExecDestroy(I->graph_exec);
         if (I->graph)
             cudaGraphDestroy(I->graph);
+        if (I->match_exec)
+            cudaGraphExecDestroy(I->match_exec);
+        if (I->match_graph)
+            cudaGraphDestroy(I->match_graph);
         for (void *p : I->allocs)
             cudaFree(p);
         delete I;
@@ -1548,6 +1557,55 @@ bool ready(struct roma_model *m)
 
 }  // namespace
 
+namespace {
+
+// The tile over the device images inA, inB captured into *graph and
+// instantiated into *exec (both replaced); the kernel count, or -1 after
+// recording an error.
+int capture_tile(struct roma_model *m, const float *inA, const float *inB, cudaGraph_t *graph,
+                 cudaGraphExec_t *exec)
+{
+    roma_impl *I = m->impl;
+    cudaStream_t st = stream_of(m->ocl);
+    if (*exec) {
+        cudaGraphExecDestroy(*exec);
+        *exec = nullptr;
+    }
+    if (*graph) {
+        cudaGraphDestroy(*graph);
+        *graph = nullptr;
+    }
+    if (!cuda_ok(cudaStreamSynchronize(st), "RoMa graph capture") ||
+        !cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal),
+                 "cudaStreamBeginCapture"))
+        return -1;
+    Ctx c{m, I, st, nullptr, 0};
+    run_tile(c, inA, inB);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (pending() || !cuda_ok(e, "cudaStreamEndCapture")) {
+        if (g)
+            cudaGraphDestroy(g);
+        return -1;
+    }
+    *graph = g;
+    if (!cuda_ok(cudaGraphInstantiate(exec, g, 0), "cudaGraphInstantiate"))
+        return -1;
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    int kernels = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        cudaGraphNodeGetType(nd, &t);
+        kernels += t == cudaGraphNodeTypeKernel;
+    }
+    return kernels;
+}
+
+}  // namespace
+
 extern "C" void roma_match_dev(struct roma_model *m, const float *imgA,
                                const float *imgB)
 {
@@ -1604,7 +1662,24 @@ extern "C" void roma_match(struct roma_model *m, const float *imgA,
                  "roma_match input"))
         return;
     Ctx c{m, I, st, dump && *dump ? dump : nullptr, tile};
-    run_tile(c, I->in_dev[0], I->in_dev[1]);
+    if (c.dump || m->ocl->profile) {
+        // Dumps read back between stages, and profiling times each
+        // launch: the tile runs launch by launch.
+        run_tile(c, I->in_dev[0], I->in_dev[1]);
+    }
+    else {
+        // Otherwise one launch of the tile's graph over in_dev (captured on
+        // the first such call, again if m->imagenet changed): the host
+        // issues one launch instead of the tile's several hundred.
+        if (!I->match_exec || I->match_imagenet != m->imagenet) {
+            if (capture_tile(m, I->in_dev[0], I->in_dev[1], &I->match_graph, &I->match_exec) <
+                0)
+                return;
+            I->match_imagenet = m->imagenet;
+        }
+        if (!cuda_ok(cudaGraphLaunch(I->match_exec, st), "cudaGraphLaunch"))
+            return;
+    }
     cudaMemcpyAsync(m->flow, I->o_flow, 2 * hw * 4, cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(m->cert, I->o_cert, hw * 4, cudaMemcpyDeviceToHost, st);
     if (m->v2)
@@ -1625,43 +1700,7 @@ extern "C" int roma_graph_build(struct roma_model *m, const float *imgA,
     if (!ready(m))
         return -1;
     cudaSetDevice(m->ocl->device);
-    roma_impl *I = m->impl;
-    cudaStream_t st = stream_of(m->ocl);
-    if (I->graph_exec) {
-        cudaGraphExecDestroy(I->graph_exec);
-        I->graph_exec = nullptr;
-    }
-    if (I->graph) {
-        cudaGraphDestroy(I->graph);
-        I->graph = nullptr;
-    }
-    if (!cuda_ok(cudaStreamSynchronize(st), "roma_graph_build") ||
-        !cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal),
-                 "cudaStreamBeginCapture"))
-        return -1;
-    Ctx c{m, I, st, nullptr, 0};
-    run_tile(c, imgA, imgB);
-    cudaGraph_t g = nullptr;
-    cudaError_t e = cudaStreamEndCapture(st, &g);
-    if (pending() || !cuda_ok(e, "cudaStreamEndCapture")) {
-        if (g)
-            cudaGraphDestroy(g);
-        return -1;
-    }
-    I->graph = g;
-    if (!cuda_ok(cudaGraphInstantiate(&I->graph_exec, g, 0), "cudaGraphInstantiate"))
-        return -1;
-    size_t n = 0;
-    cudaGraphGetNodes(g, nullptr, &n);
-    std::vector<cudaGraphNode_t> nodes(n);
-    cudaGraphGetNodes(g, nodes.data(), &n);
-    int kernels = 0;
-    for (auto nd : nodes) {
-        cudaGraphNodeType t;
-        cudaGraphNodeGetType(nd, &t);
-        kernels += t == cudaGraphNodeTypeKernel;
-    }
-    return kernels;
+    return capture_tile(m, imgA, imgB, &m->impl->graph, &m->impl->graph_exec);
 }
 
 extern "C" void roma_graph_launch(struct roma_model *m)

@@ -77,7 +77,10 @@ void roma_alloc(struct roma_model *m, int H, int W);
  * the alloc size (host memory): results in m->flow, m->cert, m->sd. With
  * dump set (a folder), the inputs and intermediate tensors are written
  * there as tileNNN_roma_<what>.f32 in the reference's layouts and names
- * (roma.c:1188-1227). */
+ * (roma.c:1188-1227). Without dump and with profiling off, the tile runs
+ * as one CUDA graph of the model, captured on the first such call (and
+ * again when m->imagenet changes), so that call must not come inside a
+ * stream capture of the calling thread. */
 void roma_match(struct roma_model *m, const float *imgA, const float *imgB,
                 const char *dump, int tile);
 
