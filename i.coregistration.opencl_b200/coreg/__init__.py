@@ -135,6 +135,7 @@ SIGNATURES = {
     "ops_gemm_noalloc": (None, [C.POINTER(Ops), I, I, I, Opnd, Opnd, I, Opnd, I, I, P, I, P, L, F, I, F]),
     "ops_gemm_noalloc_max_bytes": (C.c_size_t, []),
     "ops_attention_qkv": (None, [C.POINTER(Ops), P, I, I, I, F, P]),
+    "roma_gp_solve": (I, [C.POINTER(Ops), P, I, P, I, C.c_double, P]),
 }
 
 _lib = None

@@ -34,8 +34,11 @@ struct disk_impl {
     cl_mem input = nullptr, f[5] = {}, u[3] = {}, tmp = nullptr, cat = nullptr,
            out = nullptr, mean = nullptr, rstd = nullptr, mask = nullptr, xy = nullptr,
            desc = nullptr;
-    std::vector<float> heat;
-    std::vector<unsigned char> maskh;
+    // Keypoint selection on the device: the valid mask, per-block candidate
+    // counts and offsets, the candidates (score, cell) in raster order, the
+    // selected scores and the selection's count and cut.
+    cl_mem valid = nullptr, counts = nullptr, cscore = nullptr, ccell = nullptr,
+           score = nullptr, sel = nullptr;
 };
 
 namespace {
@@ -80,11 +83,11 @@ __global__ void nms5x5_k(const float *heat, int W, int h, int w, float thresh,
 
 // disk_kernels.cl:39-60: descriptor channels 0..D-1 at the keypoints,
 // L2-normalized (eps 1e-12). One warp per keypoint.
-__global__ void gather_desc_k(const float *feat, int H, int W, int D, const int *xy, int n,
-                              float *desc)
+__global__ void gather_desc_k(const float *feat, int H, int W, int D, const int *xy,
+                              const int *count, float *desc)
 {
     const int k = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
-    if (k >= n)
+    if (k >= *count)
         return;
     const long plane = (long)H * W, off = (long)xy[2 * k + 1] * W + xy[2 * k];
     float ss = 0.0f;
@@ -96,6 +99,225 @@ __global__ void gather_desc_k(const float *feat, int H, int W, int D, const int 
     const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
     for (int d = lane; d < D; d += 32)
         desc[(long)k * D + d] = feat[d * plane + off] * inv;
+}
+
+// ------------------------------------------- keypoint selection kernels
+//
+// The n-best rule of disk.c:236-266 (kornia heatmap_to_keypoints) on the
+// device: the NMS candidates of the h x w crop (valid cells only) in raster
+// order, the (n + 1)-th highest score as the cut (with n or fewer
+// candidates the lowest), then the candidates strictly above the cut in
+// raster order, at most n. Same values, same comparisons as the host
+// rule, so the same keypoints.
+
+constexpr int SEL_BLOCK = 1024;  // cells per block of the compaction
+
+// Candidates per block of SEL_BLOCK cells.
+__global__ void __launch_bounds__(SEL_BLOCK)
+cand_count_k(const unsigned char *mask, const unsigned char *valid, long cells, int *counts)
+{
+    __shared__ int wsum[SEL_BLOCK / 32];
+    const long i = (long)blockIdx.x * SEL_BLOCK + threadIdx.x;
+    const bool c = i < cells && mask[i] && (!valid || valid[i]);
+    const unsigned b = __ballot_sync(0xffffffffu, c);
+    if (threadIdx.x % 32 == 0)
+        wsum[threadIdx.x / 32] = __popc(b);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int v = wsum[threadIdx.x];
+        for (int o = 16; o > 0; o /= 2)
+            v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0)
+            counts[blockIdx.x] = v;
+    }
+}
+
+// Exclusive scan of nb counts in place (one block); the total into
+// counts[nb].
+__global__ void __launch_bounds__(SEL_BLOCK) cand_scan_k(int *counts, int nb)
+{
+    __shared__ int wsum[SEL_BLOCK / 32];
+    __shared__ int carry;
+    if (threadIdx.x == 0)
+        carry = 0;
+    __syncthreads();
+    for (int base = 0; base < nb; base += SEL_BLOCK) {
+        const int i = base + threadIdx.x, lane = threadIdx.x % 32, wp = threadIdx.x / 32;
+        const int v = i < nb ? counts[i] : 0;
+        int x = v;
+        for (int o = 1; o < 32; o *= 2) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o)
+                x += y;
+        }
+        if (lane == 31)
+            wsum[wp] = x;
+        __syncthreads();
+        if (wp == 0) {
+            int w = wsum[lane];
+            for (int o = 1; o < 32; o *= 2) {
+                const int y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o)
+                    w += y;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const int excl = carry + (wp ? wsum[wp - 1] : 0) + x - v;
+        __syncthreads();
+        if (i < nb)
+            counts[i] = excl;
+        if (threadIdx.x == SEL_BLOCK - 1)
+            carry = excl + v;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        counts[nb] = carry;
+}
+
+// The candidates of each block, in raster order, at the block's offset:
+// their score (heat at row pitch W) and cell (y w + x of the crop).
+__global__ void __launch_bounds__(SEL_BLOCK)
+cand_write_k(const unsigned char *mask, const unsigned char *valid, const float *heat, int W,
+             int w, long cells, const int *offs, float *cscore, int *ccell)
+{
+    __shared__ int wsum[SEL_BLOCK / 32];
+    const long i = (long)blockIdx.x * SEL_BLOCK + threadIdx.x;
+    const int lane = threadIdx.x % 32, wp = threadIdx.x / 32;
+    const bool c = i < cells && mask[i] && (!valid || valid[i]);
+    const unsigned b = __ballot_sync(0xffffffffu, c);
+    if (lane == 0)
+        wsum[wp] = __popc(b);
+    __syncthreads();
+    if (wp == 0) {
+        int x = wsum[lane];
+        for (int o = 1; o < 32; o *= 2) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o)
+                x += y;
+        }
+        wsum[lane] = x;
+    }
+    __syncthreads();
+    if (c) {
+        const int pos = offs[blockIdx.x] + (wp ? wsum[wp - 1] : 0) +
+                        __popc(b & ((1u << lane) - 1u));
+        const long y = i / w, x = i % w;
+        cscore[pos] = heat[y * W + x];
+        ccell[pos] = (int)i;
+    }
+}
+
+// Order-preserving key of a float (larger float, larger key).
+__device__ __forceinline__ unsigned fkey(float f)
+{
+    const unsigned u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : u | 0x80000000u;
+}
+
+__device__ __forceinline__ float fkey_inv(unsigned k)
+{
+    return __uint_as_float((k & 0x80000000u) ? k & 0x7fffffffu : ~k);
+}
+
+// The cut of the n-best rule over the C = *total candidate scores: the
+// (n + 1)-th highest (0-based rank kk = min(n, C - 1) from the top) by a
+// 4-round radix select on the keys, into sel[1] (as a float's bits); -inf
+// without candidates. One block.
+__global__ void __launch_bounds__(SEL_BLOCK)
+select_cut_k(const float *cscore, const int *total, int n, int *sel)
+{
+    __shared__ unsigned hist[256];
+    __shared__ unsigned prefix, pmask;
+    __shared__ int rank;
+    const int C = *total;
+    if (C == 0) {
+        if (threadIdx.x == 0)
+            sel[1] = __float_as_int(-INFINITY);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        prefix = 0;
+        pmask = 0;
+        // Rank from the bottom of the wanted key.
+        rank = C - 1 - (C > n ? n : C - 1);
+    }
+    __syncthreads();
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int t = threadIdx.x; t < 256; t += SEL_BLOCK)
+            hist[t] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < C; i += SEL_BLOCK) {
+            const unsigned k = fkey(cscore[i]);
+            if ((k & pmask) == prefix)
+                atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int r = rank;
+            unsigned d = 0;
+            for (; d < 256; d++) {
+                if (r < (int)hist[d])
+                    break;
+                r -= hist[d];
+            }
+            rank = r;
+            prefix |= d << shift;
+            pmask |= 255u << shift;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        sel[1] = __float_as_int(fkey_inv(prefix));
+}
+
+// The candidates strictly above the cut, in raster order, at most n: x, y
+// into xy, scores into score, their count into sel[0]. One block walks
+// the candidates SEL_BLOCK at a time.
+__global__ void __launch_bounds__(SEL_BLOCK)
+select_write_k(const float *cscore, const int *ccell, const int *total, int w, int n, int *sel,
+               int *xy, float *score)
+{
+    __shared__ int wsum[SEL_BLOCK / 32];
+    __shared__ int base;
+    const int C = *total;
+    const float cut = __int_as_float(sel[1]);
+    const int lane = threadIdx.x % 32, wp = threadIdx.x / 32;
+    if (threadIdx.x == 0)
+        base = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < C; c0 += SEL_BLOCK) {
+        if (base >= n)
+            break;
+        const int i = c0 + threadIdx.x;
+        const bool keep = i < C && cscore[i] > cut;
+        const unsigned b = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0)
+            wsum[wp] = __popc(b);
+        __syncthreads();
+        if (wp == 0) {
+            int x = wsum[lane];
+            for (int o = 1; o < 32; o *= 2) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o)
+                    x += y;
+            }
+            wsum[lane] = x;
+        }
+        __syncthreads();
+        const int pos = base + (wp ? wsum[wp - 1] : 0) + __popc(b & ((1u << lane) - 1u));
+        if (keep && pos < n) {
+            xy[2 * pos] = ccell[i] % w;
+            xy[2 * pos + 1] = ccell[i] / w;
+            score[pos] = cscore[i];
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            base += wsum[SEL_BLOCK / 32 - 1];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        sel[0] = base < n ? base : n;
 }
 
 void conv(struct disk_model *m, int l, cl_mem in, int H, int W, cl_mem out)
@@ -171,8 +393,13 @@ extern "C" void disk_alloc(struct disk_model *m, int H, int W, int nmax)
     I->mask = ocl_alloc(ocl, px, "nms mask");
     I->xy = ocl_alloc(ocl, 2 * (size_t)nmax * 4, "keypoints");
     I->desc = ocl_alloc(ocl, (size_t)nmax * DISK_DESC * 4, "descriptors");
-    I->heat.resize(px);
-    I->maskh.resize(px);
+    const long nblk = cdiv((long)px, SEL_BLOCK);
+    I->valid = ocl_alloc(ocl, px, "valid mask");
+    I->counts = ocl_alloc(ocl, (nblk + 1) * 4, "candidate counts");
+    I->cscore = ocl_alloc(ocl, px * 4, "candidate scores");
+    I->ccell = ocl_alloc(ocl, px * 4, "candidate cells");
+    I->score = ocl_alloc(ocl, (size_t)nmax * 4, "keypoint scores");
+    I->sel = ocl_alloc(ocl, 2 * 4, "selection");
 }
 
 extern "C" int disk_detect(struct disk_model *m, const float *img, int H, int W, int h,
@@ -222,54 +449,40 @@ extern "C" int disk_detect(struct disk_model *m, const float *img, int H, int W,
         ops_chan_stats(m->ops, I->cat, cb + ch, (int)plane, 1e-5f, I->mean, I->rstd);
         conv(m, l, I->cat, hh, ww, j < 3 ? I->u[j] : I->out);
     }
-    // Heatmap NMS on the h x w crop.
+    // Heatmap NMS on the h x w crop, then the n-best selection and the
+    // descriptor gather on the device; only the keypoints come back.
     const float *heat = (const float *)I->out->ptr + (size_t)DISK_DESC * px;
     nms5x5_k<<<dim3(cdiv(w, 128), h), 128, 0, st>>>(heat, W, h, w, thresh,
                                                     (unsigned char *)I->mask->ptr);
-    if (!launch_ok("nms5x5"))
-        return 0;
-    ocl_read(ocl, I->mask, 0, I->maskh.data(), (size_t)h * w);
-    ocl_read(ocl, I->out, (size_t)DISK_DESC * px * 4, I->heat.data(), (size_t)h * W * 4);
-    if (pending())
-        return 0;
-
-    // The n highest candidates in raster order: those above the (n + 1)-th
-    // highest score (disk.c:236-266, kornia heatmap_to_keypoints; with n or
-    // fewer candidates the lowest is the threshold and is dropped).
-    std::vector<float> cand;
-    cand.reserve((size_t)h * w / 8 + 1);
-    for (int y = 0; y < h; y++)
-        for (int x = 0; x < w; x++) {
-            const size_t i = (size_t)y * w + x;
-            if (I->maskh[i] && (!valid || valid[i]))
-                cand.push_back(I->heat[(size_t)y * W + x]);
-        }
-    float cut = -INFINITY;
-    if (!cand.empty()) {
-        const size_t kth = cand.size() > (size_t)n ? (size_t)n : cand.size() - 1;
-        std::nth_element(cand.begin(), cand.begin() + kth, cand.end(), std::greater<float>());
-        cut = cand[kth];
+    const long cells = (long)h * w;
+    const int nb = (int)cdiv(cells, SEL_BLOCK);
+    const unsigned char *vd = nullptr;
+    if (valid) {
+        ocl_write(ocl, I->valid, 0, valid, (size_t)cells);
+        vd = (const unsigned char *)I->valid->ptr;
     }
+    int *counts = (int *)I->counts->ptr, *sel = (int *)I->sel->ptr;
+    const unsigned char *mk = (const unsigned char *)I->mask->ptr;
+    cand_count_k<<<nb, SEL_BLOCK, 0, st>>>(mk, vd, cells, counts);
+    cand_scan_k<<<1, SEL_BLOCK, 0, st>>>(counts, nb);
+    cand_write_k<<<nb, SEL_BLOCK, 0, st>>>(mk, vd, heat, W, w, cells, counts,
+                                           (float *)I->cscore->ptr, (int *)I->ccell->ptr);
+    select_cut_k<<<1, SEL_BLOCK, 0, st>>>((const float *)I->cscore->ptr, counts + nb, n, sel);
+    select_write_k<<<1, SEL_BLOCK, 0, st>>>((const float *)I->cscore->ptr,
+                                            (const int *)I->ccell->ptr, counts + nb, w, n, sel,
+                                            (int *)I->xy->ptr, (float *)I->score->ptr);
+    gather_desc_k<<<cdiv(n, 8), 256, 0, st>>>((const float *)I->out->ptr, H, W, DISK_DESC,
+                                              (const int *)I->xy->ptr, sel,
+                                              (float *)I->desc->ptr);
+    if (!launch_ok("disk keypoint selection"))
+        return 0;
     int nk = 0;
-    for (int y = 0; y < h && nk < n; y++)
-        for (int x = 0; x < w && nk < n; x++) {
-            const size_t i = (size_t)y * w + x;
-            const float v = I->heat[(size_t)y * W + x];
-            if (!I->maskh[i] || (valid && !valid[i]) || !(v > cut))
-                continue;
-            xy[2 * nk] = x;
-            xy[2 * nk + 1] = y;
-            score[nk++] = v;
-        }
-    if (nk > 0) {
-        ocl_write(ocl, I->xy, 0, xy, 2 * (size_t)nk * 4);
-        gather_desc_k<<<cdiv(nk, 8), 256, 0, st>>>((const float *)I->out->ptr, H, W, DISK_DESC,
-                                                   (const int *)I->xy->ptr, nk,
-                                                   (float *)I->desc->ptr);
-        if (!launch_ok("gather_desc"))
-            return 0;
-        ocl_read(ocl, I->desc, 0, desc, (size_t)nk * DISK_DESC * 4);
-    }
+    ocl_read(ocl, I->sel, 0, &nk, sizeof(int));
+    if (pending() || nk <= 0)
+        return 0;
+    ocl_read(ocl, I->xy, 0, xy, 2 * (size_t)nk * 4);
+    ocl_read(ocl, I->score, 0, score, (size_t)nk * 4);
+    ocl_read(ocl, I->desc, 0, desc, (size_t)nk * DISK_DESC * 4);
     return pending() ? 0 : nk;
 }
 
@@ -288,7 +501,8 @@ extern "C" void disk_free(struct disk_model *m)
             ocl_release(&I->alpha[k]);
         }
         cl_mem *bufs[] = {&I->input, &I->tmp, &I->cat, &I->out, &I->mean, &I->rstd,
-                          &I->mask, &I->xy, &I->desc};
+                          &I->mask, &I->xy, &I->desc, &I->valid, &I->counts, &I->cscore,
+                          &I->ccell, &I->score, &I->sel};
         for (cl_mem *b : bufs)
             ocl_release(b);
         for (int k = 0; k < 5; k++)

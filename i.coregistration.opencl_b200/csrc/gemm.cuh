@@ -63,11 +63,11 @@ inline GemmArgs gemm_args(int M, int N, int K)
 
 // The rule by which ops_gemm (and ops_gemm_noalloc, which must give the
 // same results) rounds float32 operands to bfloat16 for the tensor-core
-// tiles: an OPS_BF16 context, a K-major B (transb) and a K the tiles take.
-inline bool gemm_packs_bf16(int precision, int M, int N, int K, int transb)
+// tiles: an OPS_BF16 context and a shape the tiles take. B is packed
+// K-major whichever its layout (transb or not).
+inline bool gemm_packs_bf16(int precision, int M, int N, int K)
 {
-    return precision == OPS_BF16 && transb && M >= 64 && N >= 1 && K >= 16 &&
-           K % 8 == 0;
+    return precision == OPS_BF16 && M >= 64 && N >= 1 && K >= 16 && K % 8 == 0;
 }
 
 // Float32 rows x cols of each of nb batch products (batch b at
@@ -75,6 +75,12 @@ inline bool gemm_packs_bf16(int precision, int M, int N, int K, int transb)
 // `cols`, batch after batch; rows are walked by a grid-stride loop, so any
 // row count launches.
 void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
+                    int nb1, int rows, int cols, __nv_bfloat16 *dst);
+
+// The transpose of the same: float32 rows x cols of each batch product into
+// packed bfloat16 rows of `rows` (cols x rows per product), so that a
+// K x N operand becomes N x K.
+void pack_bf16_cols(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
                     int nb1, int rows, int cols, __nv_bfloat16 *dst);
 
 // Float32 FMA tiles (the accurate path): any strides, any type mix.

@@ -8,8 +8,9 @@
 // double, then the two substitutions), whose device round trip
 // (roma.c:885-888) disappears.
 //
-// Blocks of NB = 64. One CTA factors each diagonal block and inverts it
-// (Linv_j), so that every other step is a double-precision GEMM. The
+// Blocks of NB = 64. One CTA of 256 threads factors each diagonal block
+// and inverts it (Linv_j), so that every other step is a double-precision
+// GEMM. The
 // working matrix A, the factor L and the right-hand sides F, Z, X live in
 // separate buffers, so no step multiplies in place:
 //   step j     L_jj, Linv_j           from A_jj
@@ -39,147 +40,100 @@ __global__ void gp_init_k(const float *K, int n, double noise, double *A)
 }
 
 constexpr int GP_P = GP_NB + 1;  // shared-memory pitch (doubles)
-
-// One warp: factor the 32 x 32 symmetric positive definite block S (pitch
-// GP_P) in place into its lower Cholesky factor (upper part zeroed) and
-// write the factor's inverse into Inv (pitch GP_P). Lane i holds row i in
-// registers; each column's entries are broadcast with shuffles (no block
-// barrier). The inverse is computed column by column (lane c solves
-// L x = e_c) in axpy order from the stored factor.
-__device__ void chol32_inv(double *S, double *Inv, int *flag, int lane)
-{
-    double r[32];
-#pragma unroll
-    for (int j = 0; j < 32; j++)
-        r[j] = S[lane * GP_P + j];
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        double d = __shfl_sync(0xffffffffu, r[k], k);
-        if (!(d > 0.0)) {
-            if (lane == 0)
-                *flag = 1;
-            d = 1.0;
-        }
-        const double rc = rsqrt(d);
-        if (lane == k)
-            r[k] = d * rc;
-        else if (lane > k)
-            r[k] *= rc;
-#pragma unroll
-        for (int j = k + 1; j < 32; j++) {
-            const double ljk = __shfl_sync(0xffffffffu, r[k], j);
-            if (lane >= j)
-                r[j] = fma(-r[k], ljk, r[j]);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < 32; j++)
-        S[lane * GP_P + j] = j <= lane ? r[j] : 0.0;
-    __syncwarp();
-    const double my_rd = 1.0 / S[lane * GP_P + lane];
-    double x[32];
-#pragma unroll
-    for (int m = 0; m < 32; m++)
-        x[m] = m == lane ? 1.0 : 0.0;
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        const double rdk = __shfl_sync(0xffffffffu, my_rd, k);
-        if (k >= lane) {
-            x[k] *= rdk;
-            const double xk = x[k];
-#pragma unroll
-            for (int m = k + 1; m < 32; m++)
-                x[m] = fma(-S[m * GP_P + k], xk, x[m]);
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < 32; m++)
-        Inv[m * GP_P + lane] = x[m];
-    __syncwarp();
-}
-
-// out = sum_k X(i, k) Y(k, j) for output row i = t / 8, columns (t % 8) 4
-// .. + 3 of a 32 x 32 product, X(i, k) = X[i xs + k xk], Y(k, j) = Y[k ys +
-// j yj]; 256 threads. Kept in registers until the caller's barrier.
-__device__ __forceinline__ void mm32(const double *X, int xs, int xk, const double *Y, int ys,
-                                     int yj, double out[4], int t)
-{
-    const int i = t / 8, j0 = (t % 8) * 4;
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-        out[q] = 0.0;
-#pragma unroll 8
-    for (int k = 0; k < 32; k++) {
-        const double x = X[i * xs + k * xk];
-#pragma unroll
-        for (int q = 0; q < 4; q++)
-            out[q] = fma(x, Y[k * ys + (j0 + q) * yj], out[q]);
-    }
-}
+// Elements of the 64 x 64 lower triangle each of the 256 threads owns.
+constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + 255) / 256;
 
 // Factor the b x b diagonal block of A at (j0, j0) (b <= 64; identity beyond
-// b) as 2 x 2 blocks of 32: L11 and its inverse by one warp, L21 =
-// A21 L11^-T, A22 -= L21 L21^T, L22 and its inverse by one warp, and
-// Inv21 = -Inv22 L21 Inv11. Writes the lower factor into L (pitch n) and
-// the 64 x 64 inverse into Linv.
+// b) with all 256 threads: a right-looking unblocked Cholesky in shared
+// memory, one barrier per column (thread t owns the lower-triangle elements
+// t, t + 256, ...: at column k it updates those right of k with the scaled
+// column, l_i = a_ik / sqrt(a_kk), a_ij -= l_i l_j, while the threads of
+// rows i > k write l_i into the factor), then the inverse of the factor,
+// four threads per column (each column of L^-1 by forward substitution,
+// the sums split four ways and joined by shuffles). Writes the lower
+// factor into L (pitch n) and the 64 x 64 inverse into Linv. A
+// non-positive pivot sets *flag (the factor is then meaningless, as the
+// reference's stop says).
 __global__ void __launch_bounds__(256)
 gp_potrf_inv_k(const double *A, double *L, int n, int j0, int b, double *Linv, int *flag)
 {
     extern __shared__ double gp_smem[];
-    double *M = gp_smem;                  // 64 x GP_P: the block, then L
-    double *Iv = gp_smem + GP_NB * GP_P;  // 64 x GP_P: the inverse
-    double *T = Iv + GP_NB * GP_P;        // 32 x GP_P: L21 Inv11
-    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
-    // Staging loops unrolled, so that each thread's loads are all in flight.
+    double *M = gp_smem;                  // 64 x GP_P: the block, updated
+    double *F = gp_smem + GP_NB * GP_P;   // 64 x GP_P: the factor
+    double *X = F + GP_NB * GP_P;         // 64 x GP_P: the inverse
+    const int t = threadIdx.x;
 #pragma unroll
     for (int e = t; e < GP_NB * GP_NB; e += 256) {
         const int i = e / GP_NB, j = e % GP_NB;
         M[i * GP_P + j] = i < b && j < b ? A[(long)(j0 + i) * n + j0 + j] : (i == j ? 1.0 : 0.0);
-        Iv[i * GP_P + j] = 0.0;
+        F[i * GP_P + j] = 0.0;
+    }
+    // This thread's lower-triangle elements (row-major order of the
+    // triangle: element e lies in row i with i (i + 1) / 2 <= e).
+    int oi[GP_OWN], oj[GP_OWN];
+#pragma unroll
+    for (int r = 0; r < GP_OWN; r++) {
+        const int e = t + 256 * r;
+        int i = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
+        while ((i + 1) * (i + 2) / 2 <= e)
+            i++;
+        while (i * (i + 1) / 2 > e)
+            i--;
+        oi[r] = e < GP_NB * (GP_NB + 1) / 2 ? i : -1;
+        oj[r] = e - i * (i + 1) / 2;
     }
     __syncthreads();
-    if (warp == 0)
-        chol32_inv(M, Iv, flag, lane);
-    __syncthreads();
-    double o[4];
-    const int oi = t / 8, oj = (t % 8) * 4;
-    // L21 = A21 Inv11^T.
-    mm32(M + 32 * GP_P, GP_P, 1, Iv, 1, GP_P, o, t);
-    __syncthreads();
+    for (int k = 0; k < GP_NB; k++) {
+        double d = M[k * GP_P + k];
+        if (!(d > 0.0)) {
+            if (t == 0)
+                *flag = 1;
+            d = 1.0;
+        }
+        const double piv = sqrt(d), rinv = 1.0 / piv;
+        if (t == k)
+            F[k * GP_P + k] = piv;
+        else if (t > k && t < GP_NB)
+            F[t * GP_P + k] = M[t * GP_P + k] * rinv;
 #pragma unroll
-    for (int q = 0; q < 4; q++)
-        M[(32 + oi) * GP_P + oj + q] = o[q];
-    __syncthreads();
-    // A22 -= L21 L21^T.
-    mm32(M + 32 * GP_P, GP_P, 1, M + 32 * GP_P, 1, GP_P, o, t);
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-        M[(32 + oi) * GP_P + 32 + oj + q] -= o[q];
-    __syncthreads();
-    if (warp == 0)
-        chol32_inv(M + 32 * GP_P + 32, Iv + 32 * GP_P + 32, flag, lane);
-    // T = L21 Inv11 (reads only L21 and Inv11, untouched by warp 0 now).
-    mm32(M + 32 * GP_P, GP_P, 1, Iv, GP_P, 1, o, t);
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-        T[oi * GP_P + oj + q] = o[q];
-    __syncthreads();
-    // Inv21 = -Inv22 T.
-    mm32(Iv + 32 * GP_P + 32, GP_P, 1, T, GP_P, 1, o, t);
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-        Iv[(32 + oi) * GP_P + oj + q] = -o[q];
+        for (int r = 0; r < GP_OWN; r++) {
+            const int i = oi[r], j = oj[r];
+            if (i >= 0 && j > k) {
+                const double li = M[i * GP_P + k] * rinv, lj = M[j * GP_P + k] * rinv;
+                M[i * GP_P + j] = fma(-li, lj, M[i * GP_P + j]);
+            }
+        }
+        __syncthreads();
+    }
+    // The inverse: column c by threads 4 c .. 4 c + 3; x_i = (delta_ic -
+    // sum_{c <= m < i} F_im x_m) / F_ii for i >= c, zero above.
+    {
+        // Every lane takes part in every shuffle (rows above a column's
+        // diagonal sum nothing and store zero).
+        const int c = t / 4, q = t % 4;
+        for (int i = 0; i < GP_NB; i++) {
+            double acc = 0.0;
+            for (int m = c + q; m < i; m += 4)
+                acc = fma(F[i * GP_P + m], X[m * GP_P + c], acc);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (q == 0)
+                X[i * GP_P + c] =
+                    i < c ? 0.0 : ((i == c ? 1.0 : 0.0) - acc) / F[i * GP_P + i];
+            __syncwarp();
+        }
+    }
     __syncthreads();
 #pragma unroll
     for (int e = t; e < GP_NB * GP_NB; e += 256) {
         const int i = e / GP_NB, j = e % GP_NB;
-        Linv[e] = Iv[i * GP_P + j];
+        Linv[e] = X[i * GP_P + j];
         if (i < b && j < b)
-            L[(long)(j0 + i) * n + j0 + j] = j <= i ? M[i * GP_P + j] : 0.0;
+            L[(long)(j0 + i) * n + j0 + j] = F[i * GP_P + j];
     }
 }
 
-constexpr size_t GP_POTRF_SMEM = (2 * GP_NB + 32) * GP_P * sizeof(double);
+constexpr size_t GP_POTRF_SMEM = 3 * GP_NB * GP_P * sizeof(double);
 
 // C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
 // sak], B(k, n) = B[k sbk + n sbn]; lower_only skips tiles and elements

@@ -121,7 +121,7 @@ extern "C" void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd
     g.c = DT_F32;
     cudaStream_t st = stream_of(o->ocl);
 
-    if (!gemm_packs_bf16(o->precision, M, N, K, transb)) {
+    if (!gemm_packs_bf16(o->precision, M, N, K)) {
         // The float32 tiles stage nothing.
         gemm_simt(st, g);
         launch_ok("ops_gemm_noalloc");
@@ -142,7 +142,10 @@ extern "C" void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd
     __nv_bfloat16 *a16 = (__nv_bfloat16 *)base;
     __nv_bfloat16 *b16 = (__nv_bfloat16 *)(base + a_bytes);
     pack_bf16_rows(st, (const float *)g.A, g.lda, g.sa0, g.sa1, nb, nb1, M, K, a16);
-    pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
+    if (transb)
+        pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
+    else
+        pack_bf16_cols(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, K, N, b16);
     if (!launch_ok("ops_gemm_noalloc pack"))
         return;
     GemmArgs h = g;
@@ -154,6 +157,7 @@ extern "C" void ops_gemm_noalloc(struct ops *o, int M, int N, int K, struct opnd
     h.ldb = K;
     h.sb0 = (long)N * K * nb1;
     h.sb1 = (long)N * K;
+    h.transb = 1;
     h.ab = DT_BF16;
     if (!gemm_tc(st, h, o->ocl->sm_count))
         gemm_simt(st, h);

@@ -86,6 +86,35 @@ void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1
                                                                rows, cols, dst);
 }
 
+
+// 32 x 32 tiles of a float32 rows x cols batch product, transposed into
+// bfloat16 (cols x rows); blockIdx.z is the batch.
+__global__ void to_bf16_t_kernel(const float *src, long ld, long s0, long s1, int nb1,
+                                 int rows, int cols, __nv_bfloat16 *dst)
+{
+    __shared__ float t[32][33];
+    const long b = blockIdx.z, b0 = b / nb1, b1 = b % nb1;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const int x = threadIdx.x % 32, y = threadIdx.x / 32;
+    const float *s = src + b0 * s0 + b1 * s1;
+    for (int r = y; r < 32; r += blockDim.x / 32)
+        t[r][x] = r0 + r < rows && c0 + x < cols ? s[(long)(r0 + r) * ld + c0 + x] : 0.0f;
+    __syncthreads();
+    __nv_bfloat16 *d = dst + b * (long)rows * cols;
+    for (int c = y; c < 32; c += blockDim.x / 32)
+        if (c0 + c < cols && r0 + x < rows)
+            d[(long)(c0 + c) * rows + r0 + x] = __float2bfloat16_rn(t[x][c]);
+}
+
+void pack_bf16_cols(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
+                    int nb1, int rows, int cols, __nv_bfloat16 *dst)
+{
+    if (nb <= 0 || rows <= 0 || cols <= 0)
+        return;
+    to_bf16_t_kernel<<<dim3(cdiv(cols, 32), cdiv(rows, 32), nb), 256, 0, st>>>(
+        src, ld, s0, s1, nb1, rows, cols, dst);
+}
+
 }  // namespace coreg
 
 extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
@@ -125,7 +154,7 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
     g.slope = slope;
     g.ab = DT_F32;
     g.c = DT_F32;
-    if (gemm_packs_bf16(o->precision, M, N, K, transb)) {
+    if (gemm_packs_bf16(o->precision, M, N, K)) {
         // Pack both operands to bfloat16 (row-major, K contiguous), then
         // the tensor-core tiles.
         size_t ea = (size_t)nb * M * K, eb = (size_t)nb * N * K;
@@ -144,7 +173,10 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
         {
             Prof p(o->ocl, "gemm_pack_bf16");
             pack_bf16_rows(st, (const float *)g.A, g.lda, g.sa0, g.sa1, nb, nb1, M, K, a16);
-            pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
+            if (transb)
+                pack_bf16_rows(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, N, K, b16);
+            else
+                pack_bf16_cols(st, (const float *)g.B, g.ldb, g.sb0, g.sb1, nb, nb1, K, N, b16);
             if (!launch_ok("gemm_pack_bf16"))
                 return;
         }
@@ -157,6 +189,7 @@ extern "C" void ops_gemm(struct ops *o, int M, int N, int K, struct opnd A,
         h.ldb = K;
         h.sb0 = (long)N * K * nb1;
         h.sb1 = (long)N * K;
+        h.transb = 1;
         h.ab = DT_BF16;
         gemm_run(o->ocl, h, "gemm_tc");
         return;

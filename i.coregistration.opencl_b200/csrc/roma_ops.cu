@@ -250,3 +250,29 @@ extern "C" void roma_local_corr_cl(struct ops *o, cl_mem f1, cl_mem f2, int C, i
                       fptr(flow), tm_out(fptr(out), side * side), 0);
     launch_ok("roma_local_corr_cl");
 }
+
+extern "C" int roma_gp_solve(struct ops *o, cl_mem K, int n, cl_mem F, int d, double noise,
+                             cl_mem X)
+{
+    if (!bufs_ok({K, F, X}, "roma_gp_solve"))
+        return -1;
+    if (n < 1 || d < 1) {
+        fail("roma_gp_solve: %d x %d", n, d);
+        return -1;
+    }
+    cl_mem work = ocl_alloc(o->ocl, gp_work_doubles(n, d) * sizeof(double), "GP work");
+    cl_mem flag = ocl_alloc(o->ocl, sizeof(int), "GP flag");
+    int f = 0;
+    if (!pending()) {
+        cudaStream_t st = stream_of(o->ocl);
+        cudaMemsetAsync(flag->ptr, 0, sizeof(int), st);
+        Prof p(o->ocl, "roma_gp_solve");
+        gp_solve_dev(st, fptr(K), n, fptr(F), d, noise, fptr(X), (double *)work->ptr,
+                     (int *)flag->ptr);
+        if (launch_ok("roma_gp_solve"))
+            ocl_read(o->ocl, flag, 0, &f, sizeof(int));
+    }
+    ocl_release(&work);
+    ocl_release(&flag);
+    return pending() ? -1 : f;
+}

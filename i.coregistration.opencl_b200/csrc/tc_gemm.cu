@@ -54,7 +54,8 @@ struct TcParams {
     int M, N, K;
     void *C;
     long ldc;
-    const float *bias;
+    const float *bias;    // per column
+    const float *bias_r;  // per row
     const void *R;
     float alpha;
     int act;
@@ -332,10 +333,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     // row's 32 values, then one TMA store of the warp's 32 x
                     // 32 block (clipped at the matrix or map edges).
                     const int col0 = tl.n0 + c0;
+                    const float br = p.bias_r && row < p.M ? __ldg(p.bias_r + row) : 0.0f;
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const float b = p.bias && col0 + j < p.N ? __ldg(p.bias + col0 + j) : 0.0f;
-                        v[j] = apply_act(p.alpha * v[j] + b, ACT >= 0 ? ACT : p.act, p.slope);
+                        v[j] = apply_act(p.alpha * v[j] + b + br, ACT >= 0 ? ACT : p.act,
+                                         p.slope);
                     }
                     if (R && row < p.M)
                         add_row(v, R + (long)row * p.ldc + col0, p.N - col0);
@@ -372,6 +375,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     if (grow < p.M && cok) {
                         const long idx = (long)grow * p.ldc + col;
                         float x = p.alpha * stage[rr * 32 + ((lane + rr) & 31)] + bias;
+                        if (p.bias_r)
+                            x += p.bias_r[grow];
                         x = apply_act(x, ACT >= 0 ? ACT : p.act, p.slope);
                         if (R)
                             x += ldf(R + idx);
@@ -461,6 +466,7 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     p.C = g.C;
     p.ldc = g.ldc;
     p.bias = g.biasrow ? nullptr : g.bias;
+    p.bias_r = g.biasrow ? g.bias : nullptr;
     p.R = g.R;
     p.alpha = g.alpha;
     p.act = g.act;
@@ -644,8 +650,6 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     const int ksz = g.cK ? g.cK : 3;
     if (g.amode == 2 ||
         (g.amode == 1 && ((ksz != 3 && ksz != 5) || g.cC % tc::BK || g.K != ksz * ksz * g.cC)))
-        return false;
-    if (g.biasrow && g.bias)
         return false;
     if (g.M < 64 || g.N < 1 || g.K < 16)
         return false;

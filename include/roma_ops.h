@@ -17,7 +17,8 @@
  *   roma_disp         replaces roma_kernels.cl:196
  *   roma_update       replaces roma_kernels.cl:213
  *   roma2_update      replaces roma_kernels.cl:232
- *   roma_dwconv5      replaces roma_kernels.cl:256 (C channels) */
+ *   roma_dwconv5      replaces roma_kernels.cl:256 (C channels)
+ *   roma_gp_solve     replaces roma.c:772-836 (the host solve, on the device) */
 
 #ifndef I_COREGISTRATION_B200_ROMA_OPS_H
 #define I_COREGISTRATION_B200_ROMA_OPS_H
@@ -45,6 +46,14 @@ void roma2_update(struct ops *o, cl_mem flow, cl_mem conf, cl_mem d, int n,
                   float W, float H);
 void roma_dwconv5(struct ops *o, cl_mem in, int C, int H, int W, cl_mem wt,
                   cl_mem bias, cl_mem out);
+
+/* The Gaussian process's solve, X = (K + noise I)^-1 F, for the n x n
+ * kernel matrix K (symmetric, row-major) and the n x d right-hand sides F,
+ * in double precision on the device (blocked Cholesky, then the two
+ * triangular solves); X may not alias F. Synchronous. Returns 0, or 1
+ * when K + noise I is not positive definite (the reference stops there
+ * with "kernel not positive definite"; X is then meaningless). */
+int roma_gp_solve(struct ops *o, cl_mem K, int n, cl_mem F, int d, double noise, cl_mem X);
 
 #ifdef __cplusplus
 }

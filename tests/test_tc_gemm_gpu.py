@@ -75,6 +75,41 @@ def test_tc_gemm_matches_rounded_oracle(dev16, shape):
     assert np.linalg.norm(got - want32) / np.linalg.norm(want32) <= 2e-2
 
 
+LAYOUTS = [
+    # M, N, K, transb, biasrow: B as K x N (a 1 x 1 convolution's input,
+    # an unfolded image) packed transposed; the bias per row (per output
+    # channel of ops_conv1x1) in the epilogue.
+    (256, 6400, 256, 0, 1),
+    (128, 1000, 576, 0, 1),
+    (96, 333, 72, 0, 0),
+    (300, 200, 96, 1, 1),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", LAYOUTS, ids=[f"{s[0]}x{s[1]}x{s[2]}_t{s[3]}_r{s[4]}"
+                                                for s in LAYOUTS])
+def test_tc_gemm_b_layouts_and_row_bias(dev16, shape):
+    M, N, K, transb, biasrow = shape
+    rng = np.random.default_rng(M + N + K)
+    a = rng.standard_normal((M, K), dtype=np.float32)
+    bt = (rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)).astype(np.float32)
+    b = bt if transb else np.ascontiguousarray(bt.T)
+    bias = rng.standard_normal(M if biasrow else N, dtype=np.float32)
+    A, B, Bi, Cb = dev16.upload(a), dev16.upload(b), dev16.upload(bias), dev16.zeros(M * N)
+    lib = dev16.lib
+    lib.ops_gemm(dev16.ops_p, M, N, K, Opnd(A.handle, 0, K, 0, 0),
+                 Opnd(B.handle, 0, K if transb else N, 0, 0), transb,
+                 Opnd(Cb.handle, 0, N, 0, 0), 1, 1, Bi.handle, biasrow, None, 0, 1.0, 2, 0.0)
+    got = Cb.read(count=M * N).reshape(M, N)
+    coreg.check(lib)
+    assert lib.coreg_tc_status() == 0
+    want = ref_gemm(bf16_round(a), bf16_round(bt), 1, M, N, K, bias=bias, biasrow=biasrow,
+                    a=2)[0]
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err
+
+
 CONVS = [
     # H, W, C, K (the VGG shapes at reduced size, ragged tiles)
     (40, 40, 64, 64),
