@@ -112,6 +112,9 @@ EXTRA_SIGNATURES.update({
     "match_add": (None, [C.POINTER(MatchList), C.POINTER(Match)]),
     "roma_sample_matches": (I, [P, P, P, P, I, I, I, I, I, F, P, P, C.POINTER(MatchList)]),
     "roma_dense_field": (None, [P, P, P, I, I, I, I, P, P, P, P, P, P]),
+    "roma_sample_matches_dev": (I, [C.POINTER(Ops), P, P, P, P, I, I, I, I, I, F, P, P,
+                                    C.POINTER(MatchList)]),
+    "roma_dense_field_dev": (None, [C.POINTER(Ops), P, P, P, I, I, I, I, P, P, P, P, P, P]),
     "eloftr_sample_matches": (I, [P, P, I, I, I, P, P, C.POINTER(MatchList)]),
     "roma_tiles_create": (P, [C.POINTER(C.c_int), I, I, I, C.c_char_p, C.c_char_p, C.c_char_p,
                               I, I, I, I]),

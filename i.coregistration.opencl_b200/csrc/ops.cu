@@ -1216,6 +1216,63 @@ void attention_l(cudaStream_t st, const void *Q, long ldq, const void *K,
 }
 }  // namespace coreg
 
+// OPS_BF16 contexts run unmasked self-sized attention (Nq = Nk) on the
+// tcgen05 attention kernels (head size 64 or 128): the float32 Q, K, V are
+// packed into one token-major bfloat16 qkv buffer, each head's d columns
+// zero-padded to 64 (d <= 64) or 128 (zeros add nothing to the scores and
+// give zero output columns), and the bfloat16 output is unpacked into O.
+// Both buffers come from o->scratch16.
+__global__ void attn_pack_k(const float *Q, long ldq, const float *K, long ldk, const float *V,
+                            long ldv, int N, int nh, int d, int dp, __nv_bfloat16 *qkv)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long dm = (long)nh * dp;
+    if (e >= (long)N * 3 * dm)
+        return;
+    const long r = e / (3 * dm), j = e % (3 * dm);
+    const int which = (int)(j / dm), h = (int)(j % dm / dp), c = (int)(j % dp);
+    const float *src = which == 0 ? Q + r * ldq : which == 1 ? K + r * ldk : V + r * ldv;
+    qkv[e] = __float2bfloat16_rn(c < d ? src[h * d + c] : 0.0f);
+}
+
+__global__ void attn_unpack_k(const __nv_bfloat16 *o16, int N, int nh, int d, int dp, float *O,
+                              long ldo)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (long)N * nh * d)
+        return;
+    const long r = e / ((long)nh * d);
+    const int h = (int)(e % ((long)nh * d) / d), c = (int)(e % d);
+    O[r * ldo + h * d + c] = __bfloat162float(o16[r * (long)nh * dp + h * dp + c]);
+}
+
+static bool attention_bf16_tc(struct ops *o, struct opnd Q, struct opnd K, struct opnd V,
+                              struct opnd O, int N, int nh, int d, float scale)
+{
+    const int dp = d <= 64 ? 64 : 128;
+    const long dm = (long)nh * dp;
+    const size_t qb = ((size_t)N * 3 * dm * 2 + 255) / 256 * 256;
+    const size_t bytes = qb + (size_t)N * dm * 2;
+    if (bytes > o->scratch16_bytes) {
+        ocl_release(&o->scratch16);
+        o->scratch16 = ocl_alloc(o->ocl, bytes, "attention operands");
+        o->scratch16_bytes = bytes;
+        if (pending())
+            return false;
+    }
+    __nv_bfloat16 *qkv = (__nv_bfloat16 *)o->scratch16->ptr;
+    __nv_bfloat16 *o16 = (__nv_bfloat16 *)((char *)o->scratch16->ptr + qb);
+    cudaStream_t st = stream_of(o->ocl);
+    attn_pack_k<<<cdiv((long)N * 3 * dm, 256), 256, 0, st>>>(
+        fptr(Q.buf, Q.off), Q.ld, fptr(K.buf, K.off), K.ld, fptr(V.buf, V.off), V.ld, N, nh, d,
+        dp, qkv);
+    if (!attention_tc(st, qkv, N, (int)dm, nh, o16, dm, scale, 1))
+        return false;
+    attn_unpack_k<<<cdiv((long)N * nh * d, 256), 256, 0, st>>>(o16, N, nh, d, dp,
+                                                              fptr(O.buf, O.off), O.ld);
+    return launch_ok("attention");
+}
+
 extern "C" void ops_attention(struct ops *o, struct opnd Q, struct opnd K,
                               struct opnd V, struct opnd O, int Nq, int Nk,
                               int nh, int d, float scale, cl_mem kmask)
@@ -1231,6 +1288,11 @@ extern "C" void ops_attention(struct ops *o, struct opnd Q, struct opnd K,
     if (Nq <= 0 || nh <= 0)
         return;
     Prof p(o->ocl, "attention");
+    if (o->precision == OPS_BF16 && Nq == Nk && !kmask &&
+        attention_bf16_tc(o, Q, K, V, O, Nq, nh, d, scale))
+        return;
+    if (pending())
+        return;
     attention_l(stream_of(o->ocl), fptr(Q.buf, Q.off), Q.ld, fptr(K.buf, K.off),
                 K.ld, fptr(V.buf, V.off), V.ld, fptr(O.buf, O.off), O.ld, Nq, Nk,
                 nh, d, scale, kmask ? (const unsigned char *)kmask->ptr : nullptr,

@@ -11,8 +11,9 @@
  *   matcher_roma_create replaces matcher_roma.c:207
  *
  * Additions without a counterpart in the reference's header: the host
- * stage on given results, which the matcher's match and field call
- * (roma_m_match matcher_roma.c:103-145, roma_m_field :150-178). */
+ * stage on given results (roma_m_match matcher_roma.c:103-145,
+ * roma_m_field :150-178), and the same on the device, which the matcher's
+ * match and field call. */
 
 #ifndef I_COREGISTRATION_B200_MATCHER_ROMA_H
 #define I_COREGISTRATION_B200_MATCHER_ROMA_H
@@ -48,6 +49,22 @@ void roma_dense_field(const float *flow, const float *cert, const float *sd,
                       int H, int W, int h, int w, const unsigned char *valid1,
                       const unsigned char *valid2, float *dx, float *dy,
                       float *certo, float *sdo);
+
+/* The same two stages on the device (no reference counterpart), from
+ * device-resident results (flow, cert, sd, bflow: device pointers such as
+ * roma_results_dev gives; sd and bflow may be NULL) on o's stream; valid1
+ * and valid2 are host masks (or NULL) and the outputs host memory, as
+ * above. The same matches and fields as roma_sample_matches and
+ * roma_dense_field, bit for bit; synchronous. The RoMa matcher's match
+ * and field use these. */
+int roma_sample_matches_dev(struct ops *o, const float *flow, const float *cert,
+                            const float *sd, const float *bflow, int H, int W, int h, int w,
+                            int spacing, float min_cert, const unsigned char *valid1,
+                            const unsigned char *valid2, struct match_list *out);
+void roma_dense_field_dev(struct ops *o, const float *flow, const float *cert,
+                          const float *sd, int H, int W, int h, int w,
+                          const unsigned char *valid1, const unsigned char *valid2,
+                          float *dx, float *dy, float *certo, float *sdo);
 
 #ifdef __cplusplus
 }

@@ -45,3 +45,41 @@ def test_attention_qkv(shape, prec):
     err = np.linalg.norm(got - want) / np.linalg.norm(want)
     assert err <= (1e-2 if prec == coreg.OPS_BF16 else 1e-5), err
     dev.close()
+
+
+GENERIC = [
+    # tokens, heads, head size: Efficient LoFTR's aggregated attention (8
+    # heads of 32, zero-padded to 64), head sizes 64 and 100 (padded to 128)
+    (400, 8, 32),
+    (130, 4, 64),
+    (90, 2, 100),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", GENERIC, ids=[f"{s[0]}h{s[1]}d{s[2]}" for s in GENERIC])
+def test_ops_attention_bf16_on_tensor_cores(shape):
+    """ops_attention (separate float32 Q, K, V of any leading dimension)
+    in a bfloat16 context: the tcgen05 kernels on the packed, zero-padded
+    heads, against the oracle on the rounded operands (1e-2, as above)."""
+    from coreg import Opnd
+
+    N, heads, d = shape
+    Dm = heads * d
+    rng = np.random.default_rng(N * heads + d)
+    q, k, v = (rng.standard_normal((N, Dm + 8), dtype=np.float32) for _ in range(3))
+    dev = coreg.Device(0, precision=coreg.OPS_BF16)
+    Q, K, V = dev.upload(q), dev.upload(k), dev.upload(v)
+    O = dev.zeros(N * (Dm + 4))
+    scale = float(1.0 / np.sqrt(d))
+    dev.lib.ops_attention(dev.ops_p, Opnd(Q.handle, 0, Dm + 8, 0, 0), Opnd(K.handle, 0, Dm + 8, 0, 0),
+                          Opnd(V.handle, 0, Dm + 8, 0, 0), Opnd(O.handle, 0, Dm + 4, 0, 0), N, N,
+                          heads, d, scale, None)
+    got = O.read(count=N * (Dm + 4)).reshape(N, Dm + 4)[:, :Dm]
+    coreg.check(dev.lib)
+    assert dev.lib.coreg_tc_status() == 0
+    want = ref_attention(bf16_round(q[:, :Dm]), bf16_round(k[:, :Dm]), bf16_round(v[:, :Dm]), N,
+                         N, heads, d, np.float32(scale))
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-2, err
+    dev.close()
