@@ -73,6 +73,24 @@ __global__ void to_bf16_kernel(const float *src, long ld, long s0, long s1,
     }
 }
 
+// The same, eight columns per thread (two 16-byte loads, one 16-byte
+// store) for rows whose starts are 16-byte aligned and cols a multiple of 8.
+__global__ void to_bf16_v8_kernel(const float *src, long ld, long s0, long s1, int nb1,
+                                  long nrows, int rows, int cols, __nv_bfloat16 *dst)
+{
+    const int c = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (c >= cols)
+        return;
+    for (long br = blockIdx.y; br < nrows; br += gridDim.y) {
+        const long b = br / rows, r = br % rows, b0 = b / nb1, b1 = b % nb1;
+        const float4 *p = (const float4 *)(src + b0 * s0 + b1 * s1 + r * ld + c);
+        const float4 x = p[0], y = p[1];
+        __nv_bfloat162 h[4] = {__floats2bfloat162_rn(x.x, x.y), __floats2bfloat162_rn(x.z, x.w),
+                               __floats2bfloat162_rn(y.x, y.y), __floats2bfloat162_rn(y.z, y.w)};
+        *(uint4 *)(dst + br * (long)cols + c) = *(const uint4 *)h;
+    }
+}
+
 namespace coreg {
 
 void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1, int nb,
@@ -82,6 +100,12 @@ void pack_bf16_rows(cudaStream_t st, const float *src, long ld, long s0, long s1
     if (nrows <= 0 || cols <= 0)
         return;
     const unsigned gy = (unsigned)(nrows < 65535 ? nrows : 65535);
+    if (cols % 8 == 0 && ld % 4 == 0 && s0 % 4 == 0 && s1 % 4 == 0 &&
+        ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+        to_bf16_v8_kernel<<<dim3(cdiv(cols / 8, 128), gy), 128, 0, st>>>(
+            src, ld, s0, s1, nb1, nrows, rows, cols, dst);
+        return;
+    }
     to_bf16_kernel<<<dim3(cdiv(cols, 256), gy), 256, 0, st>>>(src, ld, s0, s1, nb1, nrows,
                                                                rows, cols, dst);
 }
@@ -811,26 +835,64 @@ extern "C" void ops_unfold(struct ops *o, cl_mem in, int C, int H, int W,
 // ------------------------------------------------------- channel statistics
 
 // Mean and 1 / sqrt(biased variance + eps) of each channel (ops.cl:453-492
-// semantics: two passes over the plane).
-__global__ void chan_stats_kernel(const float *x, int HW, float eps,
-                                  float *mean, float *rstd)
+// semantics: two passes over the plane, the mean first, then the sum of
+// squared deviations from it). Each pass splits every channel into S
+// segments summed by their own blocks (vector loads where the plane
+// allows), then one warp per channel adds the S partial sums in a fixed
+// order: deterministic, and the whole device reads the planes.
+__global__ void __launch_bounds__(256)
+chan_partial_k(const float *x, long HW, long seg, const float *mean, float *part)
 {
     __shared__ float red[32];
-    const float *p = x + (size_t)blockIdx.x * HW;
-    float s = 0.0f;
-
-    for (int i = threadIdx.x; i < HW; i += blockDim.x)
-        s += p[i];
-    const float m = block_sum(s, red) / HW;
-    s = 0.0f;
-    for (int i = threadIdx.x; i < HW; i += blockDim.x) {
-        const float d = p[i] - m;
-        s = fmaf(d, d, s);
+    const int c = blockIdx.y, S = gridDim.x;
+    const long b0 = (long)blockIdx.x * seg, b1 = b0 + seg < HW ? b0 + seg : HW;
+    const float *p = x + (size_t)c * HW;
+    const float m = mean ? mean[c] : 0.0f;
+    float s0 = 0.0f, s1 = 0.0f;
+    if ((((uintptr_t)(p + b0)) & 15) == 0 && ((b1 - b0) & 3) == 0) {
+        const float4 *q = (const float4 *)(p + b0);
+        const long n4 = (b1 - b0) / 4;
+        for (long i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = q[i];
+            if (mean) {
+                const float d0 = v.x - m, d1 = v.y - m, d2 = v.z - m, d3 = v.w - m;
+                s0 = fmaf(d0, d0, s0);
+                s1 = fmaf(d1, d1, s1);
+                s0 = fmaf(d2, d2, s0);
+                s1 = fmaf(d3, d3, s1);
+            }
+            else {
+                s0 += v.x + v.z;
+                s1 += v.y + v.w;
+            }
+        }
     }
-    const float v = block_sum(s, red) / HW;
+    else
+        for (long i = b0 + threadIdx.x; i < b1; i += blockDim.x) {
+            const float v = p[i];
+            if (mean)
+                s0 = fmaf(v - m, v - m, s0);
+            else
+                s0 += v;
+        }
+    const float t = block_sum(s0 + s1, red);
+    if (threadIdx.x == 0)
+        part[(size_t)c * S + blockIdx.x] = t;
+}
+
+__global__ void chan_final_k(const float *part, int S, long HW, float eps, float *mean,
+                             float *rstd)
+{
+    const int c = blockIdx.x;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < S; i += 32)
+        s += part[(size_t)c * S + i];
+    s = warp_sum(s);
     if (threadIdx.x == 0) {
-        mean[blockIdx.x] = m;
-        rstd[blockIdx.x] = rsqrtf(v + eps);
+        if (rstd)
+            rstd[c] = rsqrtf(s / HW + eps);
+        else
+            mean[c] = s / HW;
     }
 }
 
@@ -840,9 +902,27 @@ extern "C" void ops_chan_stats(struct ops *o, cl_mem x, int C, int HW, float eps
     if (pending() || !need(x, "ops_chan_stats x") || !need(mean, "mean") ||
         !need(rstd, "rstd") || C <= 0)
         return;
+    // Segments: about four blocks per SM over all channels, at least 2048
+    // elements each.
+    long seg = ((long)HW * C + 4L * 148 - 1) / (4L * 148);
+    seg = seg < 2048 ? 2048 : seg;
+    seg = (seg + 3) / 4 * 4;
+    const int S = (int)((HW + seg - 1) / seg);
+    const size_t bytes = (size_t)C * S * sizeof(float);
+    if (bytes > o->scratch_bytes) {
+        ocl_release(&o->scratch);
+        o->scratch = ocl_alloc(o->ocl, bytes, "channel statistics");
+        o->scratch_bytes = bytes;
+        if (pending())
+            return;
+    }
+    cudaStream_t st = stream_of(o->ocl);
+    float *part = fptr(o->scratch);
     Prof p(o->ocl, "chan_stats");
-    chan_stats_kernel<<<C, 512, 0, stream_of(o->ocl)>>>(fptr(x), HW, eps,
-                                                        fptr(mean), fptr(rstd));
+    chan_partial_k<<<dim3(S, C), 256, 0, st>>>(fptr(x), HW, seg, nullptr, part);
+    chan_final_k<<<C, 32, 0, st>>>(part, S, HW, eps, fptr(mean), nullptr);
+    chan_partial_k<<<dim3(S, C), 256, 0, st>>>(fptr(x), HW, seg, fptr(mean), part);
+    chan_final_k<<<C, 32, 0, st>>>(part, S, HW, eps, nullptr, fptr(rstd));
     launch_ok("chan_stats");
 }
 

@@ -37,6 +37,7 @@
 // frees its tensor memory and returns.
 
 #include <mutex>
+#include <stdlib.h>
 #include <string.h>
 
 #include "tc_common.cuh"
@@ -66,6 +67,12 @@ struct TcParams {
     // is TW x TH output pixels (TW TH = 128), k-block kb = (tap, 64-channel
     // chunk), tap = ky ksz + kx.
     int conv, cH, cW, cC, TW, TH, tiles_x, tiles_y, ksz;
+    // Tap reuse (3 x 3 only): a stage is one (64-channel chunk, column tap
+    // dx) with one A box of TW x (TH + 2) pixels (tensor map tma_a3) and the
+    // three weight tiles of the row taps dy = 0..2; the A operand of tap (dy,
+    // dx) is that box from row dy TW on. reuse = the number of such stages
+    // that fit the shared memory (0: off), rsb its bytes, rab its A bytes.
+    int reuse, rsb, rab;
     // Epilogue through TMA stores (output tensor map tma_c); else one
     // coalesced store per row.
     int tma_out;
@@ -205,13 +212,19 @@ template <int BN, int STAGES, int ACT, typename TC>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                const __grid_constant__ CUtensorMap tma_b,
-               const __grid_constant__ CUtensorMap tma_c, TcParams p)
+               const __grid_constant__ CUtensorMap tma_c,
+               const __grid_constant__ CUtensorMap tma_a3, TcParams p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     Smem<BN, STAGES> &s = *reinterpret_cast<Smem<BN, STAGES> *>(
         smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u));
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int nk = (p.K + BK - 1) / BK;
+    // Stages per tile and stage slots: k-blocks, or (chunk, dx) pairs with
+    // tap reuse.
+    const int nst = p.reuse ? 3 * (p.cC / BK) : nk;
+    const int slots = p.reuse ? p.reuse : STAGES;
+    unsigned char *const rbase = reinterpret_cast<unsigned char *>(s.a);
     const int tiles_m = p.conv ? p.tiles_x * p.tiles_y : (p.M + BM - 1) / BM;
     const int ntiles = tiles_m * ((p.N + BN - 1) / BN);
 
@@ -235,20 +248,33 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t bytes = (BM + BN) * BK * 2;
+            const uint32_t bytes =
+                p.reuse ? (uint32_t)(p.rab + 3 * BN * BK * 2) : (uint32_t)((BM + BN) * BK * 2);
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const Tile tl = tile_of<BN>(p, t, tiles_m);
-                const int k_off = k_rotation(t, tiles_m, nk);
-                for (int kk = 0; kk < nk; kk++, it++) {
-                    const int kb = kk + k_off < nk ? kk + k_off : kk + k_off - nk;
-                    const int st = it % STAGES;
-                    if (it >= STAGES && !mbar_wait(&s.empty[st], ((it / STAGES) - 1) & 1, 1)) {
+                const int k_off = k_rotation(t, tiles_m, nst);
+                for (int kk = 0; kk < nst; kk++, it++) {
+                    const int kb = kk + k_off < nst ? kk + k_off : kk + k_off - nst;
+                    const int st = it % slots;
+                    if (it >= slots && !mbar_wait(&s.empty[st], ((it / slots) - 1) & 1, 1)) {
                         ok = false;
                         break;
                     }
                     mbar_expect_tx(&s.full[st], bytes);
+                    if (p.reuse) {
+                        // Stage kb = (chunk c, column tap dx): the A box one
+                        // row above the tile, then the weights of taps (dy,
+                        // dx), columns (dy 3 + dx) C + 64 c.
+                        unsigned char *sa = rbase + (size_t)st * p.rsb;
+                        const int c = kb / 3, dx = kb % 3;
+                        tma_load_3d(sa, &tma_a3, &s.full[st], c * BK, tl.cx0 + dx - 1, tl.cy0 - 1);
+                        for (int dy = 0; dy < 3; dy++)
+                            tma_load_2d(sa + p.rab + dy * BN * BK * 2, &tma_b, &s.full[st],
+                                        (dy * 3 + dx) * p.cC + c * BK, tl.n0);
+                        continue;
+                    }
                     if (p.conv) {
                         const int chunks = p.cC / BK, tap = kb / chunks;
                         const int c0 = (kb % chunks) * BK, pad = p.ksz / 2;
@@ -274,13 +300,29 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     break;
                 fence_after();
                 const uint32_t acc = tmem + (uint32_t)(buf * acc_cols<BN>());
-                for (int kk = 0; kk < nk; kk++, it++) {
-                    const int st = it % STAGES;
+                for (int kk = 0; kk < nst; kk++, it++) {
+                    const int st = it % slots;
                     // TMA completion through the mbarrier orders the tile
                     // for the tensor cores; no tcgen05 fence is needed here.
-                    if (!mbar_wait(&s.full[st], (it / STAGES) & 1, 2)) {
+                    if (!mbar_wait(&s.full[st], (it / slots) & 1, 2)) {
                         ok = false;
                         break;
+                    }
+                    if (p.reuse) {
+                        // Taps (dy, dx) for dy = 0..2: A from row dy TW of
+                        // the box (a multiple of 8 rows: 1024-byte aligned).
+                        const uint32_t sa = su32(rbase + (size_t)st * p.rsb);
+                        for (int dy = 0; dy < 3; dy++) {
+                            const uint64_t da = sw128_desc(sa + (uint32_t)(dy * p.TW * 128));
+                            const uint64_t db =
+                                sw128_desc(sa + (uint32_t)(p.rab + dy * BN * BK * 2));
+#pragma unroll
+                            for (int k = 0; k < BK / 16; k++)
+                                mma_bf16(acc, da + 2 * k, db + 2 * k, idesc,
+                                         (kk > 0 || dy > 0 || k > 0) ? 1u : 0u);
+                        }
+                        mma_commit(&s.empty[st]);
+                        continue;
                     }
                     const uint64_t da = sw128_desc(su32(s.a[st]));
                     const uint64_t db = sw128_desc(su32(s.b[st]));
@@ -423,24 +465,37 @@ int conv_tile_width(int H, int W)
 
 template <int BN, int STAGES, int ACT, typename TC>
 bool run_tc(cudaStream_t st, int grid, const CUtensorMap &ma, const CUtensorMap &mb,
-            const CUtensorMap &mc, const TcParams &p)
+            const CUtensorMap &mc, const CUtensorMap &ma3, const TcParams &p)
 {
     const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
     static unsigned done = 0;
     if (!smem_opt_in((const void *)tc_gemm_kernel<BN, STAGES, ACT, TC>, smem, &done))
         return false;
-    tc_gemm_kernel<BN, STAGES, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, mc, p);
+    tc_gemm_kernel<BN, STAGES, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, mc, ma3, p);
     return true;
 }
 
 bool make_map_c(CUtensorMap *map, void *base, int es, const TcParams &p, long ldc);
 
+// COREG_TC_TAP_REUSE=0 in the environment turns tap reuse off (the plain
+// convolution mode, one A box per tap), for comparisons.
+bool tap_reuse_off()
+{
+    static int off = -1;
+    if (off < 0) {
+        const char *e = getenv("COREG_TC_TAP_REUSE");
+        off = e && e[0] == '0';
+    }
+    return off != 0;
+}
+
 template <int BN, int STAGES>
 bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
-    CUtensorMap ma, mb, mc;
+    CUtensorMap ma, mb, mc, ma3;
     TcParams p;
     memset(&p, 0, sizeof(p));
+    memset(&ma3, 0, sizeof(ma3));
     long tiles_m = cdiv(g.M, BM);
     if (g.amode == 1) {
         p.conv = 1;
@@ -455,6 +510,17 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         tiles_m = (long)p.tiles_x * p.tiles_y;
         if (!make_map_conv(&ma, g.A, g.cH, g.cW, g.cC, p.TW, p.TH))
             return false;
+        // Tap reuse where two of its stages fit the stage memory and the
+        // shifted A operands stay 1024-byte aligned (TW a multiple of 8).
+        const int rab = (p.TW * (p.TH + 2) * BK * 2 + 1023) / 1024 * 1024;
+        const int rsb = rab + 3 * BN * BK * 2;
+        const int total = STAGES * (BM + BN) * BK * 2;
+        if (p.ksz == 3 && p.TW % 8 == 0 && p.TH + 2 <= 256 && total / rsb >= 2 &&
+            !tap_reuse_off() && make_map_conv(&ma3, g.A, g.cH, g.cW, g.cC, p.TW, p.TH + 2)) {
+            p.reuse = total / rsb;
+            p.rsb = rsb;
+            p.rab = rab;
+        }
     }
     else if (!make_map_2d(&ma, g.A, g.M, g.K, g.lda, BM))
         return false;
@@ -483,16 +549,16 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     const int grid = (int)(ntiles < sm_count ? ntiles : sm_count);
     if (p.c_bf16) {
         if (g.act == ACTF_NONE)
-            return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, mc, p);
+            return run_tc<BN, STAGES, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, mc, ma3, p);
         if (g.act == ACTF_GELU)
-            return run_tc<BN, STAGES, ACTF_GELU, __nv_bfloat16>(st, grid, ma, mb, mc, p);
+            return run_tc<BN, STAGES, ACTF_GELU, __nv_bfloat16>(st, grid, ma, mb, mc, ma3, p);
         if (g.act == ACTF_RELU)
-            return run_tc<BN, STAGES, ACTF_RELU, __nv_bfloat16>(st, grid, ma, mb, mc, p);
-        return run_tc<BN, STAGES, -1, __nv_bfloat16>(st, grid, ma, mb, mc, p);
+            return run_tc<BN, STAGES, ACTF_RELU, __nv_bfloat16>(st, grid, ma, mb, mc, ma3, p);
+        return run_tc<BN, STAGES, -1, __nv_bfloat16>(st, grid, ma, mb, mc, ma3, p);
     }
     if (g.act == ACTF_NONE)
-        return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, mc, p);
-    return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, mc, p);
+        return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, mc, ma3, p);
+    return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, mc, ma3, p);
 }
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,

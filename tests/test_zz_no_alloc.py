@@ -147,24 +147,30 @@ def test_noalloc_fp32_matches_ops_gemm_and_oracle():
 
 
 @pytest.mark.gpu
-def test_noalloc_b_as_k_by_n_matches_ops_gemm(dev16):
+def test_noalloc_b_as_k_by_n_matches_ops_gemm():
     """B given as K x N (transb 0): both entry points pack it transposed
     and agree; the context's staging buffer stays unallocated."""
-    lib = dev16.lib
+    # A context of its own, whose staging buffer no ops_gemm call has grown.
+    dev = coreg.Device(0, precision=coreg.OPS_BF16)
+    lib = dev.lib
     M, N, K = 128, 300, 64
     rng = np.random.default_rng(11)
     a = rng.standard_normal((M, K), dtype=np.float32)
     b = (rng.standard_normal((K, N), dtype=np.float32) / np.sqrt(K)).astype(np.float32)
     bias = rng.standard_normal(M, dtype=np.float32)
     outs = []
-    for fn in (lib.ops_gemm_noalloc, lib.ops_gemm_noalloc, lib.ops_gemm):
-        A, B, Bi, Cb = dev16.upload(a), dev16.upload(b), dev16.upload(bias), dev16.zeros(M * N)
-        fn(dev16.ops_p, M, N, K, Opnd(handle(A), 0, K, 0, 0), Opnd(handle(B), 0, N, 0, 0), 0,
-           Opnd(handle(Cb), 0, N, 0, 0), 1, 1, handle(Bi), 1, None, 0, 1.0, coreg.ACT_NONE, 0.0)
-        coreg.check(lib)
-        outs.append(Cb.read(count=M * N))
-        if len(outs) == 2:
-            assert dev16.ops.scratch16_bytes == 0
+    try:
+        for fn in (lib.ops_gemm_noalloc, lib.ops_gemm_noalloc, lib.ops_gemm):
+            A, B, Bi, Cb = dev.upload(a), dev.upload(b), dev.upload(bias), dev.zeros(M * N)
+            fn(dev.ops_p, M, N, K, Opnd(handle(A), 0, K, 0, 0), Opnd(handle(B), 0, N, 0, 0), 0,
+               Opnd(handle(Cb), 0, N, 0, 0), 1, 1, handle(Bi), 1, None, 0, 1.0, coreg.ACT_NONE,
+               0.0)
+            coreg.check(lib)
+            outs.append(Cb.read(count=M * N))
+            if len(outs) == 2:
+                assert dev.ops.scratch16_bytes == 0
+    finally:
+        dev.close()
     assert rel_l2(outs[0], outs[2]) <= TOL_SAME and rel_l2(outs[1], outs[2]) <= TOL_SAME
     ref = ops_ref.gemm(bf16(a), bf16(b), 0, M, N, K, bias=bias, biasrow=1)
     assert rel_l2(outs[0], ref) <= TOL_ORACLE
