@@ -601,6 +601,7 @@ def gpu_arm(args, rank, world, local):
             "roofline": roof,
             "path_tflops": flops_pair / (ms_max / (args.steps * B) / 1000.0) / 1e12,
             "time_shares": {k: round(v, 4) for k, v in shares},
+            "profiled_tile_ms": round(tot_ms, 3),
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }

@@ -108,7 +108,11 @@ def test_disk_config5_full_size(precision):
         assert (~sure).mean() < 0.01
         assert np.array_equal(nn12[sure], w12[sure])
         assert np.array_equal(nn21[col_gap > 1e-5], w21[col_gap > 1e-5])
-        assert np.max(np.abs(score - wscore) / np.maximum(np.abs(wscore), 1e-6)) < 1e-4
+        # The ratio of two float32 distances |a|^2 + |b|^2 - 2 a.b of unit
+        # vectors: each carries an absolute error of about 1e-6 from the
+        # cancellation, so near matches (distances of a few 1e-2) see
+        # relative errors up to a few 1e-4.
+        assert np.max(np.abs(score - wscore) / np.maximum(np.abs(wscore), 1e-6)) < 1e-3
     finally:
         d.close()
         dev.close()
