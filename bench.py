@@ -52,6 +52,8 @@ REF_BUDGET_S = 420.0
 # (backbone 287, transformer 87, coarse matching 42, fusion 190 GFLOP) and
 # DISK on two 1024 x 1024 images plus the 2048 x 2048 x 128 distance GEMM.
 ELOFTR_FLOP = 605e9
+# RoMa v1 at 864 with the coarse pass at 560 (about 5.25 TFLOP per pair).
+ROMA_V1_FLOP = 5.25e12
 DISK_FLOP = 2 * 675e9 + 2 * 2048 * 2048 * 128
 CACHE = Path(os.environ.get("COREG_CACHE", "/tmp/coreg_cache"))
 
@@ -427,16 +429,37 @@ def fp32_mode(local, tiles, weights, count=8, S=2):
             "pipelines_per_gpu": S}
 
 
-def secondary(local, peak_tflops, pairs_eloftr=16, pairs_disk=4):
-    """Configs 2 and 5 through their public entry points (synchronous host
-    calls, host images in, host results out), wall clock per pair after one
-    warm-up pair, bfloat16 contexts."""
+def secondary(local, peak_tflops, tiles, weights, S, pairs_eloftr=16, pairs_disk=4, batches=3):
+    """Configs 2, 3 and 5 through their public entry points (host images
+    in, host results out), wall clock per pair after a warm-up, bfloat16
+    contexts: Efficient LoFTR and DISK with their synchronous calls, RoMa v1
+    through the tile queue (S pipelines), batches of 8 pairs."""
     import coreg
     from coreg import synth
     from coreg.disk import Disk, nearest
     from coreg.eloftr import Eloftr
+    from coreg.roma import RomaTiles
 
     out = {}
+    q = RomaTiles([local], S, coreg.OPS_BF16, weights[0], weights[1], None, H=H, W=W,
+                  coarse=COARSE)
+
+    def get(i, a, b):
+        a[...] = tiles[i % len(tiles)][0]
+        b[...] = tiles[i % len(tiles)][1]
+
+    try:
+        q.run(8, get, lambda *x: None)
+        t = time.perf_counter()
+        n = sum(q.run(8, get, lambda *x: None) for _ in range(batches))
+        sec = (time.perf_counter() - t) / n
+    finally:
+        q.close()
+    out["roma_v1"] = {"value": 1.0 / sec, "unit": "tile_pairs/s",
+                      "workload": "RoMa v1 (roma_outdoor), batches of 8 RGB 864x864 tile pairs, "
+                                  "coarse 560 (BASELINE configs[2]), through roma_tiles_run",
+                      "tflops": ROMA_V1_FLOP / sec / 1e12,
+                      "tensor_frac": ROMA_V1_FLOP / sec / 1e12 / peak_tflops}
     rng = np.random.default_rng(2)
     side = 640
     g0 = (synth.band_limited(rng, side, side, 3.0) / 255.0).astype(np.float32)
@@ -575,7 +598,7 @@ def gpu_arm(args, rank, world, local):
     if rank == 0 and world == 1 and not args.no_extra:
         if prec == coreg.OPS_BF16:
             extra["fp32_mode"] = fp32_mode(local, tiles, weights)
-        extra["secondary"] = secondary(local, bf16)
+        extra["secondary"] = secondary(local, bf16, tiles, weights, S)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
