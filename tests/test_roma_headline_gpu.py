@@ -100,8 +100,10 @@ def first_argmax(L):
 def final_report(got, want):
     flow, cert, sd = got
     d = warp_px(flow, want[0], H, W)
+    ce = np.abs(cert - want[1])
     rep = dict(px_mean=float(d.mean()), px_p99=float(np.percentile(d, 99)),
-               cert_max=float(np.abs(cert - want[1]).max()), sd_rel=0.0, sd_finite=1.0)
+               cert_max=float(ce.max()), cert_p9999=float(np.quantile(ce, 0.9999)),
+               cert_over=int((ce > 1e-2).sum()), sd_rel=0.0, sd_finite=1.0)
     if sd is not None:
         ok = np.isfinite(want[2]) & np.isfinite(sd)
         rep["sd_rel"] = rel_l2(sd[ok], want[2][ok])
