@@ -1,6 +1,6 @@
 // SPDX-License-Identifier: Unlicense
 //
-// The Gaussian-process solve of RoMa on the device, in float32:
+// The Gaussian-process solve of RoMa on the device, in double precision:
 // X = (K + noise I)^-1 F for the n x n kernel matrix K (float, symmetric)
 // and the n x d basis F, by a blocked right-looking Cholesky factorization
 // L L^T = K + noise I and the two triangular solves L Z = F, L^T X = Z.
@@ -9,7 +9,8 @@
 // (roma.c:885-888) disappears.
 //
 // Blocks of NB = 64. One CTA of 256 threads factors each diagonal block
-// and inverts it (Linv_j), so that every other step is a float32 GEMM. The
+// and inverts it (Linv_j), so that every other step is a double-precision
+// GEMM. The
 // working matrix A, the factor L and the right-hand sides F, Z, X live in
 // separate buffers, so no step multiplies in place:
 //   step j     L_jj, Linv_j           from A_jj
@@ -28,25 +29,17 @@ namespace coreg {
 
 #define GP_NB 64
 
-// The solve's element type. Float32: the relative difference from the
-// reference's double solve stays near 1e-7 on the GP's kernel matrices
-// (condition numbers up to a few thousand; tests/test_gp_solve_gpu.py),
-// two orders below the stage's float32 bound, at twice the FMA rate of
-// double and with the single-precision square root and reciprocal on the
-// factorization's serial path.
-typedef float gpt;
-
-// A = K + noise I.
-__global__ void gp_init_k(const float *K, int n, gpt noise, gpt *A)
+// A = K + noise I in double.
+__global__ void gp_init_k(const float *K, int n, double noise, double *A)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= (long)n * n)
         return;
     const long i = e / n, j = e % n;
-    A[e] = (gpt)K[e] + (i == j ? noise : (gpt)0);
+    A[e] = (double)K[e] + (i == j ? noise : 0.0);
 }
 
-constexpr int GP_P = GP_NB + 1;  // shared-memory pitch (elements)
+constexpr int GP_P = GP_NB + 1;  // shared-memory pitch (doubles)
 // Elements of the 64 x 64 lower triangle each of the 256 threads owns.
 constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + 255) / 256;
 
@@ -62,12 +55,12 @@ constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + 255) / 256;
 // non-positive pivot sets *flag (the factor is then meaningless, as the
 // reference's stop says).
 __global__ void __launch_bounds__(256)
-gp_potrf_inv_k(const gpt *A, gpt *L, int n, int j0, int b, gpt *Linv, int *flag)
+gp_potrf_inv_k(const double *A, double *L, int n, int j0, int b, double *Linv, int *flag)
 {
-    extern __shared__ gpt gp_smem[];
-    gpt *M = gp_smem;                  // 64 x GP_P: the block, updated
-    gpt *F = gp_smem + GP_NB * GP_P;   // 64 x GP_P: the factor
-    gpt *X = F + GP_NB * GP_P;         // 64 x GP_P: the inverse
+    extern __shared__ double gp_smem[];
+    double *M = gp_smem;                  // 64 x GP_P: the block, updated
+    double *F = gp_smem + GP_NB * GP_P;   // 64 x GP_P: the factor
+    double *X = F + GP_NB * GP_P;         // 64 x GP_P: the inverse
     const int t = threadIdx.x;
 #pragma unroll
     for (int e = t; e < GP_NB * GP_NB; e += 256) {
@@ -91,13 +84,13 @@ gp_potrf_inv_k(const gpt *A, gpt *L, int n, int j0, int b, gpt *Linv, int *flag)
     }
     __syncthreads();
     for (int k = 0; k < GP_NB; k++) {
-        gpt d = M[k * GP_P + k];
+        double d = M[k * GP_P + k];
         if (!(d > 0.0)) {
             if (t == 0)
                 *flag = 1;
             d = 1.0;
         }
-        const gpt piv = sqrtf(d), rinv = 1.0f / piv;
+        const double piv = sqrt(d), rinv = 1.0 / piv;
         if (t == k)
             F[k * GP_P + k] = piv;
         else if (t > k && t < GP_NB)
@@ -106,7 +99,7 @@ gp_potrf_inv_k(const gpt *A, gpt *L, int n, int j0, int b, gpt *Linv, int *flag)
         for (int r = 0; r < GP_OWN; r++) {
             const int i = oi[r], j = oj[r];
             if (i >= 0 && j > k) {
-                const gpt li = M[i * GP_P + k] * rinv, lj = M[j * GP_P + k] * rinv;
+                const double li = M[i * GP_P + k] * rinv, lj = M[j * GP_P + k] * rinv;
                 M[i * GP_P + j] = fma(-li, lj, M[i * GP_P + j]);
             }
         }
@@ -119,7 +112,7 @@ gp_potrf_inv_k(const gpt *A, gpt *L, int n, int j0, int b, gpt *Linv, int *flag)
         // diagonal sum nothing and store zero).
         const int c = t / 4, q = t % 4;
         for (int i = 0; i < GP_NB; i++) {
-            gpt acc = 0.0;
+            double acc = 0.0;
             for (int m = c + q; m < i; m += 4)
                 acc = fma(F[i * GP_P + m], X[m * GP_P + c], acc);
             acc += __shfl_xor_sync(0xffffffffu, acc, 1);
@@ -140,18 +133,18 @@ gp_potrf_inv_k(const gpt *A, gpt *L, int n, int j0, int b, gpt *Linv, int *flag)
     }
 }
 
-constexpr size_t GP_POTRF_SMEM = 3 * GP_NB * GP_P * sizeof(gpt);
+constexpr size_t GP_POTRF_SMEM = 3 * GP_NB * GP_P * sizeof(double);
 
 // C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
 // sak], B(k, n) = B[k sbk + n sbn]; lower_only skips tiles and elements
 // above the diagonal.
 struct DgProb {
     int M, N, K;
-    const gpt *A;
+    const double *A;
     long sam, sak;
-    const gpt *B;
+    const double *B;
     long sbk, sbn;
-    gpt *C;
+    double *C;
     long ldc;
     int sub, lower_only;
 };
@@ -167,29 +160,28 @@ struct DgBatch {
 // blocked Cholesky's products have K <= 64, so one panel and two barriers
 // per tile.
 constexpr int DG_T = 64, DG_K = 64;
-constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(gpt);
+constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(double);
 
-__device__ __forceinline__ void cp_async_el(gpt *dst, const gpt *src, bool in)
+__device__ __forceinline__ void cp_async8(double *dst, const double *src, bool in)
 {
-    static_assert(sizeof(gpt) == 4, "cp.async of one float");
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(
                      (unsigned)__cvta_generic_to_shared(dst)),
-                 "l"(src), "r"(in ? 4 : 0)
+                 "l"(src), "r"(in ? 8 : 0)
                  : "memory");
 }
 
 __global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
 {
-    extern __shared__ gpt dg_smem[];
+    extern __shared__ double dg_smem[];
     const DgProb &q = batch.p[blockIdx.z];
-    gpt(*As)[DG_T + 1] = reinterpret_cast<gpt(*)[DG_T + 1]>(dg_smem);
-    gpt(*Bs)[DG_T + 1] = reinterpret_cast<gpt(*)[DG_T + 1]>(dg_smem + DG_K * (DG_T + 1));
+    double(*As)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem);
+    double(*Bs)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem + DG_K * (DG_T + 1));
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const int m0 = blockIdx.y * DG_T, n0 = blockIdx.x * DG_T;
     const int M = q.M, N = q.N, K = q.K;
     if (m0 >= M || n0 >= N || (q.lower_only && n0 > m0 + DG_T - 1))
         return;
-    gpt acc[4][4] = {};
+    double acc[4][4] = {};
     const bool a_k = q.sak == 1, b_n = q.sbn == 1;
     for (int k0 = 0; k0 < K; k0 += DG_K) {
         // Element-wise asynchronous copies (8 bytes, zero fill outside the
@@ -200,20 +192,20 @@ __global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
             int r = a_k ? e / DG_K : e % DG_T, k = a_k ? e % DG_K : e / DG_T;
             int m = m0 + r, kk = k0 + k;
             bool in = m < M && kk < K;
-            cp_async_el(&As[k][r], in ? q.A + (long)m * q.sam + (long)kk * q.sak : q.A, in);
+            cp_async8(&As[k][r], in ? q.A + (long)m * q.sam + (long)kk * q.sak : q.A, in);
             r = b_n ? e % DG_T : e / DG_K;
             k = b_n ? e / DG_T : e % DG_K;
             const int nn = n0 + r;
             kk = k0 + k;
             in = nn < N && kk < K;
-            cp_async_el(&Bs[k][r], in ? q.B + (long)kk * q.sbk + (long)nn * q.sbn : q.B, in);
+            cp_async8(&Bs[k][r], in ? q.B + (long)kk * q.sbk + (long)nn * q.sbn : q.B, in);
         }
         asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
         __syncthreads();
         const int kc = K - k0 < DG_K ? K - k0 : DG_K;
 #pragma unroll 8
         for (int k = 0; k < kc; k++) {
-            gpt a[4], bb[4];
+            double a[4], bb[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 a[i] = As[k][ty + 16 * i];
@@ -236,15 +228,15 @@ __global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
         for (int j = 0; j < 4; j++) {
             const int nn = n0 + tx + 16 * j;
             if (nn < N && (!q.lower_only || nn <= m)) {
-                gpt *c = q.C + (long)m * q.ldc + nn;
+                double *c = q.C + (long)m * q.ldc + nn;
                 *c = q.sub ? *c - acc[i][j] : acc[i][j];
             }
         }
     }
 }
 
-static DgProb prob(int M, int N, int K, const gpt *A, long sam, long sak, const gpt *B,
-                   long sbk, long sbn, gpt *C, long ldc, int sub, int lower_only)
+static DgProb prob(int M, int N, int K, const double *A, long sam, long sak, const double *B,
+                   long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
 {
     DgProb p = {M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, sub, lower_only};
     return p;
@@ -266,14 +258,14 @@ static void dgemm2(cudaStream_t st, const DgProb *p0, const DgProb *p1)
         dgemm_k<<<dim3(gx, gy, count), 256, DG_SMEM, st>>>(b);
 }
 
-__global__ void gp_load_rhs_k(const float *F, long e_n, gpt *Z)
+__global__ void gp_load_rhs_k(const float *F, long e_n, double *Z)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e < e_n)
         Z[e] = F[e];
 }
 
-__global__ void gp_store_k(const gpt *Z, long e_n, float *X)
+__global__ void gp_store_k(const double *Z, long e_n, float *X)
 {
     const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (e < e_n)
@@ -281,7 +273,7 @@ __global__ void gp_store_k(const gpt *Z, long e_n, float *X)
 }
 
 // Work: A and L (n x n each), F, Z, X (n x d each) and cdiv(n, 64) 64 x 64
-// inverses, counted in doubles (float32 elements fill half of it).
+// inverses, in doubles.
 size_t gp_work_doubles(int n, int d)
 {
     const size_t nb = (size_t)cdiv(n, GP_NB);
@@ -303,13 +295,12 @@ static bool opt_in(const void *fn, size_t bytes, unsigned *mask)
 }
 
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int d,
-                  double noise_d, float *X_out, double *work, int *flag)
+                  double noise, float *X_out, double *work, int *flag)
 {
     const int nb = cdiv(n, GP_NB);
-    const gpt noise = (gpt)noise_d;
-    gpt *A = reinterpret_cast<gpt *>(work), *L = A + (size_t)n * n;
-    gpt *F = L + (size_t)n * n, *Z = F + (size_t)n * d, *X = Z + (size_t)n * d;
-    gpt *Linv = X + (size_t)n * d;
+    double *A = work, *L = A + (size_t)n * n;
+    double *F = L + (size_t)n * n, *Z = F + (size_t)n * d, *X = Z + (size_t)n * d;
+    double *Linv = X + (size_t)n * d;
     const long nn = (long)n * n, nd = (long)n * d;
     static unsigned opted_g = 0, opted_p = 0;
     if (!opt_in((const void *)dgemm_k, DG_SMEM, &opted_g) ||
@@ -321,7 +312,7 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int
     for (int j = 0; j < nb; j++) {
         const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
         const int rest = n - j0 - b;
-        gpt *Li = Linv + (size_t)j * GP_NB * GP_NB;
+        double *Li = Linv + (size_t)j * GP_NB * GP_NB;
         gp_potrf_inv_k<<<1, 256, GP_POTRF_SMEM, st>>>(A, L, n, j0, b, Li, flag);
         const long below = (long)(j0 + b) * n + j0;
         // L_below = A_below Linv^T;  Z_j = Linv F_j.
@@ -339,7 +330,7 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int
     // L^T X = Z from the last block up.
     for (int j = nb - 1; j >= 0; j--) {
         const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
-        const gpt *Li = Linv + (size_t)j * GP_NB * GP_NB;
+        const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
         const DgProb xj = prob(b, d, b, Li, 1, GP_NB, Z + (long)j0 * d, d, 1, X + (long)j0 * d,
                                d, 0, 0);
         dgemm2(st, &xj, nullptr);

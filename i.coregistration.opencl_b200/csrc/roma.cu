@@ -1235,7 +1235,7 @@ void dino(Ctx &c)
 
 // Gaussian-process posterior of A's 1/16 features given B's and the
 // position basis, into t_x columns 0..511, A's features in 512..1023
-// (roma.c:873-896), the solve on the device (float32, gp_chol.cu).
+// (roma.c:873-896), the solve on the device in double.
 void gp(Ctx &c)
 {
     roma_impl *I = c.I;

@@ -49,9 +49,8 @@ void roma_dwconv5(struct ops *o, cl_mem in, int C, int H, int W, cl_mem wt,
 
 /* The Gaussian process's solve, X = (K + noise I)^-1 F, for the n x n
  * kernel matrix K (symmetric, row-major) and the n x d right-hand sides F,
- * in float32 on the device (blocked Cholesky, then the two triangular
- * solves; within about 1e-7 relative of the reference's double solve on
- * the GP's kernel matrices); X may not alias F. Synchronous. Returns 0, or 1
+ * in double precision on the device (blocked Cholesky, then the two
+ * triangular solves); X may not alias F. Synchronous. Returns 0, or 1
  * when K + noise I is not positive definite (the reference stops there
  * with "kernel not positive definite"; X is then meaningless). */
 int roma_gp_solve(struct ops *o, cl_mem K, int n, cl_mem F, int d, double noise, cl_mem X);

@@ -4,13 +4,11 @@ include/roma_ops.h) against the reference's own host solve (gp_solve,
 roma.c:772-836, compiled from its roma.c into oracle/_ref/
 libroma_host_ref.so) (GPU).
 
-The reference factors K + 0.1 I in double; the device solve runs in
-float32 (blocked Cholesky, then the two triangular solves), so X must
-agree to relative L2 1e-6 on the GP's kernel matrices (the cosine kernel of
-the build's features, temperature 0.2; condition numbers up to a few
-thousand), sizes that do and do not fill the 64-row blocks, up to the full
-1600 tokens x 512 basis columns; a matrix that is not positive definite
-is reported."""
+Both factor K + 0.1 I in double and round X to float, in different
+orders, so X must agree to relative L2 1e-6 on the GP's kernel matrices
+(the cosine kernel of the build's features, temperature 0.2), sizes that
+do and do not fill the 64-row blocks, up to the full 1600 tokens x 512
+basis columns; a matrix that is not positive definite is reported."""
 
 import ctypes as C
 from pathlib import Path
