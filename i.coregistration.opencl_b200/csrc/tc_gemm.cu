@@ -37,7 +37,6 @@
 // frees its tensor memory and returns.
 
 #include <mutex>
-#include <stdlib.h>
 #include <string.h>
 
 #include "tc_common.cuh"
@@ -477,18 +476,6 @@ bool run_tc(cudaStream_t st, int grid, const CUtensorMap &ma, const CUtensorMap 
 
 bool make_map_c(CUtensorMap *map, void *base, int es, const TcParams &p, long ldc);
 
-// COREG_TC_TAP_REUSE=0 in the environment turns tap reuse off (the plain
-// convolution mode, one A box per tap), for comparisons.
-bool tap_reuse_off()
-{
-    static int off = -1;
-    if (off < 0) {
-        const char *e = getenv("COREG_TC_TAP_REUSE");
-        off = e && e[0] == '0';
-    }
-    return off != 0;
-}
-
 template <int BN, int STAGES>
 bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
 {
@@ -516,7 +503,7 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
         const int rsb = rab + 3 * BN * BK * 2;
         const int total = STAGES * (BM + BN) * BK * 2;
         if (p.ksz == 3 && p.TW % 8 == 0 && p.TH + 2 <= 256 && total / rsb >= 2 &&
-            !tap_reuse_off() && make_map_conv(&ma3, g.A, g.cH, g.cW, g.cC, p.TW, p.TH + 2)) {
+            make_map_conv(&ma3, g.A, g.cH, g.cW, g.cC, p.TW, p.TH + 2)) {
             p.reuse = total / rsb;
             p.rsb = rsb;
             p.rab = rab;
