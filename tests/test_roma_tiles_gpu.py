@@ -67,3 +67,43 @@ def test_tiles_missing_weights_is_an_error(tmp_path):
     with pytest.raises(coreg.CoregError, match="roma_tiles_create"):
         RomaTiles([0], 2, coreg.OPS_BF16, tmp_path / "missing.safetensors", dino, v2, H=H, W=W,
                   coarse=COARSE)
+
+
+def device_count():
+    import torch
+
+    return torch.cuda.device_count()
+
+
+@pytest.mark.gpu
+def test_tiles_over_two_devices_in_order():
+    """Two devices, two pipelines each: the tiles are dealt across both GPUs
+    and come back in order, each equal to a single-device roma_match bit
+    for bit (bfloat16; the same kernels on every B200). Skips on a machine
+    with one GPU."""
+    if device_count() < 2:
+        pytest.skip("needs two GPUs")
+    main, dino, v2 = weight_paths()
+    tiles = [tile_pair(70 + i, H, W)[:2] for i in range(9)]
+    dev = coreg.Device(0, precision=coreg.OPS_BF16)
+    solo = Roma(dev, main, dino, v2, H=H, W=W, coarse=COARSE)
+    try:
+        want = [np.copy(solo.match(*t)[0]) for t in tiles]
+    finally:
+        solo.close()
+        dev.close()
+    q = RomaTiles([0, 1], 2, coreg.OPS_BF16, main, dino, v2, H=H, W=W, coarse=COARSE)
+    got = []
+
+    def get(i, a, b):
+        a[...] = tiles[i][0]
+        b[...] = tiles[i][1]
+
+    try:
+        assert q.pipelines == 4
+        assert q.run(len(tiles), get, lambda i, f, c, s: got.append((i, f.copy()))) == len(tiles)
+    finally:
+        q.close()
+    assert [g[0] for g in got] == list(range(len(tiles)))
+    for (i, f), w in zip(got, want):
+        assert np.array_equal(f, w, equal_nan=True), i
