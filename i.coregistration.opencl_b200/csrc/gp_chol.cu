@@ -8,20 +8,28 @@
 // double, then the two substitutions), whose device round trip
 // (roma.c:885-888) disappears.
 //
-// Blocks of NB = 64. One CTA of 256 threads factors each diagonal block
-// and inverts it (Linv_j), so that every other step is a double-precision
-// GEMM. The
-// working matrix A, the factor L and the right-hand sides F, Z, X live in
-// separate buffers, so no step multiplies in place:
-//   step j     L_jj, Linv_j           from A_jj
-//              L_below = A_below Linv_j^T,  Z_j = Linv_j F_j     (one launch)
-//              A_trail -= L_below L_below^T (lower),
-//              F_below -= L_below Z_j                            (one launch)
-//   backward   X_j = Linv_j^T Z_j,  then Z_above -= L_j,above^T X_j
+// Blocks of 64 rows. The factor overwrites the lower triangle of the
+// working matrix A in place; the right-hand sides F become Z, then X, in
+// place in R. Three kernels, every CTA one 64 x 64 block of work:
+//   gp_factor_k (j)  CTA 0: the diagonal block j receives the update of
+//                    block column j - 1 and is factored (L_jj and the
+//                    reciprocals 1 / L_kk); the other CTAs apply the same
+//                    update to the rest of the trailing matrix (lower
+//                    blocks) and to the right-hand sides below block j-1;
+//   gp_panel_k (j)   the blocks below the diagonal, L_ij = A_ij L_jj^-T, and
+//                    Z_j = L_jj^-1 F_j, by forward substitution;
+//   gp_back_k (j)    from the last block up: Z_j receives the update of
+//                    X_{j+1} and is solved against L_jj^T (X_j, also
+//                    rounded to float into the output), while the other
+//                    CTAs apply X_{j+1}'s update to Z_i, i < j.
+// Each 64-vector of a substitution is held by four threads of a warp (16
+// entries each); the entry solved at a step is passed to the other three
+// by a shuffle, so the 64 steps need no barrier. The diagonal factor is a
+// right-looking elimination in shared memory, one barrier per column, with
+// the reciprocal of each pivot instead of a square root on the column's
+// chain; the square roots are taken once at the end.
 // A non-positive pivot sets *flag (the reference stops with "kernel not
 // positive definite"); the host reads it after the tile.
-
-#include <initializer_list>
 
 #include "common.cuh"
 
@@ -29,316 +37,413 @@ namespace coreg {
 
 #define GP_NB 64
 
-// A = K + noise I in double.
-__global__ void gp_init_k(const float *K, int n, double noise, double *A)
+namespace {
+
+constexpr int GP_T = 256;         // threads per CTA
+constexpr int GP_SP = GP_NB + 1;  // pitch of the staged product operands and of the block
+// A staged triangular factor: row k holds four quarters of 16 entries,
+// each padded to 18 doubles, so that the four quarters a warp reads at
+// one step (16-byte loads) fall in different banks.
+constexpr int GP_QP = 18, GP_LP = 4 * GP_QP;
+constexpr size_t GP_SMEM = 2 * GP_NB * GP_SP * sizeof(double);
+static_assert((size_t)GP_NB * GP_LP * sizeof(double) + GP_NB * sizeof(double) <= GP_SMEM,
+              "the staged factor fits the operand staging");
+// Elements of the 64 x 64 lower triangle each thread of the diagonal
+// factor owns.
+constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + GP_T - 1) / GP_T;
+
+struct Gp {
+    double *A;   // n x n, pitch n: K + noise I (lower triangle), then L
+    double *R;   // n x d: F, then Z, then X
+    double *rd;  // n: 1 / L_kk
+    float *X;    // n x d: X rounded to float
+    int n, d, nb, db;
+    int *flag;
+};
+
+__device__ __forceinline__ int block_rows(int n, int i)
 {
-    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= (long)n * n)
-        return;
-    const long i = e / n, j = e % n;
-    A[e] = (double)K[e] + (i == j ? noise : 0.0);
+    return min(GP_NB, n - i * GP_NB);
 }
 
-constexpr int GP_P = GP_NB + 1;  // shared-memory pitch (doubles)
-// Elements of the 64 x 64 lower triangle each of the 256 threads owns.
-constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + 255) / 256;
-
-// Factor the b x b diagonal block of A at (j0, j0) (b <= 64; identity beyond
-// b) with all 256 threads: a right-looking unblocked Cholesky in shared
-// memory, one barrier per column (thread t owns the lower-triangle elements
-// t, t + 256, ...: at column k it updates those right of k with the scaled
-// column, l_i = a_ik / sqrt(a_kk), a_ij -= l_i l_j, while the threads of
-// rows i > k write l_i into the factor), then the inverse of the factor,
-// four threads per column (each column of L^-1 by forward substitution,
-// the sums split four ways and joined by shuffles). Writes the lower
-// factor into L (pitch n) and the 64 x 64 inverse into Linv. A
-// non-positive pivot sets *flag (the factor is then meaningless, as the
-// reference's stop says).
-__global__ void __launch_bounds__(256)
-gp_potrf_inv_k(const double *A, double *L, int n, int j0, int b, double *Linv, int *flag)
+// C (rows x cols, pitch ldc) -= P Q over kd terms, P(r, k) = P[r psr + k
+// psk], Q(k, c) = Q[k qsk + c qsc]; operand entries beyond rows, cols or kd
+// read as zero. The operands are staged k-major in shared memory (each
+// loaded along its unit-stride dimension), every thread accumulates a 4 x
+// 4 block of C.
+__device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const double *P,
+                         long psr, long psk, const double *Q, long qsk, long qsc, double *sm)
 {
-    extern __shared__ double gp_smem[];
-    double *M = gp_smem;                  // 64 x GP_P: the block, updated
-    double *F = gp_smem + GP_NB * GP_P;   // 64 x GP_P: the factor
-    double *X = F + GP_NB * GP_P;         // 64 x GP_P: the inverse
+    double(*Ps)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
+    double(*Qs)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
     const int t = threadIdx.x;
+    const bool pk = psk == 1, qk = qsk == 1;
+    // One operand at a time: 16 loads in flight per thread, 16 registers.
+    double x[16];
 #pragma unroll
-    for (int e = t; e < GP_NB * GP_NB; e += 256) {
-        const int i = e / GP_NB, j = e % GP_NB;
-        M[i * GP_P + j] = i < b && j < b ? A[(long)(j0 + i) * n + j0 + j] : (i == j ? 1.0 : 0.0);
-        F[i * GP_P + j] = 0.0;
+    for (int u = 0; u < 16; u++) {
+        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
+        const int r = pk ? hi : lo, k = pk ? lo : hi;
+        x[u] = r < rows && k < kd ? P[r * psr + k * psk] : 0.0;
     }
-    // This thread's lower-triangle elements (row-major order of the
-    // triangle: element e lies in row i with i (i + 1) / 2 <= e).
-    int oi[GP_OWN], oj[GP_OWN];
 #pragma unroll
-    for (int r = 0; r < GP_OWN; r++) {
-        const int e = t + 256 * r;
+    for (int u = 0; u < 16; u++) {
+        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
+        if (pk)
+            Ps[lo][hi] = x[u];
+        else
+            Ps[hi][lo] = x[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
+        const int c = qk ? hi : lo, k = qk ? lo : hi;
+        x[u] = c < cols && k < kd ? Q[k * qsk + c * qsc] : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
+        if (qk)
+            Qs[lo][hi] = x[u];
+        else
+            Qs[hi][lo] = x[u];
+    }
+    __syncthreads();
+    const int tx = t % 16, ty = t / 16;
+    double acc[4][4] = {};
+#pragma unroll 8
+    for (int k = 0; k < GP_NB; k++) {
+        double a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            a[i] = Ps[k][ty + 16 * i];
+            b[i] = Qs[k][tx + 16 * i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                acc[i][c] = fma(a[i], b[c], acc[i][c]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = ty + 16 * i;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int cc = tx + 16 * c;
+            if (r < rows && cc < cols)
+                C[r * ldc + cc] -= acc[i][c];
+        }
+    }
+    // The staging may be reused, and C's new values are visible to the
+    // whole CTA.
+    __syncthreads();
+}
+
+// Position of entry m of row k in a staged triangular factor.
+__device__ __forceinline__ int lpos(int k, int m)
+{
+    return k * GP_LP + (m >> 4) * GP_QP + (m & 15);
+}
+
+// Stages the factor L_jj (lower triangle of A's block (j, j), identity
+// beyond the block's b rows) into sm: transposed (Ls row k = column k of L)
+// for the forward substitution, as is for the backward one; then the
+// reciprocals 1 / L_kk (1 beyond b) at sm + 64 GP_LP.
+template <bool FWD>
+__device__ void stage_factor(const Gp &g, int j, double *sm)
+{
+    const int j0 = j * GP_NB, b = block_rows(g.n, j);
+    const double *Ab = g.A + (long)j0 * g.n + j0;
+    for (int e = threadIdx.x; e < GP_NB * GP_NB; e += GP_T) {
+        const int r = e / GP_NB, c = e % GP_NB;
+        const double v = c > r ? 0.0 : r < b ? Ab[(long)r * g.n + c] : (r == c ? 1.0 : 0.0);
+        sm[FWD ? lpos(c, r) : lpos(r, c)] = v;
+    }
+    if (threadIdx.x < GP_NB)
+        sm[GP_NB * GP_LP + threadIdx.x] = threadIdx.x < b ? g.rd[j0 + threadIdx.x] : 1.0;
+    __syncthreads();
+}
+
+// Solves L y = v (FWD) or L^T y = v in place for the 64-vector v held by
+// the four threads (lane & ~3) + 0..3 of a warp, quarter q holding entries
+// 16 q .. 16 q + 15. Ls is the staged factor (transposed for FWD: row k
+// holds L_mk; else row k holds L_km), rd the reciprocals of its diagonal.
+// Step k: the quarter that holds entry k scales it by 1 / L_kk, the
+// shuffle hands the result to the other three, and each subtracts its
+// multiples from the entries still to come (m > k forward, m < k back).
+template <bool FWD>
+__device__ __forceinline__ void tri_solve(double v[16], int q, const double *Ls, const double *rd)
+{
+    const int base = (int)(threadIdx.x & 31) & ~3;
+#pragma unroll
+    for (int s = 0; s < GP_NB; s++) {
+        const int k = FWD ? s : GP_NB - 1 - s;
+        const int qk = k >> 4, ik = k & 15;
+        double y = v[ik] * rd[k];
+        y = __shfl_sync(0xffffffffu, y, base | qk);
+        if (q == qk)
+            v[ik] = y;
+        if (FWD ? q >= qk : q <= qk) {
+            const double *lk = Ls + k * GP_LP + q * GP_QP;
+#pragma unroll
+            for (int u = 0; u < 16; u += 2) {
+                const double2 l = *reinterpret_cast<const double2 *>(lk + u);
+                const int m = 16 * q + u;
+                if (FWD ? m > k : m < k)
+                    v[u] = fma(-l.x, y, v[u]);
+                if (FWD ? m + 1 > k : m + 1 < k)
+                    v[u + 1] = fma(-l.y, y, v[u + 1]);
+            }
+        }
+    }
+}
+
+// The diagonal block j: the update of block column j - 1 (j > 0), then the
+// factorization in shared memory. Right-looking on the unscaled columns:
+// at step k every element (i, m), i >= m > k, takes a_ik a_mk / a_kk off;
+// the columns become final one step at a time, and each owner stores its
+// element to shared memory when its column does. Finally L_ik = a_ik /
+// sqrt(a_kk) into A's block and 1 / L_kk into rd.
+__device__ void diag_factor(const Gp &g, int j, double *sm)
+{
+    const int t = threadIdx.x, j0 = j * GP_NB, b = block_rows(g.n, j);
+    double *Ab = g.A + (long)j0 * g.n + j0;
+    if (j > 0)
+        tile_sub(Ab, g.n, b, b, GP_NB, Ab - GP_NB, g.n, 1, Ab - GP_NB, 1, g.n, sm);
+    double(*S)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
+    // This thread's elements of the lower triangle (row-major order of the
+    // triangle: element e lies in row i with i (i + 1) / 2 <= e).
+    int oi[GP_OWN], om[GP_OWN];
+    double ov[GP_OWN];
+#pragma unroll
+    for (int u = 0; u < GP_OWN; u++) {
+        const int e = t + GP_T * u;
         int i = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
         while ((i + 1) * (i + 2) / 2 <= e)
             i++;
         while (i * (i + 1) / 2 > e)
             i--;
-        oi[r] = e < GP_NB * (GP_NB + 1) / 2 ? i : -1;
-        oj[r] = e - i * (i + 1) / 2;
+        const int m = e - i * (i + 1) / 2;
+        const bool in = e < GP_NB * (GP_NB + 1) / 2;
+        oi[u] = in ? i : -1;
+        om[u] = m;
+        ov[u] = !in ? 0.0 : i < b ? Ab[(long)i * g.n + m] : (i == m ? 1.0 : 0.0);
+        // Column 0 is final from the start.
+        if (in && m == 0)
+            S[i][0] = ov[u];
     }
     __syncthreads();
     for (int k = 0; k < GP_NB; k++) {
-        double d = M[k * GP_P + k];
+        double d = S[k][k];
         if (!(d > 0.0)) {
-            if (t == 0)
-                *flag = 1;
+            if (t == 0 && k < b)
+                *g.flag = 1;
             d = 1.0;
         }
-        const double piv = sqrt(d), rinv = 1.0 / piv;
-        if (t == k)
-            F[k * GP_P + k] = piv;
-        else if (t > k && t < GP_NB)
-            F[t * GP_P + k] = M[t * GP_P + k] * rinv;
+        const double r = 1.0 / d;
 #pragma unroll
-        for (int r = 0; r < GP_OWN; r++) {
-            const int i = oi[r], j = oj[r];
-            if (i >= 0 && j > k) {
-                const double li = M[i * GP_P + k] * rinv, lj = M[j * GP_P + k] * rinv;
-                M[i * GP_P + j] = fma(-li, lj, M[i * GP_P + j]);
+        for (int u = 0; u < GP_OWN; u++) {
+            const int i = oi[u], m = om[u];
+            if (i >= 0 && m > k) {
+                ov[u] = fma(-S[i][k] * r, S[m][k], ov[u]);
+                if (m == k + 1)
+                    S[i][m] = ov[u];
             }
         }
         __syncthreads();
     }
-    // The inverse: column c by threads 4 c .. 4 c + 3; x_i = (delta_ic -
-    // sum_{c <= m < i} F_im x_m) / F_ii for i >= c, zero above.
-    {
-        // Every lane takes part in every shuffle (rows above a column's
-        // diagonal sum nothing and store zero).
-        const int c = t / 4, q = t % 4;
-        for (int i = 0; i < GP_NB; i++) {
-            double acc = 0.0;
-            for (int m = c + q; m < i; m += 4)
-                acc = fma(F[i * GP_P + m], X[m * GP_P + c], acc);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (q == 0)
-                X[i * GP_P + c] =
-                    i < c ? 0.0 : ((i == c ? 1.0 : 0.0) - acc) / F[i * GP_P + i];
-            __syncwarp();
+#pragma unroll
+    for (int u = 0; u < GP_OWN; u++) {
+        const int i = oi[u], m = om[u];
+        if (i >= 0 && i < b) {
+            double d = S[m][m];
+            d = d > 0.0 ? d : 1.0;
+            Ab[(long)i * g.n + m] = ov[u] * rsqrt(d);
         }
     }
-    __syncthreads();
-#pragma unroll
-    for (int e = t; e < GP_NB * GP_NB; e += 256) {
-        const int i = e / GP_NB, j = e % GP_NB;
-        Linv[e] = X[i * GP_P + j];
-        if (i < b && j < b)
-            L[(long)(j0 + i) * n + j0 + j] = F[i * GP_P + j];
+    if (t < b) {
+        const double d = S[t][t];
+        g.rd[j0 + t] = rsqrt(d > 0.0 ? d : 1.0);
     }
 }
 
-constexpr size_t GP_POTRF_SMEM = 3 * GP_NB * GP_P * sizeof(double);
-
-// C (M x N, ldc) = A B (sub 0) or C -= A B (sub 1), A(m, k) = A[m sam + k
-// sak], B(k, n) = B[k sbk + n sbn]; lower_only skips tiles and elements
-// above the diagonal.
-struct DgProb {
-    int M, N, K;
-    const double *A;
-    long sam, sak;
-    const double *B;
-    long sbk, sbn;
-    double *C;
-    long ldc;
-    int sub, lower_only;
-};
-
-// Up to two independent products per launch (blockIdx.z).
-struct DgBatch {
-    DgProb p[2];
-};
-
-// 64 x 64 tiles, 4 x 4 per thread. Each CTA stages 64-deep K panels of
-// both operands (dynamic shared memory, loads along each operand's
-// unit-stride dimension) and runs the panel with no barrier inside; the
-// blocked Cholesky's products have K <= 64, so one panel and two barriers
-// per tile.
-constexpr int DG_T = 64, DG_K = 64;
-constexpr size_t DG_SMEM = 2 * DG_K * (DG_T + 1) * sizeof(double);
-
-__device__ __forceinline__ void cp_async8(double *dst, const double *src, bool in)
+// Step j of the factorization: CTA 0 the diagonal block; CTAs 1 .. T - 1
+// the lower blocks (i, k), j <= k <= i, other than (j, j), of the trailing
+// matrix; then the right-hand-side blocks (i, column block c), i >= j, all
+// with the update of block column j - 1 (A -= L_i,j-1 L_k,j-1^T, F_i -=
+// L_i,j-1 Z_j-1).
+__global__ void __launch_bounds__(GP_T) gp_factor_k(Gp g, int j)
 {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(
-                     (unsigned)__cvta_generic_to_shared(dst)),
-                 "l"(src), "r"(in ? 8 : 0)
-                 : "memory");
-}
-
-__global__ void __launch_bounds__(256) dgemm_k(DgBatch batch)
-{
-    extern __shared__ double dg_smem[];
-    const DgProb &q = batch.p[blockIdx.z];
-    double(*As)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem);
-    double(*Bs)[DG_T + 1] = reinterpret_cast<double(*)[DG_T + 1]>(dg_smem + DG_K * (DG_T + 1));
-    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    const int m0 = blockIdx.y * DG_T, n0 = blockIdx.x * DG_T;
-    const int M = q.M, N = q.N, K = q.K;
-    if (m0 >= M || n0 >= N || (q.lower_only && n0 > m0 + DG_T - 1))
+    extern __shared__ __align__(16) double gp_sm[];
+    if (blockIdx.x == 0) {
+        diag_factor(g, j, gp_sm);
         return;
-    double acc[4][4] = {};
-    const bool a_k = q.sak == 1, b_n = q.sbn == 1;
-    for (int k0 = 0; k0 < K; k0 += DG_K) {
-        // Element-wise asynchronous copies (8 bytes, zero fill outside the
-        // operands): every load of the panel in flight at once, no register
-        // staging.
-#pragma unroll 4
-        for (int e = threadIdx.x; e < DG_T * DG_K; e += 256) {
-            int r = a_k ? e / DG_K : e % DG_T, k = a_k ? e % DG_K : e / DG_T;
-            int m = m0 + r, kk = k0 + k;
-            bool in = m < M && kk < K;
-            cp_async8(&As[k][r], in ? q.A + (long)m * q.sam + (long)kk * q.sak : q.A, in);
-            r = b_n ? e % DG_T : e / DG_K;
-            k = b_n ? e / DG_T : e % DG_K;
-            const int nn = n0 + r;
-            kk = k0 + k;
-            in = nn < N && kk < K;
-            cp_async8(&Bs[k][r], in ? q.B + (long)kk * q.sbk + (long)nn * q.sbn : q.B, in);
-        }
-        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-        __syncthreads();
-        const int kc = K - k0 < DG_K ? K - k0 : DG_K;
-#pragma unroll 8
-        for (int k = 0; k < kc; k++) {
-            double a[4], bb[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                a[i] = As[k][ty + 16 * i];
-                bb[i] = Bs[k][tx + 16 * i];
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    acc[i][j] = fma(a[i], bb[j], acc[i][j]);
-        }
-        __syncthreads();
     }
+    const int p0 = (j - 1) * GP_NB, m = g.nb - j;
+    const long nk = (long)m * (m + 1) / 2;
+    const long e = blockIdx.x;
+    if (e < nk) {
+        int ii = (int)((sqrt(8.0 * (double)e + 1.0) - 1.0) * 0.5);
+        while ((long)(ii + 1) * (ii + 2) / 2 <= e)
+            ii++;
+        while ((long)ii * (ii + 1) / 2 > e)
+            ii--;
+        const int kk = (int)(e - (long)ii * (ii + 1) / 2);
+        const int i0 = (j + ii) * GP_NB, k0 = (j + kk) * GP_NB;
+        tile_sub(g.A + (long)i0 * g.n + k0, g.n, block_rows(g.n, j + ii),
+                 block_rows(g.n, j + kk), GP_NB, g.A + (long)i0 * g.n + p0, g.n, 1,
+                 g.A + (long)k0 * g.n + p0, 1, g.n, gp_sm);
+        return;
+    }
+    const long f = e - nk;
+    const int i = j + (int)(f / g.db), c0 = (int)(f % g.db) * GP_NB, i0 = i * GP_NB;
+    tile_sub(g.R + (long)i0 * g.d + c0, g.d, block_rows(g.n, i), min(GP_NB, g.d - c0), GP_NB,
+             g.A + (long)i0 * g.n + p0, g.n, 1, g.R + (long)p0 * g.d + c0, g.d, 1, gp_sm);
+}
+
+// Block column j: CTAs 0 .. nb - j - 2 the rows of the blocks below the
+// diagonal (L_ij = A_ij L_jj^-T: each row solved against L_jj); then one
+// CTA per 64 right-hand-side columns, Z_j = L_jj^-1 F_j.
+__global__ void __launch_bounds__(GP_T) gp_panel_k(Gp g, int j)
+{
+    extern __shared__ __align__(16) double gp_sm[];
+    stage_factor<true>(g, j, gp_sm);
+    const int t = threadIdx.x, q = t & 3, vi = t >> 2;
+    const int j0 = j * GP_NB, b = block_rows(g.n, j), nk = g.nb - 1 - j;
+    const double *rd = gp_sm + GP_NB * GP_LP;
+    double v[16];
+    if ((int)blockIdx.x < nk) {
+        const int i = j + 1 + blockIdx.x, rows = block_rows(g.n, i);
+        double *row = g.A + (long)(i * GP_NB + vi) * g.n + j0 + 16 * q;
+        // Scalar accesses: the rows are 16-byte aligned only for even n.
+        const bool in = vi < rows;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int m = m0 + ty + 16 * i;
-        if (m >= M)
-            continue;
+        for (int u = 0; u < 16; u++)
+            v[u] = in ? row[u] : 0.0;
+        tri_solve<true>(v, q, gp_sm, rd);
+        if (in)
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int nn = n0 + tx + 16 * j;
-            if (nn < N && (!q.lower_only || nn <= m)) {
-                double *c = q.C + (long)m * q.ldc + nn;
-                *c = q.sub ? *c - acc[i][j] : acc[i][j];
-            }
+            for (int u = 0; u < 16; u++)
+                row[u] = v[u];
+        return;
+    }
+    const int c = ((int)blockIdx.x - nk) * GP_NB + vi;
+    double *col = g.R + (long)(j0 + 16 * q) * g.d + c;
+#pragma unroll
+    for (int u = 0; u < 16; u++)
+        v[u] = c < g.d && 16 * q + u < b ? col[(long)u * g.d] : 0.0;
+    tri_solve<true>(v, q, gp_sm, rd);
+#pragma unroll
+    for (int u = 0; u < 16; u++)
+        if (c < g.d && 16 * q + u < b)
+            col[(long)u * g.d] = v[u];
+}
+
+// Backward step j: CTAs 0 .. db - 1 take Z_j's 64-column blocks, subtract
+// L_j+1,j^T X_j+1 (j < nb - 1) and solve L_jj^T X_j = Z_j, storing X_j in
+// double and in float; the other CTAs subtract L_j+1,i^T X_j+1 from the
+// blocks Z_i, i < j.
+__global__ void __launch_bounds__(GP_T) gp_back_k(Gp g, int j)
+{
+    extern __shared__ __align__(16) double gp_sm[];
+    const int j0 = j * GP_NB, b = block_rows(g.n, j);
+    const bool next = j + 1 < g.nb;
+    const int k0 = j0 + GP_NB, kd = next ? block_rows(g.n, j + 1) : 0;
+    if ((int)blockIdx.x >= g.db) {
+        const int e = (int)blockIdx.x - g.db, i0 = (e / g.db) * GP_NB, c0 = (e % g.db) * GP_NB;
+        tile_sub(g.R + (long)i0 * g.d + c0, g.d, GP_NB, min(GP_NB, g.d - c0), kd,
+                 g.A + (long)k0 * g.n + i0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
+        return;
+    }
+    const int c0 = (int)blockIdx.x * GP_NB;
+    if (next)
+        tile_sub(g.R + (long)j0 * g.d + c0, g.d, b, min(GP_NB, g.d - c0), kd,
+                 g.A + (long)k0 * g.n + j0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
+    stage_factor<false>(g, j, gp_sm);
+    const int t = threadIdx.x, q = t & 3, c = c0 + (t >> 2);
+    double v[16];
+    const long off = (long)(j0 + 16 * q) * g.d + c;
+#pragma unroll
+    for (int u = 0; u < 16; u++)
+        v[u] = c < g.d && 16 * q + u < b ? g.R[off + (long)u * g.d] : 0.0;
+    tri_solve<false>(v, q, gp_sm, gp_sm + GP_NB * GP_LP);
+#pragma unroll
+    for (int u = 0; u < 16; u++)
+        if (c < g.d && 16 * q + u < b) {
+            g.R[off + (long)u * g.d] = v[u];
+            g.X[off + (long)u * g.d] = (float)v[u];
         }
+}
+
+// A = K + noise I (lower triangle in double), R = F in double.
+__global__ void gp_init_k(const float *K, const float *F, Gp g, double noise)
+{
+    const long nn = (long)g.n * g.n, nd = (long)g.n * g.d;
+    for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < nn + nd;
+         e += (long)gridDim.x * blockDim.x) {
+        if (e < nn) {
+            const long i = e / g.n, c = e % g.n;
+            if (c <= i)
+                g.A[e] = (double)K[e] + (i == c ? noise : 0.0);
+        }
+        else
+            g.R[e - nn] = F[e - nn];
     }
 }
 
-static DgProb prob(int M, int N, int K, const double *A, long sam, long sak, const double *B,
-                   long sbk, long sbn, double *C, long ldc, int sub, int lower_only)
+bool opt_in_all()
 {
-    DgProb p = {M, N, K, A, sam, sak, B, sbk, sbn, C, ldc, sub, lower_only};
-    return p;
-}
-
-// One launch for the non-empty products among p0 and p1 (either may be
-// NULL).
-static void dgemm2(cudaStream_t st, const DgProb *p0, const DgProb *p1)
-{
-    DgBatch b;
-    int count = 0, gx = 0, gy = 0;
-    for (const DgProb *p : {p0, p1})
-        if (p && p->M > 0 && p->N > 0 && p->K > 0) {
-            b.p[count++] = *p;
-            gx = max(gx, (int)cdiv(p->N, DG_T));
-            gy = max(gy, (int)cdiv(p->M, DG_T));
-        }
-    if (count)
-        dgemm_k<<<dim3(gx, gy, count), 256, DG_SMEM, st>>>(b);
-}
-
-__global__ void gp_load_rhs_k(const float *F, long e_n, double *Z)
-{
-    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e < e_n)
-        Z[e] = F[e];
-}
-
-__global__ void gp_store_k(const double *Z, long e_n, float *X)
-{
-    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e < e_n)
-        X[e] = (float)Z[e];
-}
-
-// Work: A and L (n x n each), F, Z, X (n x d each) and cdiv(n, 64) 64 x 64
-// inverses, in doubles.
-size_t gp_work_doubles(int n, int d)
-{
-    const size_t nb = (size_t)cdiv(n, GP_NB);
-    return 2 * (size_t)n * n + 3 * (size_t)n * d + nb * GP_NB * GP_NB;
-}
-
-static bool opt_in(const void *fn, size_t bytes, unsigned *mask)
-{
+    static unsigned mask = 0;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (*mask >> (dev & 31) & 1)
+    if (mask >> (dev & 31) & 1)
         return true;
-    if (!cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)bytes),
-                 "gp kernels"))
-        return false;
-    *mask |= 1u << (dev & 31);
+    for (const void *fn : {(const void *)gp_factor_k, (const void *)gp_panel_k,
+                           (const void *)gp_back_k})
+        if (!cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)GP_SMEM),
+                     "gp kernels"))
+            return false;
+    mask |= 1u << (dev & 31);
     return true;
+}
+
+}  // namespace
+
+// Work: A (n x n), R (n x d) and the n reciprocals, in doubles.
+size_t gp_work_doubles(int n, int d)
+{
+    return (size_t)n * n + (size_t)n * d + (size_t)n;
 }
 
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int d,
                   double noise, float *X_out, double *work, int *flag)
 {
-    const int nb = cdiv(n, GP_NB);
-    double *A = work, *L = A + (size_t)n * n;
-    double *F = L + (size_t)n * n, *Z = F + (size_t)n * d, *X = Z + (size_t)n * d;
-    double *Linv = X + (size_t)n * d;
-    const long nn = (long)n * n, nd = (long)n * d;
-    static unsigned opted_g = 0, opted_p = 0;
-    if (!opt_in((const void *)dgemm_k, DG_SMEM, &opted_g) ||
-        !opt_in((const void *)gp_potrf_inv_k, GP_POTRF_SMEM, &opted_p))
+    if (!opt_in_all())
         return;
-
-    gp_init_k<<<cdiv(nn, 256), 256, 0, st>>>(K, n, noise, A);
-    gp_load_rhs_k<<<cdiv(nd, 256), 256, 0, st>>>(F_in, nd, F);
-    for (int j = 0; j < nb; j++) {
-        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
-        const int rest = n - j0 - b;
-        double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        gp_potrf_inv_k<<<1, 256, GP_POTRF_SMEM, st>>>(A, L, n, j0, b, Li, flag);
-        const long below = (long)(j0 + b) * n + j0;
-        // L_below = A_below Linv^T;  Z_j = Linv F_j.
-        const DgProb panel = prob(rest, b, b, A + below, n, 1, Li, 1, GP_NB, L + below, n, 0, 0);
-        const DgProb zj = prob(b, d, b, Li, GP_NB, 1, F + (long)j0 * d, d, 1, Z + (long)j0 * d,
-                               d, 0, 0);
-        dgemm2(st, &panel, &zj);
-        // A_trail -= L_below L_below^T (lower);  F_below -= L_below Z_j.
-        const DgProb trail = prob(rest, rest, b, L + below, n, 1, L + below, 1, n,
-                                  A + (long)(j0 + b) * n + j0 + b, n, 1, 1);
-        const DgProb fb = prob(rest, d, b, L + below, n, 1, Z + (long)j0 * d, d, 1,
-                               F + (long)(j0 + b) * d, d, 1, 0);
-        dgemm2(st, &trail, &fb);
+    Gp g;
+    g.A = work;
+    g.R = work + (size_t)n * n;
+    g.rd = g.R + (size_t)n * d;
+    g.X = X_out;
+    g.n = n;
+    g.d = d;
+    g.nb = (int)cdiv(n, GP_NB);
+    g.db = (int)cdiv(d, GP_NB);
+    g.flag = flag;
+    const long total = (long)n * n + (long)n * d;
+    gp_init_k<<<(int)std::min<long>(cdiv(total, 256), 148 * 16), 256, 0, st>>>(K, F_in, g, noise);
+    for (int j = 0; j < g.nb; j++) {
+        const long m = g.nb - j;
+        const long grid = j == 0 ? 1 : m * (m + 1) / 2 + m * g.db;
+        gp_factor_k<<<(unsigned)grid, GP_T, GP_SMEM, st>>>(g, j);
+        gp_panel_k<<<(unsigned)(m - 1 + g.db), GP_T, GP_SMEM, st>>>(g, j);
     }
-    // L^T X = Z from the last block up.
-    for (int j = nb - 1; j >= 0; j--) {
-        const int j0 = j * GP_NB, b = n - j0 < GP_NB ? n - j0 : GP_NB;
-        const double *Li = Linv + (size_t)j * GP_NB * GP_NB;
-        const DgProb xj = prob(b, d, b, Li, 1, GP_NB, Z + (long)j0 * d, d, 1, X + (long)j0 * d,
-                               d, 0, 0);
-        dgemm2(st, &xj, nullptr);
-        const DgProb up =
-            prob(j0, d, b, L + (long)j0 * n, 1, n, X + (long)j0 * d, d, 1, Z, d, 1, 0);
-        dgemm2(st, &up, nullptr);
+    for (int j = g.nb - 1; j >= 0; j--) {
+        const int grid = g.db + (j + 1 < g.nb ? j * g.db : 0);
+        gp_back_k<<<grid, GP_T, GP_SMEM, st>>>(g, j);
     }
-    gp_store_k<<<cdiv(nd, 256), 256, 0, st>>>(X, nd, X_out);
 }
 
 }  // namespace coreg
