@@ -24,10 +24,12 @@
 //                    CTAs apply X_{j+1}'s update to Z_i, i < j.
 // Each 64-vector of a substitution is held by four threads of a warp (16
 // entries each); the entry solved at a step is passed to the other three
-// by a shuffle, so the 64 steps need no barrier. The diagonal factor is a
-// right-looking elimination in shared memory, one barrier per column, with
-// the reciprocal of each pivot instead of a square root on the column's
-// chain; the square roots are taken once at the end.
+// by a shuffle, so the 64 steps need no barrier and, with the staged
+// factor zero on and above its diagonal, no branch. The diagonal block is
+// factored 16 columns at a time, each panel by one warp in registers.
+// Operands are staged in shared memory by asynchronous copies. Every
+// chain here is latency-bound (one pivot after another), so the kernels
+// are written for short dependency chains and few instructions per step.
 // A non-positive pivot sets *flag (the reference stops with "kernel not
 // positive definite"); the host reads it after the tile.
 
@@ -48,9 +50,6 @@ constexpr int GP_QP = 18, GP_LP = 4 * GP_QP;
 constexpr size_t GP_SMEM = 2 * GP_NB * GP_SP * sizeof(double);
 static_assert((size_t)GP_NB * GP_LP * sizeof(double) + GP_NB * sizeof(double) <= GP_SMEM,
               "the staged factor fits the operand staging");
-// Elements of the 64 x 64 lower triangle each thread of the diagonal
-// factor owns.
-constexpr int GP_OWN = (GP_NB * (GP_NB + 1) / 2 + GP_T - 1) / GP_T;
 
 struct Gp {
     double *A;   // n x n, pitch n: K + noise I (lower triangle), then L
@@ -66,11 +65,27 @@ __device__ __forceinline__ int block_rows(int n, int i)
     return min(GP_NB, n - i * GP_NB);
 }
 
+// Asynchronous 8-byte copy global -> shared; zeros when !in (no bytes
+// read).
+__device__ __forceinline__ void cp8(double *dst, const double *src, bool in)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(in ? 8 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_wait_all()
+{
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // C (rows x cols, pitch ldc) -= P Q over kd terms, P(r, k) = P[r psr + k
 // psk], Q(k, c) = Q[k qsk + c qsc]; operand entries beyond rows, cols or kd
-// read as zero. The operands are staged k-major in shared memory (each
-// loaded along its unit-stride dimension), every thread accumulates a 4 x
-// 4 block of C.
+// read as zero. Both operands are staged k-major in shared memory by
+// asynchronous copies (all 32 of a thread in flight at once, each operand
+// read along its unit-stride dimension); the thread's 16 elements of C are
+// read while they land; every thread accumulates a 4 x 4 block of C.
 __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const double *P,
                          long psr, long psk, const double *Q, long qsk, long qsc, double *sm)
 {
@@ -78,39 +93,28 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
     double(*Qs)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
     const int t = threadIdx.x;
     const bool pk = psk == 1, qk = qsk == 1;
-    // One operand at a time: 16 loads in flight per thread, 16 registers.
-    double x[16];
 #pragma unroll
     for (int u = 0; u < 16; u++) {
         const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
-        const int r = pk ? hi : lo, k = pk ? lo : hi;
-        x[u] = r < rows && k < kd ? P[r * psr + k * psk] : 0.0;
+        int r = pk ? hi : lo, k = pk ? lo : hi;
+        bool in = r < rows && k < kd;
+        cp8(&Ps[k][r], in ? P + r * psr + k * psk : P, in);
+        r = qk ? hi : lo;
+        k = qk ? lo : hi;
+        in = r < cols && k < kd;
+        cp8(&Qs[k][r], in ? Q + k * qsk + r * qsc : Q, in);
     }
-#pragma unroll
-    for (int u = 0; u < 16; u++) {
-        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
-        if (pk)
-            Ps[lo][hi] = x[u];
-        else
-            Ps[hi][lo] = x[u];
-    }
-#pragma unroll
-    for (int u = 0; u < 16; u++) {
-        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
-        const int c = qk ? hi : lo, k = qk ? lo : hi;
-        x[u] = c < cols && k < kd ? Q[k * qsk + c * qsc] : 0.0;
-    }
-#pragma unroll
-    for (int u = 0; u < 16; u++) {
-        const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
-        if (qk)
-            Qs[lo][hi] = x[u];
-        else
-            Qs[hi][lo] = x[u];
-    }
-    __syncthreads();
     const int tx = t % 16, ty = t / 16;
-    double acc[4][4] = {};
+    double c0[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const int r = ty + 16 * i, cc = tx + 16 * c;
+            c0[i][c] = r < rows && cc < cols ? C[r * ldc + cc] : 0.0;
+        }
+    cp_wait_all();
+    __syncthreads();
 #pragma unroll 8
     for (int k = 0; k < GP_NB; k++) {
         double a[4], b[4];
@@ -123,7 +127,7 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
         for (int i = 0; i < 4; i++)
 #pragma unroll
             for (int c = 0; c < 4; c++)
-                acc[i][c] = fma(a[i], b[c], acc[i][c]);
+                c0[i][c] = fma(-a[i], b[c], c0[i][c]);
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -132,7 +136,7 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
         for (int c = 0; c < 4; c++) {
             const int cc = tx + 16 * c;
             if (r < rows && cc < cols)
-                C[r * ldc + cc] -= acc[i][c];
+                C[r * ldc + cc] = c0[i][c];
         }
     }
     // The staging may be reused, and C's new values are visible to the
@@ -146,126 +150,150 @@ __device__ __forceinline__ int lpos(int k, int m)
     return k * GP_LP + (m >> 4) * GP_QP + (m & 15);
 }
 
-// Stages the factor L_jj (lower triangle of A's block (j, j), identity
-// beyond the block's b rows) into sm: transposed (Ls row k = column k of L)
-// for the forward substitution, as is for the backward one; then the
-// reciprocals 1 / L_kk (1 beyond b) at sm + 64 GP_LP.
+// Stages the strictly lower part of the factor L_jj (A's block (j, j);
+// zeros on and above the diagonal and beyond the block's b rows) into sm:
+// transposed (row k = column k of L) for the forward substitution, as is
+// for the backward one; then the reciprocals 1 / L_kk (1 beyond b) at sm +
+// 64 GP_LP.
 template <bool FWD>
 __device__ void stage_factor(const Gp &g, int j, double *sm)
 {
     const int j0 = j * GP_NB, b = block_rows(g.n, j);
     const double *Ab = g.A + (long)j0 * g.n + j0;
-    for (int e = threadIdx.x; e < GP_NB * GP_NB; e += GP_T) {
-        const int r = e / GP_NB, c = e % GP_NB;
-        const double v = c > r ? 0.0 : r < b ? Ab[(long)r * g.n + c] : (r == c ? 1.0 : 0.0);
-        sm[FWD ? lpos(c, r) : lpos(r, c)] = v;
+#pragma unroll
+    for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
+        const int e = threadIdx.x + GP_T * u, r = e / GP_NB, c = e % GP_NB;
+        const bool in = c < r && r < b;
+        cp8(sm + (FWD ? lpos(c, r) : lpos(r, c)), in ? Ab + (long)r * g.n + c : Ab, in);
     }
     if (threadIdx.x < GP_NB)
         sm[GP_NB * GP_LP + threadIdx.x] = threadIdx.x < b ? g.rd[j0 + threadIdx.x] : 1.0;
+    cp_wait_all();
     __syncthreads();
 }
 
 // Solves L y = v (FWD) or L^T y = v in place for the 64-vector v held by
 // the four threads (lane & ~3) + 0..3 of a warp, quarter q holding entries
-// 16 q .. 16 q + 15. Ls is the staged factor (transposed for FWD: row k
-// holds L_mk; else row k holds L_km), rd the reciprocals of its diagonal.
-// Step k: the quarter that holds entry k scales it by 1 / L_kk, the
-// shuffle hands the result to the other three, and each subtracts its
-// multiples from the entries still to come (m > k forward, m < k back).
+// 16 q .. 16 q + 15. Ls is the staged strictly lower factor (transposed for
+// FWD: row k holds L_mk; else row k holds L_km; zero elsewhere), rd the
+// reciprocals of its diagonal. Step k: the quarter that holds entry k
+// scales it by 1 / L_kk, the shuffle hands the result to the other three,
+// and every thread subtracts its multiples from all its entries: the zeros
+// of the staged factor leave the entries already solved (and entry k)
+// unchanged, so that the 64 steps carry no branch.
 template <bool FWD>
 __device__ __forceinline__ void tri_solve(double v[16], int q, const double *Ls, const double *rd)
 {
     const int base = (int)(threadIdx.x & 31) & ~3;
+    const double *lq = Ls + q * GP_QP;
 #pragma unroll
     for (int s = 0; s < GP_NB; s++) {
         const int k = FWD ? s : GP_NB - 1 - s;
         const int qk = k >> 4, ik = k & 15;
         double y = v[ik] * rd[k];
         y = __shfl_sync(0xffffffffu, y, base | qk);
-        if (q == qk)
-            v[ik] = y;
-        if (FWD ? q >= qk : q <= qk) {
-            const double *lk = Ls + k * GP_LP + q * GP_QP;
+        v[ik] = q == qk ? y : v[ik];
+        const double *lk = lq + k * GP_LP;
 #pragma unroll
-            for (int u = 0; u < 16; u += 2) {
-                const double2 l = *reinterpret_cast<const double2 *>(lk + u);
-                const int m = 16 * q + u;
-                if (FWD ? m > k : m < k)
-                    v[u] = fma(-l.x, y, v[u]);
-                if (FWD ? m + 1 > k : m + 1 < k)
-                    v[u + 1] = fma(-l.y, y, v[u + 1]);
-            }
+        for (int u = 0; u < 16; u += 2) {
+            const double2 l = *reinterpret_cast<const double2 *>(lk + u);
+            v[u] = fma(-l.x, y, v[u]);
+            v[u + 1] = fma(-l.y, y, v[u + 1]);
         }
     }
 }
 
-// The diagonal block j: the update of block column j - 1 (j > 0), then the
-// factorization in shared memory. Right-looking on the unscaled columns:
-// at step k every element (i, m), i >= m > k, takes a_ik a_mk / a_kk off;
-// the columns become final one step at a time, and each owner stores its
-// element to shared memory when its column does. Finally L_ik = a_ik /
-// sqrt(a_kk) into A's block and 1 / L_kk into rd.
+// The diagonal block j: the update of block column j - 1 (j > 0), then its
+// factorization in shared memory, 16 columns at a time. Warp 0 factors the
+// 16-column panel (rows c0 .. 63) in registers, lane l holding rows c0 + l
+// and c0 + 32 + l: at step k the pivot comes from lane k by a shuffle, the
+// column is scaled by the pivot's inverse square root, and the entries
+// L_c,k of the panel's own rows reach every lane by shuffles, so that the
+// 16 steps need no barrier. Then all warps subtract the panel's product
+// from the trailing lower triangle. Finally L into A's block and 1 / L_kk
+// into rd. The staged upper triangle is zero, so that the lanes' updates
+// of entries above the diagonal stay finite (they are never read).
 __device__ void diag_factor(const Gp &g, int j, double *sm)
 {
-    const int t = threadIdx.x, j0 = j * GP_NB, b = block_rows(g.n, j);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int j0 = j * GP_NB, b = block_rows(g.n, j);
     double *Ab = g.A + (long)j0 * g.n + j0;
     if (j > 0)
         tile_sub(Ab, g.n, b, b, GP_NB, Ab - GP_NB, g.n, 1, Ab - GP_NB, 1, g.n, sm);
     double(*S)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
-    // This thread's elements of the lower triangle (row-major order of the
-    // triangle: element e lies in row i with i (i + 1) / 2 <= e).
-    int oi[GP_OWN], om[GP_OWN];
-    double ov[GP_OWN];
+    double *rs = sm + GP_NB * GP_SP;  // 1 / L_kk
 #pragma unroll
-    for (int u = 0; u < GP_OWN; u++) {
-        const int e = t + GP_T * u;
-        int i = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
-        while ((i + 1) * (i + 2) / 2 <= e)
-            i++;
-        while (i * (i + 1) / 2 > e)
-            i--;
-        const int m = e - i * (i + 1) / 2;
-        const bool in = e < GP_NB * (GP_NB + 1) / 2;
-        oi[u] = in ? i : -1;
-        om[u] = m;
-        ov[u] = !in ? 0.0 : i < b ? Ab[(long)i * g.n + m] : (i == m ? 1.0 : 0.0);
-        // Column 0 is final from the start.
-        if (in && m == 0)
-            S[i][0] = ov[u];
+    for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
+        const int e = t + GP_T * u, r = e / GP_NB, c = e % GP_NB;
+        const bool in = c <= r && r < b;
+        cp8(&S[r][c], in ? Ab + (long)r * g.n + c : Ab, in);
     }
+    cp_wait_all();
+    // Identity beyond the block's rows.
+    if (t >= b && t < GP_NB)
+        S[t][t] = 1.0;
     __syncthreads();
-    for (int k = 0; k < GP_NB; k++) {
-        double d = S[k][k];
-        if (!(d > 0.0)) {
-            if (t == 0 && k < b)
-                *g.flag = 1;
-            d = 1.0;
-        }
-        const double r = 1.0 / d;
+    for (int p = 0; p < GP_NB / 16; p++) {
+        const int c0 = 16 * p;
+        if (warp == 0) {
+            const int r0 = c0 + lane, r1 = c0 + 32 + lane;
+            double a0[16], a1[16];
 #pragma unroll
-        for (int u = 0; u < GP_OWN; u++) {
-            const int i = oi[u], m = om[u];
-            if (i >= 0 && m > k) {
-                ov[u] = fma(-S[i][k] * r, S[m][k], ov[u]);
-                if (m == k + 1)
-                    S[i][m] = ov[u];
+            for (int c = 0; c < 16; c++) {
+                a0[c] = r0 < GP_NB ? S[r0][c0 + c] : 0.0;
+                a1[c] = r1 < GP_NB ? S[r1][c0 + c] : 0.0;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                double d = __shfl_sync(0xffffffffu, a0[k], k);
+                if (!(d > 0.0)) {
+                    if (lane == 0 && c0 + k < b)
+                        *g.flag = 1;
+                    d = 1.0;
+                }
+                const double r = rsqrt(d);
+                a0[k] *= r;
+                a1[k] *= r;
+                if (lane == 0)
+                    rs[c0 + k] = r;
+#pragma unroll
+                for (int c = k + 1; c < 16; c++) {
+                    const double lc = __shfl_sync(0xffffffffu, a0[k], c);
+                    a0[c] = fma(-a0[k], lc, a0[c]);
+                    a1[c] = fma(-a1[k], lc, a1[c]);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+                if (r0 < GP_NB)
+                    S[r0][c0 + c] = a0[c];
+                if (r1 < GP_NB)
+                    S[r1][c0 + c] = a1[c];
+            }
+        }
+        __syncthreads();
+        // Trailing lower triangle: S_im -= sum_k L_i,k L_m,k over the panel.
+        const int t0 = c0 + 16, R = GP_NB - t0;
+        for (int e = t; e < R * R; e += GP_T) {
+            const int i = t0 + e / R, m = t0 + e % R;
+            if (m <= i) {
+                double acc = S[i][m];
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    acc = fma(-S[i][c0 + k], S[m][c0 + k], acc);
+                S[i][m] = acc;
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int u = 0; u < GP_OWN; u++) {
-        const int i = oi[u], m = om[u];
-        if (i >= 0 && i < b) {
-            double d = S[m][m];
-            d = d > 0.0 ? d : 1.0;
-            Ab[(long)i * g.n + m] = ov[u] * rsqrt(d);
-        }
+    for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
+        const int e = t + GP_T * u, r = e / GP_NB, c = e % GP_NB;
+        if (c <= r && r < b)
+            Ab[(long)r * g.n + c] = S[r][c];
     }
-    if (t < b) {
-        const double d = S[t][t];
-        g.rd[j0 + t] = rsqrt(d > 0.0 ? d : 1.0);
-    }
+    if (t < b)
+        g.rd[j0 + t] = rs[t];
 }
 
 // Step j of the factorization: CTA 0 the diagonal block; CTAs 1 .. T - 1
