@@ -10,26 +10,27 @@
 //
 // Blocks of 64 rows. The factor overwrites the lower triangle of the
 // working matrix A in place; the right-hand sides F become Z, then X, in
-// place in R. Three kernels, every CTA one 64 x 64 block of work:
+// place in R. Three kernels:
 //   gp_factor_k (j)  CTA 0: the diagonal block j receives the update of
-//                    block column j - 1 and is factored (L_jj and the
-//                    reciprocals 1 / L_kk); the other CTAs apply the same
+//                    block column j - 1 and is factored (L_jj, the
+//                    reciprocals 1 / L_kk and the inverse L_jj^-1, by
+//                    block inversion); the other CTAs apply the same
 //                    update to the rest of the trailing matrix (lower
 //                    blocks) and to the right-hand sides below block j-1;
-//   gp_panel_k (j)   the blocks below the diagonal, L_ij = A_ij L_jj^-T, and
-//                    Z_j = L_jj^-1 F_j, by forward substitution;
+//   gp_panel_k (j)   the blocks below the diagonal, L_ij = A_ij L_jj^-T,
+//                    and Z_j = L_jj^-1 F_j, as block products with the
+//                    inverse L_jj^-1 that the diagonal factor stored;
 //   gp_back_k (j)    from the last block up: Z_j receives the update of
-//                    X_{j+1} and is solved against L_jj^T (X_j, also
-//                    rounded to float into the output), while the other
-//                    CTAs apply X_{j+1}'s update to Z_i, i < j.
-// Each 64-vector of a substitution is held by four threads of a warp (16
-// entries each); the entry solved at a step is passed to the other three
-// by a shuffle, so the 64 steps need no barrier and, with the staged
-// factor zero on and above its diagonal, no branch. The diagonal block is
-// factored 16 columns at a time, each panel by one warp in registers.
-// Operands are staged in shared memory by asynchronous copies. Every
-// chain here is latency-bound (one pivot after another), so the kernels
-// are written for short dependency chains and few instructions per step.
+//                    X_{j+1} and X_j = L_jj^-T Z_j (a block product with
+//                    the stored inverse; also rounded to float into the
+//                    output), while the other CTAs apply X_{j+1}'s update
+//                    to Z_i, i < j.
+// The diagonal block is factored 16 columns at a time, each panel by one
+// warp in registers, and inverted by block inversion (a 16-step chain);
+// everything else is 64 x 64 block products. Operands are staged in shared
+// memory by asynchronous copies. Every chain here is latency-bound (one
+// pivot after another), so the kernels are written for short dependency
+// chains and few instructions per step.
 // A non-positive pivot sets *flag (the reference stops with "kernel not
 // positive definite"); the host reads it after the tile.
 
@@ -43,18 +44,16 @@ namespace {
 
 constexpr int GP_T = 256;         // threads per CTA
 constexpr int GP_SP = GP_NB + 1;  // pitch of the staged product operands and of the block
-// A staged triangular factor: row k holds four quarters of 16 entries,
-// each padded to 18 doubles, so that the four quarters a warp reads at
-// one step (16-byte loads) fall in different banks.
-constexpr int GP_QP = 18, GP_LP = 4 * GP_QP;
-constexpr size_t GP_SMEM = 2 * GP_NB * GP_SP * sizeof(double);
-static_assert((size_t)GP_NB * GP_LP * sizeof(double) + GP_NB * sizeof(double) <= GP_SMEM,
-              "the staged factor fits the operand staging");
+// Staging: two padded 64 x 64 blocks, then (diagonal factor) 64
+// reciprocals and a 32 x 32 scratch block.
+constexpr int GP_RS = 2 * GP_NB * GP_SP, GP_US = GP_RS + GP_NB;
+constexpr size_t GP_SMEM = (GP_US + 32 * 32) * sizeof(double);
 
 struct Gp {
     double *A;   // n x n, pitch n: K + noise I (lower triangle), then L
     double *R;   // n x d: F, then Z, then X
     double *rd;  // n: 1 / L_kk
+    double *Li;  // nb blocks of 64 x 64: the inverses L_jj^-1, row-major
     float *X;    // n x d: X rounded to float
     int n, d, nb, db;
     int *flag;
@@ -80,14 +79,18 @@ __device__ __forceinline__ void cp_wait_all()
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// C (rows x cols, pitch ldc) -= P Q over kd terms, P(r, k) = P[r psr + k
+// C (rows x cols, pitch ldc) -= P Q over kd terms (C = P Q with assign,
+// and then also Cf = C in float where Cf is given), P(r, k) = P[r psr + k
 // psk], Q(k, c) = Q[k qsk + c qsc]; operand entries beyond rows, cols or kd
 // read as zero. Both operands are staged k-major in shared memory by
 // asynchronous copies (all 32 of a thread in flight at once, each operand
-// read along its unit-stride dimension); the thread's 16 elements of C are
-// read while they land; every thread accumulates a 4 x 4 block of C.
+// read along its unit-stride dimension) before C is written, so that Q may
+// be C itself; the thread's 16 elements of C are read while they land;
+// every thread accumulates a 4 x 4 block of C.
+template <bool ASSIGN = false>
 __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const double *P,
-                         long psr, long psk, const double *Q, long qsk, long qsc, double *sm)
+                         long psr, long psk, const double *Q, long qsk, long qsc, double *sm,
+                         float *Cf = nullptr)
 {
     double(*Ps)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
     double(*Qs)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
@@ -111,7 +114,7 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             const int r = ty + 16 * i, cc = tx + 16 * c;
-            c0[i][c] = r < rows && cc < cols ? C[r * ldc + cc] : 0.0;
+            c0[i][c] = !ASSIGN && r < rows && cc < cols ? C[r * ldc + cc] : 0.0;
         }
     cp_wait_all();
     __syncthreads();
@@ -127,7 +130,7 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
         for (int i = 0; i < 4; i++)
 #pragma unroll
             for (int c = 0; c < 4; c++)
-                c0[i][c] = fma(-a[i], b[c], c0[i][c]);
+                c0[i][c] = fma(ASSIGN ? a[i] : -a[i], b[c], c0[i][c]);
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -135,8 +138,11 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             const int cc = tx + 16 * c;
-            if (r < rows && cc < cols)
+            if (r < rows && cc < cols) {
                 C[r * ldc + cc] = c0[i][c];
+                if (Cf)
+                    Cf[r * ldc + cc] = (float)c0[i][c];
+            }
         }
     }
     // The staging may be reused, and C's new values are visible to the
@@ -144,63 +150,63 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
     __syncthreads();
 }
 
-// Position of entry m of row k in a staged triangular factor.
-__device__ __forceinline__ int lpos(int k, int m)
+// The inverse of the 64 x 64 lower factor L (in S, 1 / L_kk in rs, the
+// identity beyond the block's rows) into Li (row-major, zeros above the
+// diagonal), by block inversion, inv([[A, 0], [B, C]]) = [[A^-1, 0],
+// [-C^-1 B A^-1, C^-1]]: the four 16 x 16 diagonal blocks by substitution
+// (a thread per column, 16 steps), then the 16 -> 32 and 32 -> 64 joins as
+// block products over all threads. The chain is 16 steps long instead of
+// 64, so that the blocks below the diagonal can be multiplied by the
+// inverse instead of substituted.
+__device__ void invert_factor(double (*S)[GP_SP], const double *rs, double *sm, double *Li)
 {
-    return k * GP_LP + (m >> 4) * GP_QP + (m & 15);
-}
-
-// Stages the strictly lower part of the factor L_jj (A's block (j, j);
-// zeros on and above the diagonal and beyond the block's b rows) into sm:
-// transposed (row k = column k of L) for the forward substitution, as is
-// for the backward one; then the reciprocals 1 / L_kk (1 beyond b) at sm +
-// 64 GP_LP.
-template <bool FWD>
-__device__ void stage_factor(const Gp &g, int j, double *sm)
-{
-    const int j0 = j * GP_NB, b = block_rows(g.n, j);
-    const double *Ab = g.A + (long)j0 * g.n + j0;
-#pragma unroll
-    for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
-        const int e = threadIdx.x + GP_T * u, r = e / GP_NB, c = e % GP_NB;
-        const bool in = c < r && r < b;
-        cp8(sm + (FWD ? lpos(c, r) : lpos(r, c)), in ? Ab + (long)r * g.n + c : Ab, in);
-    }
-    if (threadIdx.x < GP_NB)
-        sm[GP_NB * GP_LP + threadIdx.x] = threadIdx.x < b ? g.rd[j0 + threadIdx.x] : 1.0;
-    cp_wait_all();
+    const int t = threadIdx.x;
+    double(*T)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
+    double(*U)[32] = reinterpret_cast<double(*)[32]>(sm + GP_US);
+    for (int e = t; e < GP_NB * GP_SP; e += GP_T)
+        (&T[0][0])[e] = 0.0;
     __syncthreads();
-}
-
-// Solves L y = v (FWD) or L^T y = v in place for the 64-vector v held by
-// the four threads (lane & ~3) + 0..3 of a warp, quarter q holding entries
-// 16 q .. 16 q + 15. Ls is the staged strictly lower factor (transposed for
-// FWD: row k holds L_mk; else row k holds L_km; zero elsewhere), rd the
-// reciprocals of its diagonal. Step k: the quarter that holds entry k
-// scales it by 1 / L_kk, the shuffle hands the result to the other three,
-// and every thread subtracts its multiples from all its entries: the zeros
-// of the staged factor leave the entries already solved (and entry k)
-// unchanged, so that the 64 steps carry no branch.
-template <bool FWD>
-__device__ __forceinline__ void tri_solve(double v[16], int q, const double *Ls, const double *rd)
-{
-    const int base = (int)(threadIdx.x & 31) & ~3;
-    const double *lq = Ls + q * GP_QP;
+    if (t < GP_NB) {
+        // Diagonal block p, column c: D y = e_c.
+        const int p = t >> 4, c = t & 15, o = 16 * p;
+        double y[16];
 #pragma unroll
-    for (int s = 0; s < GP_NB; s++) {
-        const int k = FWD ? s : GP_NB - 1 - s;
-        const int qk = k >> 4, ik = k & 15;
-        double y = v[ik] * rd[k];
-        y = __shfl_sync(0xffffffffu, y, base | qk);
-        v[ik] = q == qk ? y : v[ik];
-        const double *lk = lq + k * GP_LP;
+        for (int m = 0; m < 16; m++) {
+            double acc = m == c ? 1.0 : 0.0;
 #pragma unroll
-        for (int u = 0; u < 16; u += 2) {
-            const double2 l = *reinterpret_cast<const double2 *>(lk + u);
-            v[u] = fma(-l.x, y, v[u]);
-            v[u + 1] = fma(-l.y, y, v[u + 1]);
+            for (int q = 0; q < m; q++)
+                acc = fma(-S[o + m][o + q], y[q], acc);
+            y[m] = acc * rs[o + m];
         }
+#pragma unroll
+        for (int m = 0; m < 16; m++)
+            T[o + m][o + c] = y[m];
     }
+    __syncthreads();
+    // Joins: width w (16, then 32), pairs of diagonal blocks at o and o + w.
+    for (int w = 16; w < GP_NB; w *= 2) {
+        const int pairs = GP_NB / (2 * w), outs = pairs * w * w;
+        // U = B A^-1 (B = L below the first block of the pair).
+        for (int e = t; e < outs; e += GP_T) {
+            const int pr = e / (w * w), r = (e / w) % w, c = e % w, o = 2 * w * pr;
+            double acc = 0.0;
+            for (int k = c; k < w; k++)
+                acc = fma(S[o + w + r][o + k], T[o + k][o + c], acc);
+            U[pr * w + r][c] = acc;
+        }
+        __syncthreads();
+        // The lower-left block of the pair's inverse, -C^-1 U.
+        for (int e = t; e < outs; e += GP_T) {
+            const int pr = e / (w * w), r = (e / w) % w, c = e % w, o = 2 * w * pr;
+            double acc = 0.0;
+            for (int k = 0; k <= r; k++)
+                acc = fma(T[o + w + r][o + w + k], U[pr * w + k][c], acc);
+            T[o + w + r][o + c] = -acc;
+        }
+        __syncthreads();
+    }
+    for (int e = t; e < GP_NB * GP_NB; e += GP_T)
+        Li[e] = T[e >> 6][e & 63];
 }
 
 // The diagonal block j: the update of block column j - 1 (j > 0), then its
@@ -221,7 +227,7 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
     if (j > 0)
         tile_sub(Ab, g.n, b, b, GP_NB, Ab - GP_NB, g.n, 1, Ab - GP_NB, 1, g.n, sm);
     double(*S)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
-    double *rs = sm + GP_NB * GP_SP;  // 1 / L_kk
+    double *rs = sm + GP_RS;  // 1 / L_kk
 #pragma unroll
     for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
         const int e = t + GP_T * u, r = e / GP_NB, c = e % GP_NB;
@@ -294,6 +300,7 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
     }
     if (t < b)
         g.rd[j0 + t] = rs[t];
+    invert_factor(S, rs, sm, g.Li + (long)j * GP_NB * GP_NB);
 }
 
 // Step j of the factorization: CTA 0 the diagonal block; CTAs 1 .. T - 1
@@ -330,48 +337,34 @@ __global__ void __launch_bounds__(GP_T) gp_factor_k(Gp g, int j)
              g.A + (long)i0 * g.n + p0, g.n, 1, g.R + (long)p0 * g.d + c0, g.d, 1, gp_sm);
 }
 
-// Block column j: CTAs 0 .. nb - j - 2 the rows of the blocks below the
-// diagonal (L_ij = A_ij L_jj^-T: each row solved against L_jj); then one
-// CTA per 64 right-hand-side columns, Z_j = L_jj^-1 F_j.
+// Block column j, one 64 x 64 block product per CTA with the inverse that
+// the diagonal factor stored: CTAs 0 .. nb - j - 2 the blocks below the
+// diagonal, L_ij = A_ij L_jj^-T; then one CTA per 64 right-hand-side
+// columns, Z_j = L_jj^-1 F_j. Each product overwrites its own operand (the
+// operands are staged before the result is written).
 __global__ void __launch_bounds__(GP_T) gp_panel_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
-    stage_factor<true>(g, j, gp_sm);
-    const int t = threadIdx.x, q = t & 3, vi = t >> 2;
     const int j0 = j * GP_NB, b = block_rows(g.n, j), nk = g.nb - 1 - j;
-    const double *rd = gp_sm + GP_NB * GP_LP;
-    double v[16];
+    const double *li = g.Li + (long)j * GP_NB * GP_NB;
     if ((int)blockIdx.x < nk) {
-        const int i = j + 1 + blockIdx.x, rows = block_rows(g.n, i);
-        double *row = g.A + (long)(i * GP_NB + vi) * g.n + j0 + 16 * q;
-        // Scalar accesses: the rows are 16-byte aligned only for even n.
-        const bool in = vi < rows;
-#pragma unroll
-        for (int u = 0; u < 16; u++)
-            v[u] = in ? row[u] : 0.0;
-        tri_solve<true>(v, q, gp_sm, rd);
-        if (in)
-#pragma unroll
-            for (int u = 0; u < 16; u++)
-                row[u] = v[u];
+        const int i = j + 1 + (int)blockIdx.x;
+        double *blk = g.A + (long)i * GP_NB * g.n + j0;
+        // (L_jj^-T)_kc = Li[c][k].
+        tile_sub<true>(blk, g.n, block_rows(g.n, i), GP_NB, GP_NB, blk, g.n, 1, li, 1, GP_NB,
+                       gp_sm);
         return;
     }
-    const int c = ((int)blockIdx.x - nk) * GP_NB + vi;
-    double *col = g.R + (long)(j0 + 16 * q) * g.d + c;
-#pragma unroll
-    for (int u = 0; u < 16; u++)
-        v[u] = c < g.d && 16 * q + u < b ? col[(long)u * g.d] : 0.0;
-    tri_solve<true>(v, q, gp_sm, rd);
-#pragma unroll
-    for (int u = 0; u < 16; u++)
-        if (c < g.d && 16 * q + u < b)
-            col[(long)u * g.d] = v[u];
+    const int c0 = ((int)blockIdx.x - nk) * GP_NB;
+    double *zj = g.R + (long)j0 * g.d + c0;
+    tile_sub<true>(zj, g.d, b, min(GP_NB, g.d - c0), b, li, GP_NB, 1, zj, g.d, 1, gp_sm);
 }
 
 // Backward step j: CTAs 0 .. db - 1 take Z_j's 64-column blocks, subtract
-// L_j+1,j^T X_j+1 (j < nb - 1) and solve L_jj^T X_j = Z_j, storing X_j in
-// double and in float; the other CTAs subtract L_j+1,i^T X_j+1 from the
-// blocks Z_i, i < j.
+// L_j+1,j^T X_j+1 (j < nb - 1) and multiply by the inverse, X_j = L_jj^-T
+// Z_j, storing X_j in double and in float; the other CTAs subtract L_j+1,i^T
+// X_j+1 from the blocks Z_i, i < j. Two block products per step on the
+// critical path, no substitution.
 __global__ void __launch_bounds__(GP_T) gp_back_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
@@ -384,24 +377,14 @@ __global__ void __launch_bounds__(GP_T) gp_back_k(Gp g, int j)
                  g.A + (long)k0 * g.n + i0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
         return;
     }
-    const int c0 = (int)blockIdx.x * GP_NB;
+    const int c0 = (int)blockIdx.x * GP_NB, cols = min(GP_NB, g.d - c0);
+    double *zj = g.R + (long)j0 * g.d + c0;
     if (next)
-        tile_sub(g.R + (long)j0 * g.d + c0, g.d, b, min(GP_NB, g.d - c0), kd,
-                 g.A + (long)k0 * g.n + j0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
-    stage_factor<false>(g, j, gp_sm);
-    const int t = threadIdx.x, q = t & 3, c = c0 + (t >> 2);
-    double v[16];
-    const long off = (long)(j0 + 16 * q) * g.d + c;
-#pragma unroll
-    for (int u = 0; u < 16; u++)
-        v[u] = c < g.d && 16 * q + u < b ? g.R[off + (long)u * g.d] : 0.0;
-    tri_solve<false>(v, q, gp_sm, gp_sm + GP_NB * GP_LP);
-#pragma unroll
-    for (int u = 0; u < 16; u++)
-        if (c < g.d && 16 * q + u < b) {
-            g.R[off + (long)u * g.d] = v[u];
-            g.X[off + (long)u * g.d] = (float)v[u];
-        }
+        tile_sub(zj, g.d, b, cols, kd, g.A + (long)k0 * g.n + j0, 1, g.n,
+                 g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
+    // (L_jj^-T)_mk = Li[k][m].
+    tile_sub<true>(zj, g.d, b, cols, b, g.Li + (long)j * GP_NB * GP_NB, 1, GP_NB, zj, g.d, 1,
+                   gp_sm, g.X + (long)j0 * g.d + c0);
 }
 
 // A = K + noise I (lower triangle in double), R = F in double.
@@ -439,10 +422,11 @@ bool opt_in_all()
 
 }  // namespace
 
-// Work: A (n x n), R (n x d) and the n reciprocals, in doubles.
+// Work: A (n x n), R (n x d), the n reciprocals and the block inverses, in
+// doubles.
 size_t gp_work_doubles(int n, int d)
 {
-    return (size_t)n * n + (size_t)n * d + (size_t)n;
+    return (size_t)n * n + (size_t)n * d + (size_t)n + (size_t)cdiv(n, GP_NB) * GP_NB * GP_NB;
 }
 
 void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int d,
@@ -454,6 +438,7 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int
     g.A = work;
     g.R = work + (size_t)n * n;
     g.rd = g.R + (size_t)n * d;
+    g.Li = g.rd + n;
     g.X = X_out;
     g.n = n;
     g.d = d;
