@@ -158,53 +158,79 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
 // block products over all threads. The chain is 16 steps long instead of
 // 64, so that the blocks below the diagonal can be multiplied by the
 // inverse instead of substituted.
+// One join of the block inversion at width W: for each pair of W x W
+// diagonal blocks of the inverse at o and o + W, the block below them,
+// -C^-1 (B A^-1), with B the factor's block there. Every thread computes
+// NC columns of one row, NC independent sums.
+template <int W>
+__device__ __forceinline__ void invert_join(double (*S)[GP_SP], double (*T)[GP_SP],
+                                            double (*U)[32])
+{
+    constexpr int P = GP_NB / (2 * W), NC = P * W * W / GP_T, PER = W * W / NC;
+    const int t = threadIdx.x, pr = t / PER, rem = t % PER, r = rem / (W / NC),
+              c0 = (rem % (W / NC)) * NC, o = 2 * W * pr;
+    double acc[NC];
+#pragma unroll
+    for (int i = 0; i < NC; i++)
+        acc[i] = 0.0;
+#pragma unroll
+    for (int k = 0; k < W; k++) {
+        const double bk = S[o + W + r][o + k];
+#pragma unroll
+        for (int i = 0; i < NC; i++)
+            acc[i] = fma(bk, T[o + k][o + c0 + i], acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < NC; i++)
+        U[pr * W + r][c0 + i] = acc[i];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NC; i++)
+        acc[i] = 0.0;
+#pragma unroll
+    for (int k = 0; k < W; k++) {
+        const double ck = T[o + W + r][o + W + k];
+#pragma unroll
+        for (int i = 0; i < NC; i++)
+            acc[i] = fma(ck, U[pr * W + k][c0 + i], acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < NC; i++)
+        T[o + W + r][o + c0 + i] = -acc[i];
+    __syncthreads();
+}
+
 __device__ void invert_factor(double (*S)[GP_SP], const double *rs, double *sm, double *Li)
 {
     const int t = threadIdx.x;
     double(*T)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
     double(*U)[32] = reinterpret_cast<double(*)[32]>(sm + GP_US);
+    // Zeros above the diagonal blocks as they are built.
     for (int e = t; e < GP_NB * GP_SP; e += GP_T)
         (&T[0][0])[e] = 0.0;
     __syncthreads();
     if (t < GP_NB) {
-        // Diagonal block p, column c: D y = e_c.
+        // Diagonal block p, column c: D y = e_c, right-looking (each step
+        // one multiply, then independent updates of the later entries).
         const int p = t >> 4, c = t & 15, o = 16 * p;
         double y[16];
 #pragma unroll
-        for (int m = 0; m < 16; m++) {
-            double acc = m == c ? 1.0 : 0.0;
+        for (int m = 0; m < 16; m++)
+            y[m] = m == c ? 1.0 : 0.0;
 #pragma unroll
-            for (int q = 0; q < m; q++)
-                acc = fma(-S[o + m][o + q], y[q], acc);
-            y[m] = acc * rs[o + m];
+        for (int m = 0; m < 16; m++) {
+            y[m] *= rs[o + m];
+#pragma unroll
+            for (int q = m + 1; q < 16; q++)
+                y[q] = fma(-S[o + q][o + m], y[m], y[q]);
         }
 #pragma unroll
         for (int m = 0; m < 16; m++)
             T[o + m][o + c] = y[m];
     }
     __syncthreads();
-    // Joins: width w (16, then 32), pairs of diagonal blocks at o and o + w.
-    for (int w = 16; w < GP_NB; w *= 2) {
-        const int pairs = GP_NB / (2 * w), outs = pairs * w * w;
-        // U = B A^-1 (B = L below the first block of the pair).
-        for (int e = t; e < outs; e += GP_T) {
-            const int pr = e / (w * w), r = (e / w) % w, c = e % w, o = 2 * w * pr;
-            double acc = 0.0;
-            for (int k = c; k < w; k++)
-                acc = fma(S[o + w + r][o + k], T[o + k][o + c], acc);
-            U[pr * w + r][c] = acc;
-        }
-        __syncthreads();
-        // The lower-left block of the pair's inverse, -C^-1 U.
-        for (int e = t; e < outs; e += GP_T) {
-            const int pr = e / (w * w), r = (e / w) % w, c = e % w, o = 2 * w * pr;
-            double acc = 0.0;
-            for (int k = 0; k <= r; k++)
-                acc = fma(T[o + w + r][o + w + k], U[pr * w + k][c], acc);
-            T[o + w + r][o + c] = -acc;
-        }
-        __syncthreads();
-    }
+    invert_join<16>(S, T, U);
+    invert_join<32>(S, T, U);
     for (int e = t; e < GP_NB * GP_NB; e += GP_T)
         Li[e] = T[e >> 6][e & 63];
 }
@@ -249,6 +275,9 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
                 a0[c] = r0 < GP_NB ? S[r0][c0 + c] : 0.0;
                 a1[c] = r1 < GP_NB ? S[r1][c0 + c] : 0.0;
             }
+            // The scaled column's entries of the panel's own rows pass
+            // through shared memory (two buffers, one warp barrier a step).
+            double *colb = sm + GP_US;
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 double d = __shfl_sync(0xffffffffu, a0[k], k);
@@ -262,9 +291,13 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
                 a1[k] *= r;
                 if (lane == 0)
                     rs[c0 + k] = r;
+                double *cb = colb + 16 * (k & 1);
+                if (lane < 16)
+                    cb[lane] = a0[k];
+                __syncwarp();
 #pragma unroll
                 for (int c = k + 1; c < 16; c++) {
-                    const double lc = __shfl_sync(0xffffffffu, a0[k], c);
+                    const double lc = cb[c];
                     a0[c] = fma(-a0[k], lc, a0[c]);
                     a1[c] = fma(-a1[k], lc, a1[c]);
                 }
@@ -308,7 +341,7 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
 // matrix; then the right-hand-side blocks (i, column block c), i >= j, all
 // with the update of block column j - 1 (A -= L_i,j-1 L_k,j-1^T, F_i -=
 // L_i,j-1 Z_j-1).
-__global__ void __launch_bounds__(GP_T) gp_factor_k(Gp g, int j)
+__global__ void __launch_bounds__(GP_T, 1) gp_factor_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
     if (blockIdx.x == 0) {
