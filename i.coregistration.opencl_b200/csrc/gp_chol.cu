@@ -18,13 +18,16 @@
 //                    update to the rest of the trailing matrix (lower
 //                    blocks) and to the right-hand sides below block j-1;
 //   gp_panel_k (j)   the blocks below the diagonal, L_ij = A_ij L_jj^-T,
-//                    and Z_j = L_jj^-1 F_j, as block products with the
-//                    inverse L_jj^-1 that the diagonal factor stored;
+//                    and Z_j = L_jj^-1 F_j, as products with the inverse
+//                    L_jj^-1 that the diagonal factor stored, each block's
+//                    product split over four CTAs;
 //   gp_back_k (j)    from the last block up: Z_j receives the update of
-//                    X_{j+1} and X_j = L_jj^-T Z_j (a block product with
-//                    the stored inverse; also rounded to float into the
+//                    X_{j+1} and X_j = L_jj^-T Z_j (products with the
+//                    operands staged in one round, the second with the
+//                    stored inverse; also rounded to float into the
 //                    output), while the other CTAs apply X_{j+1}'s update
-//                    to Z_i, i < j.
+//                    to Z_i, i < j (Z_j in 16-column slabs, four CTAs a
+//                    block).
 // The diagonal block is factored 16 columns at a time, each panel by one
 // warp in registers, and inverted by block inversion (a 16-step chain);
 // everything else is 64 x 64 block products. Operands are staged in shared
@@ -158,6 +161,67 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
 // block products over all threads. The chain is 16 steps long instead of
 // 64, so that the blocks below the diagonal can be multiplied by the
 // inverse instead of substituted.
+// A slab of a 64 x 64 block product on one CTA, four outputs a thread:
+// C (R x CC, CC = 1024 / R, pitch ldc) -= P Q over kd terms (C = P Q with
+// ASSIGN, and then Cf = C in float where Cf is given), P(r, k) = P[r psr +
+// k psk] (R x 64), Q(k, c) = Q[k qsk + c qsc] (64 x CC); entries beyond
+// rows, cols or kd read as zero. R = 64 with CC = 16 (a column slab) or R =
+// 16 with CC = 64 (a row slab): a quarter of the block's work, so that four
+// CTAs share one block product and each finishes four times sooner. The
+// slab reads only its own rows of P and columns of Q, so that a product
+// may overwrite its operand slab by slab.
+template <int R, bool ASSIGN>
+__device__ void slab_prod(double *C, long ldc, int rows, int cols, int kd, const double *P,
+                          long psr, long psk, const double *Q, long qsk, long qsc, double *sm,
+                          float *Cf = nullptr)
+{
+    constexpr int CC = GP_NB * GP_NB / 4 / R, RP = R + 1, CP = CC + 1, RT = GP_T / CC;
+    double *Ps = sm;            // Ps[k * RP + r]
+    double *Qs = sm + GP_NB * RP;  // Qs[k * CP + c]
+    const int t = threadIdx.x;
+    const bool pk = psk == 1, qk = qsk == 1;
+#pragma unroll
+    for (int u = 0; u < R * GP_NB / GP_T; u++) {
+        const int e = t + GP_T * u;
+        const int r = pk ? e / GP_NB : e % R, k = pk ? e % GP_NB : e / R;
+        const bool in = r < rows && k < kd;
+        cp8(Ps + k * RP + r, in ? P + r * psr + k * psk : P, in);
+    }
+#pragma unroll
+    for (int u = 0; u < CC * GP_NB / GP_T; u++) {
+        const int e = t + GP_T * u;
+        const int c = qk ? e / GP_NB : e % CC, k = qk ? e % GP_NB : e / CC;
+        const bool in = c < cols && k < kd;
+        cp8(Qs + k * CP + c, in ? Q + k * qsk + c * qsc : Q, in);
+    }
+    const int tx = t % CC, ty = t / CC;
+    double acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = ty + RT * i;
+        acc[i] = !ASSIGN && r < rows && tx < cols ? C[r * ldc + tx] : 0.0;
+    }
+    cp_wait_all();
+    __syncthreads();
+#pragma unroll 16
+    for (int k = 0; k < GP_NB; k++) {
+        const double q = Qs[k * CP + tx];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            acc[i] = fma(ASSIGN ? Ps[k * RP + ty + RT * i] : -Ps[k * RP + ty + RT * i], q, acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = ty + RT * i;
+        if (r < rows && tx < cols) {
+            C[r * ldc + tx] = acc[i];
+            if (Cf)
+                Cf[r * ldc + tx] = (float)acc[i];
+        }
+    }
+    __syncthreads();
+}
+
 // One join of the block inversion at width W: for each pair of W x W
 // diagonal blocks of the inverse at o and o + W, the block below them,
 // -C^-1 (B A^-1), with B the factor's block there. Every thread computes
@@ -370,54 +434,129 @@ __global__ void __launch_bounds__(GP_T, 1) gp_factor_k(Gp g, int j)
              g.A + (long)i0 * g.n + p0, g.n, 1, g.R + (long)p0 * g.d + c0, g.d, 1, gp_sm);
 }
 
-// Block column j, one 64 x 64 block product per CTA with the inverse that
-// the diagonal factor stored: CTAs 0 .. nb - j - 2 the blocks below the
-// diagonal, L_ij = A_ij L_jj^-T; then one CTA per 64 right-hand-side
-// columns, Z_j = L_jj^-1 F_j. Each product overwrites its own operand (the
-// operands are staged before the result is written).
+// Block column j, products with the inverse that the diagonal factor
+// stored, each block split over four CTAs (blockIdx.y = slab): CTAs 0 ..
+// nb - j - 2 the blocks below the diagonal, L_ij = A_ij L_jj^-T (16-row
+// slabs, each overwriting its own rows); then one CTA per 64
+// right-hand-side columns, Z_j = L_jj^-1 F_j (16-column slabs).
 __global__ void __launch_bounds__(GP_T) gp_panel_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
-    const int j0 = j * GP_NB, b = block_rows(g.n, j), nk = g.nb - 1 - j;
+    const int j0 = j * GP_NB, b = block_rows(g.n, j), nk = g.nb - 1 - j, sl = 16 * blockIdx.y;
     const double *li = g.Li + (long)j * GP_NB * GP_NB;
     if ((int)blockIdx.x < nk) {
-        const int i = j + 1 + (int)blockIdx.x;
-        double *blk = g.A + (long)i * GP_NB * g.n + j0;
+        const int i = j + 1 + (int)blockIdx.x, rows = block_rows(g.n, i) - sl;
+        if (rows <= 0)
+            return;
+        double *blk = g.A + (long)(i * GP_NB + sl) * g.n + j0;
         // (L_jj^-T)_kc = Li[c][k].
-        tile_sub<true>(blk, g.n, block_rows(g.n, i), GP_NB, GP_NB, blk, g.n, 1, li, 1, GP_NB,
-                       gp_sm);
+        slab_prod<16, true>(blk, g.n, min(16, rows), GP_NB, GP_NB, blk, g.n, 1, li, 1, GP_NB,
+                            gp_sm);
         return;
     }
-    const int c0 = ((int)blockIdx.x - nk) * GP_NB;
+    const int c0 = ((int)blockIdx.x - nk) * GP_NB + sl;
+    if (c0 >= g.d)
+        return;
     double *zj = g.R + (long)j0 * g.d + c0;
-    tile_sub<true>(zj, g.d, b, min(GP_NB, g.d - c0), b, li, GP_NB, 1, zj, g.d, 1, gp_sm);
+    slab_prod<64, true>(zj, g.d, b, min(16, g.d - c0), b, li, GP_NB, 1, zj, g.d, 1, gp_sm);
 }
 
-// Backward step j: CTAs 0 .. db - 1 take Z_j's 64-column blocks, subtract
-// L_j+1,j^T X_j+1 (j < nb - 1) and multiply by the inverse, X_j = L_jj^-T
-// Z_j, storing X_j in double and in float; the other CTAs subtract L_j+1,i^T
-// X_j+1 from the blocks Z_i, i < j. Two block products per step on the
-// critical path, no substitution.
+// Shared memory of the backward kernel: two staged 64 x 64 blocks and two
+// 64 x 16 slabs.
+constexpr int GP_SL = 17;  // pitch of a staged 16-column slab
+constexpr size_t GP_SMEM_BACK = (2 * GP_NB * GP_SP + 2 * GP_NB * GP_SL) * sizeof(double);
+
+// X_j = L_jj^-T (Z_j - L_j+1,j^T X_j+1) for the 16 columns from c0 (no
+// update for the last block), stored in double and in float. One round of
+// asynchronous copies stages L_j+1,j, the inverse and the slab of X_j+1
+// while the slab of Z_j comes into registers; the updated slab goes through
+// shared memory into the second product. Thread (ty, tx): rows ty + 16 i,
+// column tx.
+__device__ void back_slab(const Gp &g, int j, int c0, double *sm)
+{
+    const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+    const int j0 = j * GP_NB, b = block_rows(g.n, j), cols = min(16, g.d - c0);
+    const bool next = j + 1 < g.nb;
+    const int k0 = j0 + GP_NB, kd = next ? block_rows(g.n, j + 1) : 0;
+    double(*Ps)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
+    double(*Ls)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
+    double(*Qs)[GP_SL] = reinterpret_cast<double(*)[GP_SL]>(sm + 2 * GP_NB * GP_SP);
+    double(*Zs)[GP_SL] = reinterpret_cast<double(*)[GP_SL]>(sm + 2 * GP_NB * GP_SP + GP_NB * GP_SL);
+    const double *li = g.Li + (long)j * GP_NB * GP_NB;
+    double *zj = g.R + (long)j0 * g.d + c0;
+#pragma unroll
+    for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
+        const unsigned e = t + GP_T * u;
+        const int k = (int)(e >> 6), m = (int)(e & 63);
+        // Ps[k][m] = L_j+1,j[k][m], Ls[k][m] = Li[k][m].
+        const bool in = k < kd;
+        cp8(&Ps[k][m], in ? g.A + (long)(k0 + k) * g.n + j0 + m : g.A, in);
+        cp8(&Ls[k][m], li + e, true);
+    }
+#pragma unroll
+    for (int u = 0; u < GP_NB * 16 / GP_T; u++) {
+        const int e = t + GP_T * u, k = e / 16, c = e % 16;
+        const bool in = k < kd && c < cols;
+        cp8(&Qs[k][c], in ? g.R + (long)(k0 + k) * g.d + c0 + c : g.R, in);
+    }
+    double z[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = ty + 16 * i;
+        z[i] = r < b && tx < cols ? zj[(long)r * g.d + tx] : 0.0;
+    }
+    cp_wait_all();
+    __syncthreads();
+    if (next) {
+#pragma unroll 16
+        for (int k = 0; k < GP_NB; k++) {
+            const double q = Qs[k][tx];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                z[i] = fma(-Ps[k][ty + 16 * i], q, z[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        Zs[ty + 16 * i][tx] = z[i];
+    __syncthreads();
+    double x[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll 16
+    for (int k = 0; k < GP_NB; k++) {
+        const double q = Zs[k][tx];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            x[i] = fma(Ls[k][ty + 16 * i], q, x[i]);
+    }
+    float *xf = g.X + (long)j0 * g.d + c0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = ty + 16 * i;
+        if (r < b && tx < cols) {
+            zj[(long)r * g.d + tx] = x[i];
+            xf[(long)r * g.d + tx] = (float)x[i];
+        }
+    }
+}
+
+// Backward step j: CTAs 0 .. 4 db - 1 take Z_j's 16-column slabs
+// (back_slab: the update by X_j+1 and the product with the inverse, X_j =
+// L_jj^-T Z_j; split four ways, they are the step's critical path); the
+// other CTAs subtract L_j+1,i^T X_j+1 from the whole 64 x 64 blocks Z_i, i <
+// j (whole blocks read each factor block once).
 __global__ void __launch_bounds__(GP_T) gp_back_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
-    const int j0 = j * GP_NB, b = block_rows(g.n, j);
-    const bool next = j + 1 < g.nb;
-    const int k0 = j0 + GP_NB, kd = next ? block_rows(g.n, j + 1) : 0;
-    if ((int)blockIdx.x >= g.db) {
-        const int e = (int)blockIdx.x - g.db, i0 = (e / g.db) * GP_NB, c0 = (e % g.db) * GP_NB;
-        tile_sub(g.R + (long)i0 * g.d + c0, g.d, GP_NB, min(GP_NB, g.d - c0), kd,
-                 g.A + (long)k0 * g.n + i0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
+    if ((int)blockIdx.x < 4 * g.db) {
+        const int c0 = (int)blockIdx.x * 16;
+        if (c0 < g.d)
+            back_slab(g, j, c0, gp_sm);
         return;
     }
-    const int c0 = (int)blockIdx.x * GP_NB, cols = min(GP_NB, g.d - c0);
-    double *zj = g.R + (long)j0 * g.d + c0;
-    if (next)
-        tile_sub(zj, g.d, b, cols, kd, g.A + (long)k0 * g.n + j0, 1, g.n,
-                 g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
-    // (L_jj^-T)_mk = Li[k][m].
-    tile_sub<true>(zj, g.d, b, cols, b, g.Li + (long)j * GP_NB * GP_NB, 1, GP_NB, zj, g.d, 1,
-                   gp_sm, g.X + (long)j0 * g.d + c0);
+    const int k0 = (j + 1) * GP_NB, kd = block_rows(g.n, j + 1);
+    const int e = (int)blockIdx.x - 4 * g.db, i0 = (e / g.db) * GP_NB, c0 = (e % g.db) * GP_NB;
+    tile_sub(g.R + (long)i0 * g.d + c0, g.d, GP_NB, min(GP_NB, g.d - c0), kd,
+             g.A + (long)k0 * g.n + i0, 1, g.n, g.R + (long)k0 * g.d + c0, g.d, 1, gp_sm);
 }
 
 // A = K + noise I (lower triangle in double), R = F in double.
@@ -443,12 +582,16 @@ bool opt_in_all()
     cudaGetDevice(&dev);
     if (mask >> (dev & 31) & 1)
         return true;
-    for (const void *fn : {(const void *)gp_factor_k, (const void *)gp_panel_k,
-                           (const void *)gp_back_k})
+    for (const void *fn : {(const void *)gp_factor_k, (const void *)gp_panel_k})
         if (!cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)GP_SMEM),
                      "gp kernels"))
             return false;
+    if (!cuda_ok(cudaFuncSetAttribute((const void *)gp_back_k,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)GP_SMEM_BACK),
+                 "gp kernels"))
+        return false;
     mask |= 1u << (dev & 31);
     return true;
 }
@@ -484,11 +627,11 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int
         const long m = g.nb - j;
         const long grid = j == 0 ? 1 : m * (m + 1) / 2 + m * g.db;
         gp_factor_k<<<(unsigned)grid, GP_T, GP_SMEM, st>>>(g, j);
-        gp_panel_k<<<(unsigned)(m - 1 + g.db), GP_T, GP_SMEM, st>>>(g, j);
+        gp_panel_k<<<dim3((unsigned)(m - 1 + g.db), 4), GP_T, GP_SMEM, st>>>(g, j);
     }
     for (int j = g.nb - 1; j >= 0; j--) {
-        const int grid = g.db + (j + 1 < g.nb ? j * g.db : 0);
-        gp_back_k<<<grid, GP_T, GP_SMEM, st>>>(g, j);
+        const int grid = 4 * g.db + (j + 1 < g.nb ? j * g.db : 0);
+        gp_back_k<<<grid, GP_T, GP_SMEM_BACK, st>>>(g, j);
     }
 }
 
