@@ -51,6 +51,7 @@ constexpr int GP_SP = GP_NB + 1;  // pitch of the staged product operands and of
 // reciprocals and a 32 x 32 scratch block.
 constexpr int GP_RS = 2 * GP_NB * GP_SP, GP_US = GP_RS + GP_NB;
 constexpr size_t GP_SMEM = (GP_US + 32 * 32) * sizeof(double);
+static_assert(2 * GP_NB * 68 <= GP_US + 32 * 32, "tile_sub's staging fits");
 
 struct Gp {
     double *A;   // n x n, pitch n: K + noise I (lower triangle), then L
@@ -82,21 +83,34 @@ __device__ __forceinline__ void cp_wait_all()
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// C (rows x cols, pitch ldc) -= P Q over kd terms (C = P Q with assign,
+// Pitch of tile_sub's staged operands: with 68, the eight rows times four
+// k of a warp's fragment loads fall on distinct banks in each half warp.
+constexpr int GP_TP = 68;
+
+// D += A B on the double-precision tensor cores (m8n8k4): a = A[g][q], b =
+// B[q][g], d = D[g][2 q .. 2 q + 1] with g = lane / 4, q = lane % 4.
+__device__ __forceinline__ void dmma(double d[2], double a, double b)
+{
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+// C (rows x cols, pitch ldc) -= P Q over kd terms (C = P Q with ASSIGN,
 // and then also Cf = C in float where Cf is given), P(r, k) = P[r psr + k
 // psk], Q(k, c) = Q[k qsk + c qsc]; operand entries beyond rows, cols or kd
 // read as zero. Both operands are staged k-major in shared memory by
 // asynchronous copies (all 32 of a thread in flight at once, each operand
 // read along its unit-stride dimension) before C is written, so that Q may
-// be C itself; the thread's 16 elements of C are read while they land;
-// every thread accumulates a 4 x 4 block of C.
+// be C itself; the thread's 16 elements of C are read while they land. The
+// product runs on the double-precision tensor cores: warp w owns the rows 8
+// w .. 8 w + 7 and all eight 8-column tiles.
 template <bool ASSIGN = false>
 __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const double *P,
                          long psr, long psk, const double *Q, long qsk, long qsc, double *sm,
-                         float *Cf = nullptr)
+                         float *Cf = nullptr, double *Cs = nullptr)
 {
-    double(*Ps)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
-    double(*Qs)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm + GP_NB * GP_SP);
+    double *Ps = sm, *Qs = sm + GP_NB * GP_TP;  // Ps[k][r], Qs[k][c]
     const int t = threadIdx.x;
     const bool pk = psk == 1, qk = qsk == 1;
 #pragma unroll
@@ -104,63 +118,59 @@ __device__ void tile_sub(double *C, long ldc, int rows, int cols, int kd, const 
         const int e = t + GP_T * u, hi = e / GP_NB, lo = e % GP_NB;
         int r = pk ? hi : lo, k = pk ? lo : hi;
         bool in = r < rows && k < kd;
-        cp8(&Ps[k][r], in ? P + r * psr + k * psk : P, in);
+        cp8(Ps + k * GP_TP + r, in ? P + r * psr + k * psk : P, in);
         r = qk ? hi : lo;
         k = qk ? lo : hi;
         in = r < cols && k < kd;
-        cp8(&Qs[k][r], in ? Q + k * qsk + r * qsc : Q, in);
+        cp8(Qs + k * GP_TP + r, in ? Q + k * qsk + r * qsc : Q, in);
     }
-    const int tx = t % 16, ty = t / 16;
-    double c0[4][4];
+    const int w = t >> 5, lane = t & 31, gr = lane >> 2, q = lane & 3, r = 8 * w + gr;
+    double acc[8][2];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int n = 0; n < 8; n++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int r = ty + 16 * i, cc = tx + 16 * c;
-            c0[i][c] = !ASSIGN && r < rows && cc < cols ? C[r * ldc + cc] : 0.0;
+        for (int i = 0; i < 2; i++) {
+            const int cc = 8 * n + 2 * q + i;
+            acc[n][i] = !ASSIGN && r < rows && cc < cols ? C[r * ldc + cc] : 0.0;
         }
     cp_wait_all();
     __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < GP_NB; k++) {
-        double a[4], b[4];
+#pragma unroll 4
+    for (int k4 = 0; k4 < GP_NB / 4; k4++) {
+        const double *pr = Ps + (4 * k4 + q) * GP_TP, *qr = Qs + (4 * k4 + q) * GP_TP;
+        const double a = ASSIGN ? pr[8 * w + gr] : -pr[8 * w + gr];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            a[i] = Ps[k][ty + 16 * i];
-            b[i] = Qs[k][tx + 16 * i];
-        }
+        for (int n = 0; n < 8; n++)
+            dmma(acc[n], a, qr[8 * n + gr]);
+    }
+    if (Cs) {
+        // The result into shared memory (pitch GP_SP, over the staging):
+        // every warp has read its operands first.
+        __syncthreads();
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int n = 0; n < 8; n++)
 #pragma unroll
-            for (int c = 0; c < 4; c++)
-                c0[i][c] = fma(ASSIGN ? a[i] : -a[i], b[c], c0[i][c]);
+            for (int i = 0; i < 2; i++)
+                Cs[r * GP_SP + 8 * n + 2 * q + i] = acc[n][i];
+        __syncthreads();
+        return;
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = ty + 16 * i;
+    for (int n = 0; n < 8; n++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int cc = tx + 16 * c;
+        for (int i = 0; i < 2; i++) {
+            const int cc = 8 * n + 2 * q + i;
             if (r < rows && cc < cols) {
-                C[r * ldc + cc] = c0[i][c];
+                C[r * ldc + cc] = acc[n][i];
                 if (Cf)
-                    Cf[r * ldc + cc] = (float)c0[i][c];
+                    Cf[r * ldc + cc] = (float)acc[n][i];
             }
         }
-    }
     // The staging may be reused, and C's new values are visible to the
     // whole CTA.
     __syncthreads();
 }
 
-// The inverse of the 64 x 64 lower factor L (in S, 1 / L_kk in rs, the
-// identity beyond the block's rows) into Li (row-major, zeros above the
-// diagonal), by block inversion, inv([[A, 0], [B, C]]) = [[A^-1, 0],
-// [-C^-1 B A^-1, C^-1]]: the four 16 x 16 diagonal blocks by substitution
-// (a thread per column, 16 steps), then the 16 -> 32 and 32 -> 64 joins as
-// block products over all threads. The chain is 16 steps long instead of
-// 64, so that the blocks below the diagonal can be multiplied by the
-// inverse instead of substituted.
 // A slab of a 64 x 64 block product on one CTA, four outputs a thread:
 // C (R x CC, CC = 1024 / R, pitch ldc) -= P Q over kd terms (C = P Q with
 // ASSIGN, and then Cf = C in float where Cf is given), P(r, k) = P[r psr +
@@ -314,20 +324,31 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int j0 = j * GP_NB, b = block_rows(g.n, j);
     double *Ab = g.A + (long)j0 * g.n + j0;
-    if (j > 0)
-        tile_sub(Ab, g.n, b, b, GP_NB, Ab - GP_NB, g.n, 1, Ab - GP_NB, 1, g.n, sm);
     double(*S)[GP_SP] = reinterpret_cast<double(*)[GP_SP]>(sm);
     double *rs = sm + GP_RS;  // 1 / L_kk
+    if (j > 0) {
+        // The update of block column j - 1 straight into S (rows and
+        // columns beyond b come out zero).
+        tile_sub(Ab, g.n, b, b, GP_NB, Ab - GP_NB, g.n, 1, Ab - GP_NB, 1, g.n, sm, nullptr,
+                 &S[0][0]);
+    }
+    else {
+#pragma unroll
+        for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
+            const int e = t + GP_T * u, r = e / GP_NB, c = e % GP_NB;
+            const bool in = c <= r && r < b;
+            cp8(&S[r][c], in ? Ab + (long)r * g.n + c : Ab, in);
+        }
+        cp_wait_all();
+        __syncthreads();
+    }
+    // Zeros above the diagonal, the identity beyond the block's rows.
 #pragma unroll
     for (int u = 0; u < GP_NB * GP_NB / GP_T; u++) {
         const int e = t + GP_T * u, r = e / GP_NB, c = e % GP_NB;
-        const bool in = c <= r && r < b;
-        cp8(&S[r][c], in ? Ab + (long)r * g.n + c : Ab, in);
+        if (c > r || r >= b)
+            S[r][c] = r == c ? 1.0 : 0.0;
     }
-    cp_wait_all();
-    // Identity beyond the block's rows.
-    if (t >= b && t < GP_NB)
-        S[t][t] = 1.0;
     __syncthreads();
     for (int p = 0; p < GP_NB / 16; p++) {
         const int c0 = 16 * p;
