@@ -83,6 +83,17 @@ __device__ __forceinline__ void cp_wait_all()
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
+// Programmatic dependent launch across the chain of kernels: the next
+// kernel may be scheduled as soon as every CTA of this one has started,
+// and waits (griddepcontrol.wait) until this one has completed and its
+// writes are visible, before it reads anything. Launch gaps overlap the
+// previous kernel's tail.
+__device__ __forceinline__ void chain_enter()
+{
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Pitch of tile_sub's staged operands: with 68, the eight rows times four
 // k of a warp's fragment loads fall on distinct banks in each half warp.
 constexpr int GP_TP = 68;
@@ -429,6 +440,7 @@ __device__ void diag_factor(const Gp &g, int j, double *sm)
 __global__ void __launch_bounds__(GP_T, 1) gp_factor_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
+    chain_enter();
     if (blockIdx.x == 0) {
         diag_factor(g, j, gp_sm);
         return;
@@ -463,6 +475,7 @@ __global__ void __launch_bounds__(GP_T, 1) gp_factor_k(Gp g, int j)
 __global__ void __launch_bounds__(GP_T) gp_panel_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
+    chain_enter();
     const int j0 = j * GP_NB, b = block_rows(g.n, j), nk = g.nb - 1 - j, sl = 16 * blockIdx.y;
     const double *li = g.Li + (long)j * GP_NB * GP_NB;
     if ((int)blockIdx.x < nk) {
@@ -568,6 +581,7 @@ __device__ void back_slab(const Gp &g, int j, int c0, double *sm)
 __global__ void __launch_bounds__(GP_T) gp_back_k(Gp g, int j)
 {
     extern __shared__ __align__(16) double gp_sm[];
+    chain_enter();
     if ((int)blockIdx.x < 4 * g.db) {
         const int c0 = (int)blockIdx.x * 16;
         if (c0 < g.d)
@@ -617,6 +631,23 @@ bool opt_in_all()
     return true;
 }
 
+// A kernel of the chain with programmatic stream serialization (see
+// chain_enter).
+void chain_launch(void (*k)(Gp, int), dim3 grid, size_t smem, cudaStream_t st, Gp g, int j)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(GP_T);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k, g, j);
+}
+
 }  // namespace
 
 // Work: A (n x n), R (n x d), the n reciprocals and the block inverses, in
@@ -647,12 +678,12 @@ void gp_solve_dev(cudaStream_t st, const float *K, int n, const float *F_in, int
     for (int j = 0; j < g.nb; j++) {
         const long m = g.nb - j;
         const long grid = j == 0 ? 1 : m * (m + 1) / 2 + m * g.db;
-        gp_factor_k<<<(unsigned)grid, GP_T, GP_SMEM, st>>>(g, j);
-        gp_panel_k<<<dim3((unsigned)(m - 1 + g.db), 4), GP_T, GP_SMEM, st>>>(g, j);
+        chain_launch(gp_factor_k, dim3((unsigned)grid), GP_SMEM, st, g, j);
+        chain_launch(gp_panel_k, dim3((unsigned)(m - 1 + g.db), 4), GP_SMEM, st, g, j);
     }
     for (int j = g.nb - 1; j >= 0; j--) {
         const int grid = 4 * g.db + (j + 1 < g.nb ? j * g.db : 0);
-        gp_back_k<<<grid, GP_T, GP_SMEM_BACK, st>>>(g, j);
+        chain_launch(gp_back_k, dim3(grid), GP_SMEM_BACK, st, g, j);
     }
 }
 
