@@ -37,6 +37,7 @@
 // frees its tensor memory and returns.
 
 #include <mutex>
+#include <stdlib.h>
 #include <string.h>
 
 #include "tc_common.cuh"
@@ -445,6 +446,179 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
     }
 }
 
+// ------------------------------------------------------------ 256 x 256
+//
+// Dense products with 256 x BN2 output tiles (BN2 256, 192 or 160): two M =
+// 128 tcgen05.mma per k-step share each B tile (acc0 = rows 0..127 in TMEM
+// columns 0.., acc1 = rows 128..255 from column 256). Per staged byte that
+// is up to 1.5 times the tensor work of the 128 x 256 tile (64 KB feed 8
+// MMAs instead of 48 KB feeding 4) and a third less L2 traffic per
+// product, so that the three stages that fit the shared memory hold more
+// work in flight; the width is chosen so that the tiles fill whole rounds
+// of the SMs. The price: the accumulators take the tensor memory, so that
+// a tile's epilogue overlaps only the TMA loads of the next. Same
+// warp roles as tc_gemm_kernel: warp 0 TMA, warp 1 TMEM and MMA, warps
+// 2..9 epilogue (warp w: TMEM lane quadrant w % 4 of accumulator (w - 2) /
+// 4, all 256 columns in 32-column chunks, TMA stores).
+constexpr int BM2 = 256, ST2 = 3;
+
+template <int BN2>
+struct Smem2 {
+    alignas(1024) __nv_bfloat16 a[ST2][BM2 * BK];
+    alignas(1024) __nv_bfloat16 b[ST2][BN2 * BK];
+    alignas(1024) unsigned char cst[8][4096];
+    uint64_t full[ST2], empty[ST2], acc_full, acc_empty;
+    uint32_t tmem;
+};
+
+template <int BN2, int ACT, typename TC>
+__global__ void __launch_bounds__(NTHREADS, 1)
+tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a,
+                const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_c, TcParams p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Smem2<BN2> &s =
+        *reinterpret_cast<Smem2<BN2> *>(smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int nk = (p.K + BK - 1) / BK;
+    const int tiles_m = (p.M + BM2 - 1) / BM2;
+    const int ntiles = tiles_m * ((p.N + BN2 - 1) / BN2);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ST2; i++) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.acc_full, 1);
+        mbar_init(&s.acc_empty, EPI_WARPS);
+        mbar_fence_init();
+    }
+    if (warp == 1)
+        tmem_alloc(&s.tmem, 512);
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = s.tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            constexpr uint32_t bytes = (uint32_t)(BM2 + BN2) * BK * 2;
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int m0 = (t % tiles_m) * BM2, n0 = (t / tiles_m) * BN2;
+                const int k_off = k_rotation(t, tiles_m, nk);
+                for (int kk = 0; kk < nk; kk++, it++) {
+                    const int kb = kk + k_off < nk ? kk + k_off : kk + k_off - nk;
+                    const int st = it % ST2;
+                    if (it >= ST2 && !mbar_wait(&s.empty[st], ((it / ST2) - 1) & 1, 31)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&s.full[st], bytes);
+                    tma_load_2d(s.a[st], &tma_a, &s.full[st], kb * BK, m0);
+                    tma_load_2d(s.b[st], &tma_b, &s.full[st], kb * BK, n0);
+                }
+            }
+        }
+    }
+    else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(128, BN2);
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
+                // The epilogue has read both accumulators of the previous tile.
+                if (lt > 0 && !mbar_wait(&s.acc_empty, (lt - 1) & 1, 34))
+                    break;
+                fence_after();
+                for (int kk = 0; kk < nk; kk++, it++) {
+                    const int st = it % ST2;
+                    if (!mbar_wait(&s.full[st], (it / ST2) & 1, 32)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = su32(s.a[st]);
+                    const uint64_t da0 = sw128_desc(sa), da1 = sw128_desc(sa + 128 * 128);
+                    const uint64_t db = sw128_desc(su32(s.b[st]));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++) {
+                        const uint32_t acc = (kk > 0 || k > 0) ? 1u : 0u;
+                        mma_bf16(tmem, da0 + 2 * k, db + 2 * k, idesc, acc);
+                        mma_bf16(tmem + 256, da1 + 2 * k, db + 2 * k, idesc, acc);
+                    }
+                    mma_commit(&s.empty[st]);
+                }
+                if (ok)
+                    mma_commit(&s.acc_full);
+            }
+        }
+    }
+    else {
+        const int q = warp % 4, half = (warp - 2) / 4;
+        const int rr = 128 * half + 32 * q + lane;
+        unsigned char *cst = s.cst[warp - 2];
+        const TC *R = (const TC *)p.R;
+        int lt = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+            const int m0 = (t % tiles_m) * BM2, n0 = (t / tiles_m) * BN2;
+            const int row = m0 + rr;
+            if (!__all_sync(0xffffffffu, mbar_wait_backoff(&s.acc_full, lt & 1, 33)))
+                break;
+            fence_after();
+            const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(256 * half);
+            const float br = p.bias_r && row < p.M ? __ldg(p.bias_r + row) : 0.0f;
+            for (int c0 = 0; c0 < BN2 && n0 + c0 < p.N; c0 += 32) {
+                float v[32];
+                tmem_ld32(acc + c0, v);
+                const int col0 = n0 + c0;
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const float b = p.bias && col0 + j < p.N ? __ldg(p.bias + col0 + j) : 0.0f;
+                    v[j] = apply_act(p.alpha * v[j] + b + br, ACT >= 0 ? ACT : p.act, p.slope);
+                }
+                if (R && row < p.M)
+                    add_row(v, R + (long)row * p.ldc + col0, p.N - col0);
+                if (lane == 0)
+                    bulk_wait_read<0>();
+                __syncwarp();
+                stage_row(cst, lane, v, (TC *)nullptr);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tma_c, cst, col0, m0 + 128 * half + 32 * q);
+                    bulk_commit();
+                }
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&s.acc_empty);
+        }
+        if (lane == 0)
+            bulk_wait_all();
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int BN2, int ACT, typename TC>
+bool run_tc2(cudaStream_t st, int grid, const CUtensorMap &ma, const CUtensorMap &mb,
+             const CUtensorMap &mc, const TcParams &p)
+{
+    const size_t smem = sizeof(Smem2<BN2>) + 1024;
+    static unsigned done = 0;
+    if (!smem_opt_in((const void *)tc_gemm2_kernel<BN2, ACT, TC>, smem, &done))
+        return false;
+    tc_gemm2_kernel<BN2, ACT, TC><<<grid, NTHREADS, smem, st>>>(ma, mb, mc, p);
+    return true;
+}
+
 // Tile width (pixels) of the convolution mode with the fewest wasted
 // output positions for an H x W map.
 int conv_tile_width(int H, int W)
@@ -546,6 +720,40 @@ bool launch_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     if (g.act == ACTF_NONE)
         return run_tc<BN, STAGES, ACTF_NONE, float>(st, grid, ma, mb, mc, ma3, p);
     return run_tc<BN, STAGES, -1, float>(st, grid, ma, mb, mc, ma3, p);
+}
+
+// 256 x BN2 tiles for a dense product without an activation (GemmArgs
+// amode 0).
+template <int BN2>
+bool launch_tc2(cudaStream_t st, const GemmArgs &g, int sm_count)
+{
+    CUtensorMap ma, mb, mc;
+    TcParams p;
+    memset(&p, 0, sizeof(p));
+    if (!make_map_2d(&ma, g.A, g.M, g.K, g.lda, BM2) || !make_map_2d(&mb, g.B, g.N, g.K, g.ldb, BN2))
+        return false;
+    p.M = g.M;
+    p.N = g.N;
+    p.K = g.K;
+    p.C = g.C;
+    p.ldc = g.ldc;
+    p.bias = g.biasrow ? nullptr : g.bias;
+    p.bias_r = g.biasrow ? g.bias : nullptr;
+    p.R = g.R;
+    p.alpha = g.alpha;
+    p.act = g.act;
+    p.slope = g.slope;
+    p.c_bf16 = g.c == DT_BF16;
+    memset(&mc, 0, sizeof(mc));
+    if (!make_map_c(&mc, g.C, g.c == DT_BF16 ? 2 : 4, p, g.ldc))
+        return false;
+    const long ntiles = (long)cdiv(g.M, BM2) * cdiv(g.N, BN2);
+    const int grid = (int)(ntiles < sm_count ? ntiles : sm_count);
+    if (g.act != ACTF_NONE)
+        return false;
+    if (p.c_bf16)
+        return run_tc2<BN2, ACTF_NONE, __nv_bfloat16>(st, grid, ma, mb, mc, p);
+    return run_tc2<BN2, ACTF_NONE, float>(st, grid, ma, mb, mc, p);
 }
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -709,6 +917,38 @@ bool gemm_tc(cudaStream_t st, const GemmArgs &g, int sm_count)
     if (((uintptr_t)g.A & 15) || ((uintptr_t)g.B & 15) ||
         (g.amode == 0 && (g.lda & 7)) || (g.ldb & 7))
         return false;
+    // Large dense products without an activation: 256-row tiles, 256, 192
+    // or 160 columns wide, whichever fills the rounds of tiles over the SMs
+    // best, where that is at least 80 % (COREG_GEMM256=0 turns them off, for
+    // comparison). With an activation the epilogue, which these tiles
+    // cannot overlap with the next tile's products, costs more than the
+    // wider tile saves (measured on the ViT's fc1).
+    static const bool t256 = [] {
+        const char *e = getenv("COREG_GEMM256");
+        return !(e && e[0] == '0');
+    }();
+    if (t256 && g.amode == 0 && g.act == ACTF_NONE && g.N >= 512 && g.M >= 512 && g.K >= 256 &&
+        ((uintptr_t)g.C & 15) == 0 && (g.ldc * (g.c == DT_BF16 ? 2 : 4)) % 16 == 0) {
+        int best = 0;
+        double best_u = 0.0;
+        for (int bn : {256, 192, 160}) {
+            const long tiles = (long)cdiv(g.M, 256) * cdiv(g.N, bn);
+            const long rounds = (tiles + sm_count - 1) / sm_count;
+            const double u = (double)tiles / (double)(rounds * sm_count);
+            if (u > best_u + 1e-9) {
+                best_u = u;
+                best = bn;
+            }
+        }
+        if (best_u >= 0.8) {
+            if (best == 256 && tc::launch_tc2<256>(st, g, sm_count))
+                return true;
+            if (best == 192 && tc::launch_tc2<192>(st, g, sm_count))
+                return true;
+            if (best == 160 && tc::launch_tc2<160>(st, g, sm_count))
+                return true;
+        }
+    }
     // Tile width by the rounds of tiles the persistent CTAs walk: a 128 x
     // 128 tile takes about half the time of a 128 x 256 one plus the
     // overhead of reading its operands twice as often (weighted 1.15).

@@ -26,6 +26,11 @@ SHAPES = [
     (1601, 1024, 4096, 0, True),   # DINOv2 fc2 with the residual
     (1600, 4097, 1024, 0, False),  # decoder to_out (odd N)
     (4900, 1136, 1136, 0, False),  # refiner 1 x 1 at 1/8
+    # 256-row tiles (256, 192 and 160 columns, filling whole rounds of SMs)
+    (3202, 3072, 1024, 0, False),  # DINOv2 qkv, both images
+    (3202, 4096, 1024, 0, True),   # fc1 shape with a residual
+    (3300, 2900, 712, 0, True),    # ragged M, N and K (K a multiple of 8 only)
+    (9472, 1024, 256, 0, False),   # 148 tiles of 256 x 256
     # narrow outputs: 16-, 32- and 64-column tiles
     (5000, 32, 32, 2, False),      # refiner pointwise at full size (32 channels)
     (746, 6, 32, 0, True),         # refiner heads (warp 2 + confidence 4)
@@ -83,6 +88,7 @@ LAYOUTS = [
     (128, 1000, 576, 0, 1),
     (96, 333, 72, 0, 0),
     (300, 200, 96, 1, 1),
+    (4000, 2600, 320, 1, 1),       # 256 x 256 tiles with the row bias
 ]
 
 
