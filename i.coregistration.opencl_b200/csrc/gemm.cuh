@@ -123,6 +123,13 @@ bool attention_tc(cudaStream_t st, const void *qkv, int N, int Dm, int heads, vo
 void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, int C, int kp,
                        const __nv_bfloat16 *wk, const float *bias, int K, int act,
                        float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count);
+
+// The 3 -> 64 channel 3 x 3 convolution with bias and ReLU over a
+// three-channel map, on the tensor cores without an im2col buffer
+// (tc_conv_rgb.cu): wk is 64 x 32 (column j = tap 3 + c); false where it
+// does not apply.
+bool conv_rgb_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W,
+                 const __nv_bfloat16 *wk, const float *bias, void *out, DType ot, int sm_count);
 // One hidden block of RoMa's refiners, out = W relu(dw5x5(in) + b_dw) + b_pw,
 // over a channels-last bfloat16 (H, W, C) map in one tensor-core kernel
 // (tc_dwpw.cu): dw_w (C x 25) and dw_b float32, pw_w (C x C, output-major)

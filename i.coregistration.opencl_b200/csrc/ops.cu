@@ -655,6 +655,10 @@ void conv3x3_im2col_tc(cudaStream_t st, const __nv_bfloat16 *in, int H, int W, i
                        float slope, void *out, DType ot, __nv_bfloat16 *col, int sm_count)
 {
     const long n = (long)H * W;
+    // RGB to 64 channels with ReLU: one kernel, no im2col buffer.
+    if (C == 3 && kp == 32 && K == 64 && act == ACTF_RELU &&
+        conv_rgb_tc(st, in, H, W, wk, bias, out, ot, sm_count))
+        return;
     if (C == 3 && kp == 32 && n < (1L << 31))
         im2col3_row_k<3, 32><<<cdiv(n, 256), 256, 0, st>>>(in, H, W, col);
     else
