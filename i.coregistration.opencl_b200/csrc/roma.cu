@@ -125,6 +125,10 @@ struct roma_impl {
     float *t_x = nullptr, *t_out = nullptr;
     void *t_n = nullptr, *t_qkv = nullptr, *t_o = nullptr, *t_h = nullptr;
     float *g_nx, *g_ny, *g_kyy, *g_kxy, *g_x;
+    // bfloat16 mode: the GP features split into bfloat16 parts for the
+    // kernel matrices on the tensor cores (A3 forms of A's and B's
+    // features, B3 form of B's; n16 x 3 GP_DIM each).
+    __nv_bfloat16 *g_s3[3];
     double *gp_work;
     int *gp_flag;
     void *d_a = nullptr, *d_b = nullptr;
@@ -851,6 +855,9 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
     I->t_out = (float *)dmalloc(I, n16 * (NCLS + 1) * 4, "anchor logits");
     I->g_nx = (float *)dmalloc(I, n16 * 4, "norms");
     I->g_ny = (float *)dmalloc(I, n16 * 4, "norms");
+    if (I->at == DT_BF16)
+        for (int k = 0; k < 3; k++)
+            I->g_s3[k] = (__nv_bfloat16 *)dmalloc(I, n16 * 3 * GP_DIM * 2, "GP split features");
     I->g_kyy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_kxy = (float *)dmalloc(I, n16 * n16 * 4, "GP kernel");
     I->g_x = (float *)dmalloc(I, n16 * GP_DIM * 4, "GP solve");
@@ -1233,9 +1240,37 @@ void dino(Ctx &c)
     }
 }
 
+// x = hi + lo with hi, lo bfloat16 (hi = x rounded, lo = the rest
+// rounded): the A form [hi | hi | lo] and the B form [hi | lo | hi] of an n x
+// d float matrix, so that A3 B3^T = hi hi' + hi lo' + lo hi', the float
+// product up to the lo lo' term and the rounding of lo (relative 2^-16).
+__global__ void split3_k(const float *x, long n, int d, __nv_bfloat16 *a3, __nv_bfloat16 *b3)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n * d)
+        return;
+    const long r = e / d;
+    const int c = (int)(e % d);
+    const float v = x[e];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+    __nv_bfloat16 *ra = a3 + r * 3 * d, *rb = b3 ? b3 + r * 3 * d : nullptr;
+    ra[c] = hi;
+    ra[d + c] = hi;
+    ra[2 * d + c] = lo;
+    if (rb) {
+        rb[c] = hi;
+        rb[d + c] = lo;
+        rb[2 * d + c] = hi;
+    }
+}
+
 // Gaussian-process posterior of A's 1/16 features given B's and the
 // position basis, into t_x columns 0..511, A's features in 512..1023
-// (roma.c:873-896), the solve on the device in double.
+// (roma.c:873-896), the solve on the device in double. In bfloat16 mode the
+// two kernel matrices' products (cosines of normalized features) run on the
+// tensor cores as three-term bfloat16 splits (K = 3 x 512), float32 mode
+// keeps the float32 products.
 void gp(Ctx &c)
 {
     roma_impl *I = c.I;
@@ -1246,10 +1281,25 @@ void gp(Ctx &c)
         roma_row_norm_l(c.st, ya, n, GP_DIM, I->g_nx);
         roma_row_norm_l(c.st, yb, n, GP_DIM, I->g_ny);
     }
-    gemm_nt(c, "gp_gemm", n, n, GP_DIM, yb, GP_DIM, DT_F32, yb, nullptr, I->g_kyy,
-            n, DT_F32, ACTF_NONE, false);
-    gemm_nt(c, "gp_gemm", n, n, GP_DIM, ya, GP_DIM, DT_F32, yb, nullptr, I->g_kxy,
-            n, DT_F32, ACTF_NONE, false);
+    if (I->at == DT_BF16) {
+        {
+            Prof p(c.m->ocl, "gp_kernel");
+            const long e = (long)n * GP_DIM;
+            split3_k<<<cdiv(e, 256), 256, 0, c.st>>>(yb, n, GP_DIM, I->g_s3[1], I->g_s3[2]);
+            split3_k<<<cdiv(e, 256), 256, 0, c.st>>>(ya, n, GP_DIM, I->g_s3[0], nullptr);
+            launch_ok("gp_kernel");
+        }
+        gemm_nt(c, "gp_gemm", n, n, 3 * GP_DIM, I->g_s3[1], 3 * GP_DIM, DT_BF16, I->g_s3[2],
+                nullptr, I->g_kyy, n, DT_F32, ACTF_NONE, false);
+        gemm_nt(c, "gp_gemm", n, n, 3 * GP_DIM, I->g_s3[0], 3 * GP_DIM, DT_BF16, I->g_s3[2],
+                nullptr, I->g_kxy, n, DT_F32, ACTF_NONE, false);
+    }
+    else {
+        gemm_nt(c, "gp_gemm", n, n, GP_DIM, yb, GP_DIM, DT_F32, yb, nullptr, I->g_kyy,
+                n, DT_F32, ACTF_NONE, false);
+        gemm_nt(c, "gp_gemm", n, n, GP_DIM, ya, GP_DIM, DT_F32, yb, nullptr, I->g_kxy,
+                n, DT_F32, ACTF_NONE, false);
+    }
     {
         Prof p(c.m->ocl, "gp_kernel");
         roma_cos_exp_l(c.st, I->g_kyy, I->g_ny, I->g_ny, n, n, GP_T, COS_EPS);
