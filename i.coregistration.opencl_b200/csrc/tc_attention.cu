@@ -115,17 +115,6 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b)
     return d;
 }
 
-__device__ __forceinline__ float2 fsub2(float2 a, float2 b)
-{
-    unsigned long long aa, bb, dd;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(aa) : "f"(a.x), "f"(a.y));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(bb) : "f"(b.x), "f"(b.y));
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(dd) : "l"(aa), "l"(bb));
-    float2 d;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dd));
-    return d;
-}
-
 // The hardware base-2 exponential (results below 2^-126 flush to zero,
 // negligible next to the row maximum's 1).
 __device__ __forceinline__ float ex2(float x)
@@ -134,42 +123,6 @@ __device__ __forceinline__ float ex2(float x)
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-
-// Base-2 exponential of a pair on the FMA pipe, so that the softmax can
-// share its exponentials between that pipe and the exponential unit (which
-// alone bounds the head-64 kernel: 128 exponentials per query row and
-// key block against 2 x 64 x 128 multiply-adds on the tensor cores).
-// Range reduction x = n + f, n = rint(x) (adding 1.5 2^23 leaves n in the
-// low mantissa bits), |f| <= 1/2; 2^f by a degree-3 polynomial fitted here
-// for least maximum relative error on [-1/2, 1/2] (Lawson's iteration,
-// float32 coefficients): at most 7.5e-5 relative, against the 3.9e-3
-// half-unit of the bfloat16 P it feeds; 2^n added into the exponent field.
-// Inputs are clamped at -125 (masked keys give -inf): the result is then
-// 2^-125 instead of 0, nothing next to the row maximum's 1.
-constexpr float EX2_C0 = 0.99992806f, EX2_C1 = 0.69326097f, EX2_C2 = 0.24261114f,
-                EX2_C3 = 0.05517167f;
-
-__device__ __forceinline__ float2 ex2_poly2(float2 x)
-{
-    x.x = fmaxf(x.x, -125.0f);
-    x.y = fmaxf(x.y, -125.0f);
-    const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);
-    const float2 t = fadd2(x, magic);
-    const float2 n = fadd2(t, nmagic);
-    const float2 f = fsub2(x, n);
-    float2 q = ffma2(f, make_float2(EX2_C3, EX2_C3), make_float2(EX2_C2, EX2_C2));
-    q = ffma2(q, f, make_float2(EX2_C1, EX2_C1));
-    q = ffma2(q, f, make_float2(EX2_C0, EX2_C0));
-    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
-                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
-}
-
-// Of every eight exponential pairs of a query row, how many the head-64
-// kernel computes with ex2_poly2 (the rest on the exponential unit).
-#ifndef COREG_ATTN_POLY8
-#define COREG_ATTN_POLY8 2
-#endif
 
 template <int D>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
@@ -462,9 +415,7 @@ tc_attn_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
 //               tensor memory, masked keys, online maximum (O_t and the row
 //               sum rescaled in tensor memory only when the maximum grows
 //               by more than 2^8), P_t(j) = exp2 as bfloat16 into the tile's
-//               128-byte swizzled P buffer (free once PV_t(j - 1) is done),
-//               a quarter of the exponentials as polynomials on the FMA
-//               pipe (ex2_poly2), the rest on the exponential unit;
+//               128-byte swizzled P buffer (free once PV_t(j - 1) is done);
 //               at the end O_t / l to global memory.
 constexpr int ATT2_THREADS = 320;
 
@@ -657,17 +608,8 @@ tc_attn2_kernel(const __grid_constant__ CUtensorMap map, AttnParams p)
                     for (int u = 0; u < 4; u++) {
                         const int i = a * 64 + cc * 8 + 2 * u;
                         const float2 x = ffma2(make_float2(sv[i], sv[i + 1]), sc, mm);
-                        // Pairs 4 (cc % 2) + u of each 16 keys: the last
-                        // COREG_ATTN_POLY8 on the FMA pipe.
-                        if (4 * (cc & 1) + u >= 8 - COREG_ATTN_POLY8) {
-                            const float2 y = ex2_poly2(x);
-                            e[2 * u] = y.x;
-                            e[2 * u + 1] = y.y;
-                        }
-                        else {
-                            e[2 * u] = ex2(x.x);
-                            e[2 * u + 1] = ex2(x.y);
-                        }
+                        e[2 * u] = ex2(x.x);
+                        e[2 * u + 1] = ex2(x.y);
                         s2 = fadd2(s2, make_float2(e[2 * u], e[2 * u + 1]));
                     }
                     uint4 w;
