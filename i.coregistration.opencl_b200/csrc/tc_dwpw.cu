@@ -19,8 +19,11 @@
 //          k-block) in float32 (packed FMAs, weights from shared memory,
 //          the taps in the reference's order) from its input patch and
 //          write the bfloat16 result, 128-byte swizzled, into a ring of NA
-//          A buffers; sixteen warps, so that each scheduler has four to
-//          hide the shared-memory latency with;
+//          A buffers. A thread takes one tile row of one channel pair, so
+//          that every weight and patch value it reads from shared memory
+//          (the bound of this stage) feeds 16 and up to 5 packed FMAs; an
+//          item takes 8 warps (CK 64) or 4 (CK 32), and the sixteen warps
+//          work on 2 or 4 consecutive items at once;
 //   16     tensor-memory allocator, weight loader (one TMA load, resident
 //          for the kernel) and MMA issuer into one of two 128 x C float32
 //          accumulators (tiles alternate);
@@ -63,18 +66,24 @@ struct DwCfg {
     static constexpr int CK = C < 64 ? C : 64;        // channels per k-block
     static constexpr int NKB = C / CK;
     static constexpr int NP = CK / 2;                 // channel pairs per k-block
-    // Output pixels per producer thread, a run of one tile row: CK 64, a
-    // warp takes half a row (lane = channel pair); CK 32, a quarter of two
-    // adjacent rows (half warp = row).
-    static constexpr int SPX = CK == 64 ? 8 : 4;
+    // A producer thread computes one whole tile row (TX pixels) of one
+    // channel pair, so that its weights and each patch value it loads feed
+    // TX and up to five outputs: CK 64, a warp per row (lane = pair), eight
+    // warps per item; CK 32, a half warp per row, four warps per item. The
+    // producer warps form PG groups that work on PG consecutive items at
+    // once (group g takes items g, g + PG, ...).
+    static constexpr int WI = CK == 64 ? 8 : 4;      // warps per item
+    static constexpr int PG = PROD_WARPS / WI;       // items in flight
     // Patch width loaded (pixels) and row pitch in 32-bit words: with CK 32
     // the two half warps read adjacent patch rows, which one extra pixel
     // per row puts 16 banks apart.
     static constexpr int PXL = CK == 32 ? PX + 1 : PX;
     static constexpr int RPW = PXL * NP;
     static constexpr int PATCH_WORDS = PY * RPW;
-    static constexpr int NA = 3;                      // A ring
-    static constexpr int NH = 3;                      // patch ring
+    // Rings: one slot more than the items in flight, where shared memory
+    // allows (C 128 fills it at three).
+    static constexpr int NA = C == 32 ? PG + 1 : 3;   // A ring
+    static constexpr int NH = C == 32 ? PG + 2 : 3;   // patch ring
     static constexpr int NO = C <= 64 ? 2 : 1;        // output staging buffers
     static constexpr int TMEM_COLS = 2 * C;           // two accumulators
     static constexpr int OSW = CK == 64 ? 128 : 64;   // output swizzle (bytes)
@@ -158,7 +167,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
     if (threadIdx.x == 0) {
         mbar_init(&s.bfull, 1);
         for (int i = 0; i < G::NA; i++) {
-            mbar_init(&s.afull[i], PROD_WARPS);
+            mbar_init(&s.afull[i], G::WI);
             mbar_init(&s.aempty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
@@ -167,7 +176,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
         }
         for (int i = 0; i < G::NH; i++) {
             mbar_init(&s.pfull[i], 1);
-            mbar_init(&s.pempty[i], PROD_WARPS);
+            mbar_init(&s.pempty[i], G::WI);
         }
         s.eabort = 0;
         mbar_fence_init();
@@ -190,18 +199,17 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
 
     if (warp < PROD_WARPS) {
         // ------------------------------------------------------ producers
-        int row, pair, px0;
+        const int grp = warp / G::WI, gw = warp % G::WI;
+        int row, pair;
         if (G::CK == 64) {
-            row = warp >> 1;
+            row = gw;
             pair = lane;
-            px0 = G::SPX * (warp & 1);
         }
         else {
-            row = 2 * (warp >> 2) + (lane >> 4);
+            row = 2 * gw + (lane >> 4);
             pair = lane & 15;
-            px0 = G::SPX * (warp & 3);
         }
-        for (int i = 0; i < nitems; i++) {
+        for (int i = grp; i < nitems; i += G::PG) {
             const int slot = i % G::NA, use = i / G::NA;
             // The MMAs of this A buffer's previous item are done, and item
             // i's patch has landed.
@@ -211,10 +219,10 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
                 break;
             const uint32_t *pb = s.patch[i % G::NH];
             const int kb = i % G::NKB, c = kb * G::CK + 2 * pair;
-            u64 acc[G::SPX];
+            u64 acc[TX];
             const u64 bb = *(const u64 *)&s.dwb[c];
 #pragma unroll
-            for (int o = 0; o < G::SPX; o++)
+            for (int o = 0; o < TX; o++)
                 acc[o] = bb;
 #pragma unroll
             for (int a = 0; a < 5; a++) {
@@ -222,14 +230,14 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
 #pragma unroll
                 for (int k = 0; k < 5; k++)
                     w[k] = *(const u64 *)&s.dw[kb][a * 5 + k][pair];
-                const uint32_t *rp = pb + (row + a) * G::RPW + px0 * G::NP + pair;
+                const uint32_t *rp = pb + (row + a) * G::RPW + pair;
 #pragma unroll
-                for (int x = 0; x < G::SPX + 4; x++) {
+                for (int x = 0; x < TX + 4; x++) {
                     const u64 v = bf2(rp[x * G::NP]);
 #pragma unroll
                     for (int k = 0; k < 5; k++) {
                         const int ox = x - k;
-                        if (ox >= 0 && ox < G::SPX)
+                        if (ox >= 0 && ox < TX)
                             acc[ox] = fma2p(v, w[k], acc[ox]);
                     }
                 }
@@ -240,8 +248,8 @@ dwpw_kernel(const __grid_constant__ CUtensorMap tma_in, const __grid_constant__ 
             uint32_t *ab = (uint32_t *)s.a[slot];
             const int chunk = pair >> 2, sub = pair & 3;
 #pragma unroll
-            for (int o = 0; o < G::SPX; o++) {
-                const int m = row * TX + px0 + o;
+            for (int o = 0; o < TX; o++) {
+                const int m = row * TX + o;
                 ab[m * 32 + ((chunk ^ (m & 7)) << 2) + sub] = relu_bf2(acc[o]);
             }
             fence_async_smem();
