@@ -5,6 +5,7 @@
 // replaces (cited per function); the kernels are this build's own.
 
 #include <math.h>
+#include <type_traits>
 #include <string.h>
 
 #include "gemm.cuh"
@@ -1057,12 +1058,15 @@ __device__ __forceinline__ void store4(__nv_bfloat16 *y, float4 v)
     *(uint2 *)y = u;
 }
 
-template <typename TO>
+// NVMAX: the row's float4 per lane, a compile-time bound, so that a row
+// of 1024 channels holds 32 registers of values and not 64 (at 93
+// registers a thread only two 256-thread blocks fit an SM, and the 3202
+// rows of the ViT took two waves).
+template <typename TO, int NVMAX>
 __global__ void __launch_bounds__(256)
 layernorm_warp_k(const float *X, TO *Y, const float *g, const float *bt, long rows, int nv,
                  float eps, int act, float slope)
 {
-    constexpr int NVMAX = 16;
     const int lane = threadIdx.x % 32;
     const long row = (long)blockIdx.x * 8 + threadIdx.x / 32;
     if (row >= rows)
@@ -1125,12 +1129,24 @@ void layernorm_rows(cudaStream_t st, const float *X, void *Y, DType ty,
     if (C % 128 == 0 && C <= 2048 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)Y & 15) == 0 &&
         (!g || (((uintptr_t)g & 15) == 0 && ((uintptr_t)b & 15) == 0))) {
         const unsigned blocks = (unsigned)((rows + 7) / 8);
-        if (ty == DT_BF16)
-            layernorm_warp_k<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-                X, (__nv_bfloat16 *)Y, g, b, rows, C / 128, eps, act, slope);
+        const int nv = C / 128;
+        auto run = [&](auto nvmax) {
+            constexpr int NV = decltype(nvmax)::value;
+            if (ty == DT_BF16)
+                layernorm_warp_k<__nv_bfloat16, NV><<<blocks, 256, 0, st>>>(
+                    X, (__nv_bfloat16 *)Y, g, b, rows, nv, eps, act, slope);
+            else
+                layernorm_warp_k<float, NV><<<blocks, 256, 0, st>>>(X, (float *)Y, g, b, rows,
+                                                                    nv, eps, act, slope);
+        };
+        if (nv <= 2)
+            run(std::integral_constant<int, 2>());
+        else if (nv <= 4)
+            run(std::integral_constant<int, 4>());
+        else if (nv <= 8)
+            run(std::integral_constant<int, 8>());
         else
-            layernorm_warp_k<float><<<blocks, 256, 0, st>>>(X, (float *)Y, g, b, rows, C / 128,
-                                                            eps, act, slope);
+            run(std::integral_constant<int, 16>());
         return;
     }
     if (ty == DT_BF16)
