@@ -124,6 +124,7 @@ struct roma_impl {
     void *P[ROMA_SCALES][2] = {}, *P2[ROMA2_SCALES][2] = {};
     float *t_x = nullptr, *t_out = nullptr;
     void *t_n = nullptr, *t_qkv = nullptr, *t_o = nullptr, *t_h = nullptr;
+    size_t t_qkv_bytes = 0;
     float *g_nx, *g_ny, *g_kyy, *g_kxy, *g_x;
     // bfloat16 mode: the GP features split into bfloat16 parts for the
     // kernel matrices on the tensor cores (A3 forms of A's and B's
@@ -849,7 +850,8 @@ extern "C" void roma_alloc(struct roma_model *m, int H, int W)
     // Token buffers for both images' DINOv2 tokens.
     I->t_x = (float *)dmalloc(I, 2 * ntok * D * 4, "tokens");
     I->t_n = dmalloc(I, 2 * ntok * D * as, "tokens");
-    I->t_qkv = dmalloc(I, 2 * ntok * 3 * D * as, "qkv");
+    I->t_qkv_bytes = (size_t)2 * ntok * 3 * D * as;
+    I->t_qkv = dmalloc(I, I->t_qkv_bytes, "qkv");
     I->t_o = dmalloc(I, 2 * ntok * D * as, "attention");
     I->t_h = dmalloc(I, 2 * ntok * MLP_RATIO * D * as, "mlp");
     I->t_out = (float *)dmalloc(I, n16 * (NCLS + 1) * 4, "anchor logits");
@@ -1265,12 +1267,42 @@ __global__ void split3_k(const float *x, long n, int d, __nv_bfloat16 *a3, __nv_
     }
 }
 
+// The same split of the transpose of a float n x d matrix x (row k, column
+// j): row j of b3 is [hi, lo, hi] of column j of x, so that a3 b3^T with
+// a3 = split3_k's [hi, hi, lo] rows of another matrix is that matrix times
+// x. 32 x 32 tiles through shared memory: coalesced reads along j, writes
+// along k.
+__global__ void split3t_k(const float *x, int n, int d, __nv_bfloat16 *b3)
+{
+    __shared__ float t[32][33];
+    const int k0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int k = k0 + r, j = j0 + threadIdx.x;
+        t[r][threadIdx.x] = k < n && j < d ? x[(long)k * d + j] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int j = j0 + r, k = k0 + threadIdx.x;
+        if (j >= d || k >= n)
+            continue;
+        const float v = t[threadIdx.x][r];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+        __nv_bfloat16 *rb = b3 + (long)j * 3 * n;
+        rb[k] = hi;
+        rb[n + k] = lo;
+        rb[2 * n + k] = hi;
+    }
+}
+
 // Gaussian-process posterior of A's 1/16 features given B's and the
 // position basis, into t_x columns 0..511, A's features in 512..1023
 // (roma.c:873-896), the solve on the device in double. In bfloat16 mode the
-// two kernel matrices' products (cosines of normalized features) run on the
-// tensor cores as three-term bfloat16 splits (K = 3 x 512), float32 mode
-// keeps the float32 products.
+// two kernel matrices' products (cosines of normalized features) and the
+// posterior product K_xy X run on the tensor cores as three-term bfloat16
+// splits (K = 3 x 512 and 3 n; the split K_xy is staged in the qkv buffer,
+// free between the encoder and the decoder); float32 mode keeps the float32
+// products.
 void gp(Ctx &c)
 {
     roma_impl *I = c.I;
@@ -1311,7 +1343,20 @@ void gp(Ctx &c)
                      I->gp_work, I->gp_flag);
         launch_ok("gp_cholesky");
     }
-    {
+    if (I->at == DT_BF16 && (size_t)6 * n * n <= I->t_qkv_bytes && n % 8 == 0) {
+        __nv_bfloat16 *a3 = (__nv_bfloat16 *)I->t_qkv, *b3 = I->g_s3[0];
+        {
+            Prof p(c.m->ocl, "gp_kernel");
+            const long e = (long)n * n;
+            split3_k<<<cdiv(e, 256), 256, 0, c.st>>>(I->g_kxy, n, n, a3, nullptr);
+            split3t_k<<<dim3(cdiv(GP_DIM, 32), cdiv(n, 32)), dim3(32, 8), 0, c.st>>>(
+                (const float *)I->g_x, n, GP_DIM, b3);
+            launch_ok("gp_kernel");
+        }
+        gemm_nt(c, "gp_gemm", n, GP_DIM, 3 * n, a3, 3 * n, DT_BF16, b3, nullptr, I->t_x,
+                ROMA_DEC_DIM, DT_F32, ACTF_NONE, false);
+    }
+    else {
         GemmArgs g = gemm_args(n, GP_DIM, n);
         g.A = I->g_kxy;
         g.lda = n;
