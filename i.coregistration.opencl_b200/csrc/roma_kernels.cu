@@ -846,8 +846,17 @@ dwconv5_pair_k(const __nv_bfloat16 *in, long ps, int C, int H, int W, const floa
                const float *bias, __nv_bfloat16 *out, long ops)
 {
     __shared__ __align__(16) uint32_t tile[DWP_TW * DWP_RP];
+    // The block's taps, tap-major with channel pairs innermost (a row's five
+    // taps are five conflict-free 8-byte reads; global loads there stalled
+    // every row on their latency).
+    __shared__ float2 wsm[25][DWP_C / 2];
     const int tid = threadIdx.x, c0 = blockIdx.z * DWP_C;
     const int x0 = blockIdx.x * DWP_T - 2, y0 = blockIdx.y * DWP_T - 2;
+    for (int e = tid; e < 25 * (DWP_C / 2); e += 256) {
+        const int q = e % (DWP_C / 2), tap = e / (DWP_C / 2), c = c0 + 2 * q;
+        wsm[tap][q] = c < C ? make_float2(wt[c * 25 + tap], wt[(c + 1) * 25 + tap])
+                            : make_float2(0.0f, 0.0f);
+    }
     for (int e = tid; e < DWP_TW * DWP_TW * (DWP_C / 8); e += 256) {
         const int j = e % (DWP_C / 8), px = (e / (DWP_C / 8)) % DWP_TW;
         const int py = e / ((DWP_C / 8) * DWP_TW);
@@ -872,7 +881,7 @@ dwconv5_pair_k(const __nv_bfloat16 *in, long ps, int C, int H, int W, const floa
         float2 w[5];
 #pragma unroll
         for (int k = 0; k < 5; k++)
-            w[k] = make_float2(wt[cg * 25 + a * 5 + k], wt[(cg + 1) * 25 + a * 5 + k]);
+            w[k] = wsm[a * 5 + k][pr];
         const uint32_t *row = tile + (oy + a) * DWP_RP + pr;
 #pragma unroll
         for (int x = 0; x < DWP_TW; x++) {
