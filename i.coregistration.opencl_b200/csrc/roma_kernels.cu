@@ -644,6 +644,35 @@ __global__ void disp_emb4_k(const float *flow, int H, int W, float fx, float fy,
     out[(long)i * ops4 + coff4 + g] = o;
 }
 
+// The same for any embedding width and channel offset (RoMa v2's 79 and
+// 23 channels): one thread per cell and 4 channels (the last group
+// shorter), 32-bit indices, the displacement computed once per thread and
+// the channels stored one by one.
+template <typename TO>
+__global__ void disp_emb_g_k(const float *flow, int H, int W, float fx, float fy,
+                             const float *ew, const float *eb, int emb, TO *out, long ops,
+                             int coff, int total)
+{
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= total)
+        return;
+    const int groups = (emb + 3) / 4;
+    const int g = e % groups, i = e / groups, n = H * W;
+    float gx, gy;
+    cell_centre(i, H, W, &gx, &gy);
+    const float dx = fx * (flow[i] - gx), dy = fy * (flow[n + i] - gy);
+    TO *o = out + (long)i * ops + coff;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const int k = 4 * g + c;
+        if (k < emb) {
+            float acc = ew[2 * k] * dx;
+            acc = fmaf(ew[2 * k + 1], dy, acc);
+            stf(o + k, acc + eb[k]);
+        }
+    }
+}
+
 void roma_disp_emb_l(cudaStream_t st, const float *flow, int H, int W, float fx,
                      float fy, const float *emb_w, const float *emb_b, int emb,
                      MapOut out, int coff)
@@ -657,6 +686,18 @@ void roma_disp_emb_l(cudaStream_t st, const float *flow, int H, int W, float fx,
         disp_emb4_k<<<cdiv(total, 256), 256, 0, st>>>(flow, H, W, fx, fy, emb_w, emb_b, emb / 4,
                                                       (uint2 *)out.p, out.ps / 4, coff / 4,
                                                       total);
+        return;
+    }
+    const long groups = (long)H * W * ((emb + 3) / 4);
+    if (out.cs == 1 && groups < (1L << 30) && (long)H * W < (1L << 30)) {
+        if (out.t == DT_BF16)
+            disp_emb_g_k<<<cdiv(groups, 256), 256, 0, st>>>(
+                flow, H, W, fx, fy, emb_w, emb_b, emb, (__nv_bfloat16 *)out.p, out.ps, coff,
+                (int)groups);
+        else
+            disp_emb_g_k<<<cdiv(groups, 256), 256, 0, st>>>(
+                flow, H, W, fx, fy, emb_w, emb_b, emb, (float *)out.p, out.ps, coff,
+                (int)groups);
         return;
     }
     if (out.t == DT_BF16)
@@ -1027,12 +1068,57 @@ __global__ void copy2d_k(const TS *src, long sp, TD *dst, long dp, long rows,
     stf(dst + r * dp + c, ldf(src + r * sp + c));
 }
 
+// The same-type copy in chunks of V elements (V * element size = 16, 8 or
+// 4 bytes) per thread, for pitches, widths and addresses that allow it:
+// one vector load and store each instead of V scalar ones, and the
+// 64-bit index division once per chunk.
+template <typename W>
+__global__ void copy2d_vec_k(const W *src, long sp, W *dst, long dp, long rows, long cols)
+{
+    const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= rows * cols)
+        return;
+    const long r = e / cols, c = e % cols;
+    dst[r * dp + c] = src[r * sp + c];
+}
+
+// Chunk bytes (16, 8 or 4) that divide every pitch, the width and both
+// addresses, in bytes; 0 if none does.
+static int copy_chunk(const void *src, long spb, const void *dst, long dpb, long colsb)
+{
+    for (int b = 16; b >= 4; b /= 2)
+        if (((uintptr_t)src % b) == 0 && ((uintptr_t)dst % b) == 0 && spb % b == 0 &&
+            dpb % b == 0 && colsb % b == 0)
+            return b;
+    return 0;
+}
+
 void copy2d(cudaStream_t st, const void *src, DType ts, long spitch, void *dst,
             DType td, long dpitch, long rows, long cols)
 {
     const long tot = rows * cols;
     if (tot <= 0)
         return;
+    if (ts == td) {
+        const long es = ts == DT_F32 ? 4 : 2;
+        const int b = copy_chunk(src, spitch * es, dst, dpitch * es, cols * es);
+        const long cw = cols * es / (b ? b : 1), sw = spitch * es / (b ? b : 1),
+                   dw = dpitch * es / (b ? b : 1);
+        const unsigned gv = cdiv(rows * cw, 256);
+        if (b == 16) {
+            copy2d_vec_k<<<gv, 256, 0, st>>>((const uint4 *)src, sw, (uint4 *)dst, dw, rows, cw);
+            return;
+        }
+        if (b == 8) {
+            copy2d_vec_k<<<gv, 256, 0, st>>>((const uint2 *)src, sw, (uint2 *)dst, dw, rows, cw);
+            return;
+        }
+        if (b == 4) {
+            copy2d_vec_k<<<gv, 256, 0, st>>>((const uint32_t *)src, sw, (uint32_t *)dst, dw,
+                                             rows, cw);
+            return;
+        }
+    }
     const unsigned g = cdiv(tot, 256);
     if (ts == DT_F32 && td == DT_F32)
         copy2d_k<<<g, 256, 0, st>>>((const float *)src, spitch, (float *)dst,
