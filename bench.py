@@ -192,6 +192,9 @@ def work_model(Hp=H, Wp=W, Cs=COARSE, es=2):
                         ("fc1", 2 * N * D * 4 * D), ("fc2", 2 * N * 4 * D * D),
                         ("attention", 4 * N * N * D)):
             add(fl, name, f * blocks * imgs)
+    # LayerNorm: float32 residual rows in, es-byte rows out (two per block,
+    # DINOv2's final norm; both images' rows in one call).
+    add(by, "layernorm", (24 * 2 + 1) * 2 * ntok * D * (4 + es) + 5 * 2 * n16 * D * (4 + es))
     add(fl, "patch_embed", 2 * 2 * n16 * 588 * D)
     add(fl, "proj16", 2 * 2 * n16 * D * 512)
     add(fl, "to_out", 2 * n16 * D * 4097)
