@@ -31,7 +31,8 @@
 //          staging -> TMA store of the tile (clipped at the map border);
 //   21     patch loader: the 20 x 12-pixel x CK-channel input patch of each
 //          item by TMA (zeros outside the map) into a ring of NH buffers,
-//          a buffer refilled once every producer warp has released it.
+//          a buffer refilled once the producer warps of its last item have
+//          released it.
 // Producers, loader and MMA issuer meet only at mbarriers. Every wait is
 // bounded (global time, about two seconds); a wait that runs out records
 // an error code (coreg_tc_status) and the waiting warp leaves its loop,
@@ -80,8 +81,9 @@ struct DwCfg {
     static constexpr int PXL = CK == 32 ? PX + 1 : PX;
     static constexpr int RPW = PXL * NP;
     static constexpr int PATCH_WORDS = PY * RPW;
-    // Rings: one slot more than the items in flight, where shared memory
-    // allows (C 128 fills it at three).
+    // Rings: with 32 channels one A slot and two patch slots more than the
+    // items in flight; the wider blocks keep three of each (C 128 fills the
+    // shared memory at that).
     static constexpr int NA = C == 32 ? PG + 1 : 3;   // A ring
     static constexpr int NH = C == 32 ? PG + 2 : 3;   // patch ring
     static constexpr int NO = C <= 64 ? 2 : 1;        // output staging buffers
